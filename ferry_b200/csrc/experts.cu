@@ -1,0 +1,490 @@
+// experts.cu -- routed/shared-expert SwiGLU as a grouped bf16 GEMM on the
+// 5th-generation tensor cores (tcgen05.mma, accumulators in TMEM, operands
+// staged by TMA with the 128-byte swizzle).
+//
+// Replaces ferry/csrc/expert_ops.cpp:16-45 (execute_experts: per cached expert
+// x = input[rows]; y = (silu(x Wg^T) * (x Wu^T)) Wd^T; y * w[rows, cols]) and
+// the silu_mul kernel of ferry/csrc/expert_ops.cu:6-25.
+//
+// Data layout.  An expert row of the cache is [gate I x H | up I x H | down
+// H x I] bf16 (ferry/model.py:86-88).  The kernel sees the cache through two
+// 2D tensor maps: W1 = [slots*3I, H] (gate rows of slot s at s*3I, up rows at
+// s*3I + I) and W2 = [slots*3H, I] (down rows of slot s at s*3H + 2H).  The
+// routed tokens of all groups sit back to back in X = [routes, H] (one row per
+// (token, expert) route, grouped by expert); the activations in A = [routes, I].
+//
+// Orientation ("swap AB").  The expert weight tile is the MMA's M = 128 side
+// and the group's routes are the N side (16..128 columns), so a decode group
+// with a handful of tokens costs one pass over its weights: the kernel is
+// HBM-bound at decode and tensor-bound only for groups of hundreds of routes.
+//
+// Phase 1 (GATE_UP): per (group, 128-row tile of I): D_g = Wg_tile X^T and
+// D_u = Wu_tile X^T over K = H; epilogue act = bf16(silu(bf16 D_g) * bf16 D_u)
+// in float32, written to A.  Phase 2 (DOWN): per (group, 128-row tile of H):
+// D = Wd_tile A^T over K = I; epilogue out = bf16(bf16(D) * w_route), written
+// to OUT = [routes, H].  The bf16 rounding points are the reference's.
+//
+// CTA roles (192 threads): warp 0 issues TMA loads, warp 1 allocates TMEM and
+// issues tcgen05.mma from one elected lane, warps 2-5 drain TMEM (warp w reads
+// TMEM lanes 32*(w%4)..+31).  Shared-memory stages are a ring guarded by
+// full/empty mbarriers; TMEM holds two accumulator buffers so the epilogue of
+// one tile overlaps the MMAs of the next.  The grid is persistent (<= #SMs).
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+
+namespace ferryb {
+
+constexpr int kThreads = 192;
+constexpr int kBlockM = 128;   // weight rows per tile (MMA M)
+constexpr int kBlockK = 64;    // bf16 elements per 128-byte swizzle row
+constexpr int kMaxN = 128;     // routes per tile (MMA N)
+constexpr uint32_t kTileBytesA = kBlockM * kBlockK * 2;  // 16 KB
+constexpr uint32_t kTileBytesB = kMaxN * kBlockK * 2;    // 16 KB (max)
+constexpr uint64_t kWaitNs = 2000000000ull;               // 2 s bound on any wait
+
+struct GemmGroup {
+  int32_t slot;   // cache slot holding the expert's weights
+  int32_t start;  // first route row in X / A / OUT
+  int32_t count;  // number of routes
+  int32_t pad;
+};
+
+// Tensor maps of the B operand for box heights 16, 32, 64, 128.
+struct BMaps {
+  CUtensorMap m[4];
+};
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for an mbarrier phase, bounded by time; on timeout raise the CTA's
+// abort flag and the kernel's error word.
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity,
+                                             volatile int* abort_flag, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kWaitNs) {
+        *abort_flag = 1;
+        atomicCAS(err, 0, DEV_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ int box_index(int n) {
+  return n <= 16 ? 0 : n <= 32 ? 1 : n <= 64 ? 2 : 3;
+}
+
+template <int PHASE>
+struct PhaseCfg;
+template <>
+struct PhaseCfg<1> {
+  static constexpr int kA = 2;  // gate and up tiles per stage
+  static constexpr int kStages = 4;
+};
+template <>
+struct PhaseCfg<2> {
+  static constexpr int kA = 1;
+  static constexpr int kStages = 6;
+};
+
+template <int PHASE>
+constexpr uint32_t stage_bytes() {
+  return PhaseCfg<PHASE>::kA * kTileBytesA + kTileBytesB;
+}
+template <int PHASE>
+constexpr uint32_t smem_bytes() {
+  return PhaseCfg<PHASE>::kStages * stage_bytes<PHASE>() + 1024 /*align*/ + 256 /*barriers*/;
+}
+
+struct GemmParams {
+  const GemmGroup* groups;
+  int n_groups;
+  int m_tiles;       // I/128 (phase 1) or H/128 (phase 2)
+  int k_blocks;      // H/64 (phase 1) or I/64 (phase 2)
+  int rows_per_slot; // 3I (W1 view) or 3H (W2 view)
+  int up_offset;     // I: rows from gate to up inside a slot (phase 1)
+  int down_offset;   // 2H: rows from slot start to down (phase 2)
+  int out_cols;      // I (phase 1, act width) or H (phase 2, out width)
+  __nv_bfloat16* out;             // A (phase 1) or OUT (phase 2)
+  const __nv_bfloat16* route_w;   // per-route routing weight (phase 2), may be null (=1)
+  int* err;
+};
+
+template <int PHASE>
+__global__ void __launch_bounds__(kThreads, 1)
+    swiglu_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
+                       const __grid_constant__ BMaps bmaps, const GemmParams p) {
+  using Cfg = PhaseCfg<PHASE>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes<PHASE>());
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;   // [2]
+  uint64_t* tempty = tfull + 2;  // [2]
+  uint64_t* drain = tempty + 2;  // [1] MMA drain on abort
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_items = p.n_groups * p.m_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&wmap);
+    for (int i = 0; i < 4; ++i) tma_prefetch_desc(&bmaps.m[i]);
+  }
+  if (warp == 1) { tmem_alloc(tmem_base_smem, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_smem;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t pending = 0, pend_parity = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const GemmGroup g = p.groups[item / p.m_tiles];
+        const int mt = item % p.m_tiles;
+        const int chunks = (g.count + kMaxN - 1) / kMaxN;
+        for (int c = 0; c < chunks && ok; ++c) {
+          const int n_valid = min(kMaxN, g.count - c * kMaxN);
+          const int bi = box_index(n_valid);
+          const uint32_t b_bytes = (16u << bi) * kBlockK * 2;
+          const int row_b = g.start + c * kMaxN;
+          int row_a;
+          if (PHASE == 1) row_a = g.slot * p.rows_per_slot + mt * kBlockM;
+          else row_a = g.slot * p.rows_per_slot + p.down_offset + mt * kBlockM;
+          for (int kb = 0; kb < p.k_blocks; ++kb) {
+            if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err)) { ok = false; break; }
+            uint8_t* st = smem + stage * stage_bytes<PHASE>();
+            mbar_expect_tx(&full[stage], Cfg::kA * kTileBytesA + b_bytes);
+            tma_load_2d(st, &wmap, &full[stage], kb * kBlockK, row_a);
+            if (PHASE == 1)
+              tma_load_2d(st + kTileBytesA, &wmap, &full[stage], kb * kBlockK, row_a + p.up_offset);
+            tma_load_2d(st + Cfg::kA * kTileBytesA, &bmaps.m[bi], &full[stage], kb * kBlockK, row_b);
+            pending |= 1u << stage;
+            pend_parity = (pend_parity & ~(1u << stage)) | (phase << stage);
+            if (++stage == S) { stage = 0; phase ^= 1; }
+          }
+        }
+      }
+      if (!ok) {
+        // Drain this CTA's TMA loads still in flight before the CTA exits.
+        uint64_t t0 = global_ns();
+        for (int s = 0; s < S; ++s)
+          if (pending & (1u << s))
+            while (!mbar_try_wait(&full[s], (pend_parity >> s) & 1) && global_ns() - t0 < kWaitNs) {}
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const GemmGroup g = p.groups[item / p.m_tiles];
+        const int chunks = (g.count + kMaxN - 1) / kMaxN;
+        for (int c = 0; c < chunks && ok; ++c) {
+          const int n_valid = min(kMaxN, g.count - c * kMaxN);
+          const uint32_t n_mma = 16u << box_index(n_valid);
+          const uint32_t idesc = idesc_bf16_f32(kBlockM, n_mma);
+          if (!wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d0 = tmem_base + acc * 256;        // gate (phase 1) / out (phase 2)
+          const uint32_t d1 = tmem_base + acc * 256 + 128;  // up (phase 1)
+          for (int kb = 0; kb < p.k_blocks; ++kb) {
+            if (!wait_bounded(&full[stage], phase, abort_flag, p.err)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t st = smem_u32(smem + stage * stage_bytes<PHASE>());
+            const uint32_t sb = st + Cfg::kA * kTileBytesA;
+#pragma unroll
+            for (int k = 0; k < kBlockK / 16; ++k) {
+              const uint64_t bdesc = smem_desc_sw128(sb + k * 32);
+              const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+              umma_bf16(d0, smem_desc_sw128(st + k * 32), bdesc, idesc, accum);
+              if (PHASE == 1) umma_bf16(d1, smem_desc_sw128(st + kTileBytesA + k * 32), bdesc, idesc, accum);
+            }
+            umma_commit(&empty[stage]);
+            if (++stage == S) { stage = 0; phase ^= 1; }
+          }
+          if (!ok) break;
+          umma_commit(&tfull[acc]);
+          if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        }
+      }
+      // Make sure no MMA is still writing TMEM before the CTA frees it.
+      umma_commit(drain);
+      uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain, 0) && global_ns() - t0 < kWaitNs) {}
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const GemmGroup g = p.groups[item / p.m_tiles];
+      const int mt = item % p.m_tiles;
+      const int chunks = (g.count + kMaxN - 1) / kMaxN;
+      const int feature = mt * kBlockM + q * 32 + lane;
+      for (int c = 0; c < chunks; ++c) {
+        const int n_valid = min(kMaxN, g.count - c * kMaxN);
+        if (!wait_bounded(&tfull[acc], acc_phase, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+        const uint32_t d0 = tmem_base + lane_addr + acc * 256;
+        for (int c0 = 0; c0 < n_valid; c0 += 16) {
+          float v0[16];
+          tmem_ld16(d0 + c0, v0);
+          if (PHASE == 1) {
+            float v1[16];
+            tmem_ld16(d0 + 128 + c0, v1);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if (c0 + j < n_valid) {
+                const float gt = bf16_round(v0[j]);
+                const float up = bf16_round(v1[j]);
+                const float a = (gt / (1.0f + expf(-gt))) * up;
+                const size_t row = static_cast<size_t>(g.start + c * kMaxN + c0 + j);
+                p.out[row * p.out_cols + feature] = __float2bfloat16_rn(a);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if (c0 + j < n_valid) {
+                const size_t row = static_cast<size_t>(g.start + c * kMaxN + c0 + j);
+                float y = bf16_round(v0[j]);
+                if (p.route_w) y = y * __bfloat162float(p.route_w[row]);
+                p.out[row * p.out_cols + feature] = __float2bfloat16_rn(y);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Gather of the routed rows into X (one row per route, grouped) and of their
+// routing weights: X[p] = input[rows[p]], W[p] = routing_weights[rows[p], cols[p]].
+__global__ void gather_routes_kernel(const __nv_bfloat16* __restrict__ input, int64_t n_input,
+                                     const __nv_bfloat16* __restrict__ weights, int64_t topk,
+                                     const int64_t* __restrict__ rows,
+                                     const int64_t* __restrict__ cols, int64_t total,
+                                     int64_t hidden, __nv_bfloat16* __restrict__ x,
+                                     __nv_bfloat16* __restrict__ w, int* err) {
+  const int64_t vec_per_row = hidden / 8;  // 16-byte vectors
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total * vec_per_row;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pidx = i / vec_per_row, v = i % vec_per_row;
+    const int64_t r = rows[pidx];
+    if (r < 0 || r >= n_input) { atomicCAS(err, 0, DEV_BAD_INPUT); continue; }
+    reinterpret_cast<uint4*>(x + pidx * hidden)[v] =
+        reinterpret_cast<const uint4*>(input + r * hidden)[v];
+    if (v == 0) {
+      const int64_t c = cols[pidx];
+      if (c < 0 || c >= topk) { atomicCAS(err, 0, DEV_BAD_INPUT); continue; }
+      w[pidx] = weights[r * topk + c];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+static int launch_phase(int phase, const CUtensorMap& wmap, const BMaps& bmaps,
+                        const GemmParams& p, int device, cudaStream_t stream) {
+  const int items = p.n_groups * p.m_tiles;
+  if (items == 0) return FERRYB_OK;
+  const int grid = items < num_sms(device) ? items : num_sms(device);
+  if (phase == 1) {
+    const int smem = smem_bytes<1>();
+    FB_CUDA(cudaFuncSetAttribute(swiglu_gemm_kernel<1>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    swiglu_gemm_kernel<1><<<grid, kThreads, smem, stream>>>(wmap, bmaps, p);
+  } else {
+    const int smem = smem_bytes<2>();
+    FB_CUDA(cudaFuncSetAttribute(swiglu_gemm_kernel<2>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    swiglu_gemm_kernel<2><<<grid, kThreads, smem, stream>>>(wmap, bmaps, p);
+  }
+  FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}
+
+static int make_bmaps(BMaps* maps, const void* base, int64_t rows, int64_t cols) {
+  for (int i = 0; i < 4; ++i) {
+    int s = make_map_2d_bf16(&maps->m[i], base, rows > 0 ? rows : 1, cols, cols * 2, 16u << i,
+                             kBlockK);
+    if (s) return s;
+  }
+  return FERRYB_OK;
+}
+
+// Shared by the public entry points: run both phases over `groups` (device),
+// given X (routes already gathered), route weights, and scratch A.
+int swiglu_grouped(const void* cache, int64_t cache_slots, const GemmGroup* groups,
+                   int n_groups, int64_t total_routes, const __nv_bfloat16* x,
+                   const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
+                   int64_t hidden, int64_t inter, int* err, cudaStream_t stream) {
+  FB_CHECK_ARG(hidden % kBlockM == 0 && inter % kBlockM == 0,
+               "hidden (%lld) and intermediate (%lld) must be multiples of 128",
+               (long long)hidden, (long long)inter);
+  if (n_groups == 0 || total_routes == 0) return FERRYB_OK;
+  int device = 0;
+  FB_CUDA(cudaGetDevice(&device));
+  CUtensorMap w1, w2;
+  BMaps bx, ba;
+  int s;
+  if ((s = make_map_2d_bf16(&w1, cache, cache_slots * 3 * inter, hidden, hidden * 2, kBlockM,
+                            kBlockK)))
+    return s;
+  if ((s = make_map_2d_bf16(&w2, cache, cache_slots * 3 * hidden, inter, inter * 2, kBlockM,
+                            kBlockK)))
+    return s;
+  if ((s = make_bmaps(&bx, x, total_routes, hidden))) return s;
+  if ((s = make_bmaps(&ba, act, total_routes, inter))) return s;
+
+  GemmParams p1{};
+  p1.groups = groups;
+  p1.n_groups = n_groups;
+  p1.m_tiles = static_cast<int>(inter / kBlockM);
+  p1.k_blocks = static_cast<int>(hidden / kBlockK);
+  p1.rows_per_slot = static_cast<int>(3 * inter);
+  p1.up_offset = static_cast<int>(inter);
+  p1.out_cols = static_cast<int>(inter);
+  p1.out = act;
+  p1.err = err;
+  if ((s = launch_phase(1, w1, bx, p1, device, stream))) return s;
+
+  GemmParams p2{};
+  p2.groups = groups;
+  p2.n_groups = n_groups;
+  p2.m_tiles = static_cast<int>(hidden / kBlockM);
+  p2.k_blocks = static_cast<int>(inter / kBlockK);
+  p2.rows_per_slot = static_cast<int>(3 * hidden);
+  p2.down_offset = static_cast<int>(2 * hidden);
+  p2.out_cols = static_cast<int>(hidden);
+  p2.out = out;
+  p2.route_w = route_w;
+  p2.err = err;
+  return launch_phase(2, w2, ba, p2, device, stream);
+}
+
+static int64_t align256(int64_t b) { return (b + 255) & ~int64_t(255); }
+
+// Workspace carve-up of ferryb_execute_experts.
+struct ExecWs {
+  int64_t x, act, w, groups, err, total;
+};
+static ExecWs exec_ws(int64_t total, int64_t n_groups, int64_t hidden, int64_t inter) {
+  ExecWs w{};
+  w.x = 0;
+  w.act = w.x + align256(total * hidden * 2);
+  w.w = w.act + align256(total * inter * 2);
+  w.groups = w.w + align256(total * 2);
+  w.err = w.groups + align256(n_groups * (int64_t)sizeof(GemmGroup));
+  w.total = w.err + 256;
+  return w;
+}
+
+}  // namespace ferryb
+
+using namespace ferryb;
+
+extern "C" int64_t ferryb_execute_experts_workspace(int64_t total_routes, int64_t n_groups,
+                                                    int64_t hidden, int64_t intermediate) {
+  return exec_ws(total_routes, n_groups, hidden, intermediate).total;
+}
+
+extern "C" int ferryb_execute_experts(const void* cache, int64_t cache_slots, const void* input,
+                                      int64_t n_input, const void* routing_weights, int64_t topk,
+                                      const int64_t* slots, const int64_t* group_sizes,
+                                      int64_t n_groups, const int64_t* rows, const int64_t* cols,
+                                      int64_t hidden, int64_t intermediate, void* out,
+                                      void* workspace, int64_t workspace_bytes,
+                                      cudaStream_t stream) {
+  FB_CHECK_ARG(n_groups >= 0 && hidden > 0 && intermediate > 0, "bad sizes");
+  FB_CHECK_ARG(n_groups == 0 || (slots && group_sizes), "slots/group_sizes required");
+  int64_t total = 0;
+  std::vector<GemmGroup> host_groups(static_cast<size_t>(n_groups));
+  for (int64_t i = 0; i < n_groups; ++i) {
+    FB_CHECK_ARG(slots[i] >= 0 && slots[i] < cache_slots, "slot %lld out of range [0, %lld)",
+                 (long long)slots[i], (long long)cache_slots);
+    FB_CHECK_ARG(group_sizes[i] >= 0, "negative group size");
+    host_groups[i] = GemmGroup{static_cast<int32_t>(slots[i]), static_cast<int32_t>(total),
+                               static_cast<int32_t>(group_sizes[i]), 0};
+    total += group_sizes[i];
+  }
+  if (total == 0) return FERRYB_OK;
+  FB_CHECK_ARG(cache && input && routing_weights && rows && cols && out, "null pointer");
+  const ExecWs ws = exec_ws(total, n_groups, hidden, intermediate);
+  FB_CHECK_ARG(workspace && workspace_bytes >= ws.total, "workspace too small (%lld < %lld)",
+               (long long)workspace_bytes, (long long)ws.total);
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  auto* x = reinterpret_cast<__nv_bfloat16*>(base + ws.x);
+  auto* act = reinterpret_cast<__nv_bfloat16*>(base + ws.act);
+  auto* w = reinterpret_cast<__nv_bfloat16*>(base + ws.w);
+  auto* groups = reinterpret_cast<GemmGroup*>(base + ws.groups);
+  int* err = reinterpret_cast<int*>(base + ws.err);
+  FB_CUDA(cudaMemsetAsync(err, 0, sizeof(int), stream));
+  FB_CUDA(cudaMemcpyAsync(groups, host_groups.data(), n_groups * sizeof(GemmGroup),
+                          cudaMemcpyHostToDevice, stream));
+  const int64_t work = total * (hidden / 8);
+  int blocks = static_cast<int>((work + 255) / 256);
+  if (blocks > 4096) blocks = 4096;
+  gather_routes_kernel<<<blocks, 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(input), n_input,
+      static_cast<const __nv_bfloat16*>(routing_weights), topk, rows, cols, total, hidden, x, w,
+      err);
+  FB_LAUNCH_CHECK();
+  int s = swiglu_grouped(cache, cache_slots, groups, static_cast<int>(n_groups), total, x, w, act,
+                         static_cast<__nv_bfloat16*>(out), hidden, intermediate, err, stream);
+  if (s) return s;
+  // Synchronous status check of the device error word (compat API semantics:
+  // errors surface at the call, like the reference's TORCH_CHECKs).
+  int h_err = 0;
+  FB_CUDA(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  FB_CUDA(cudaStreamSynchronize(stream));
+  if (h_err) return fail(FERRYB_EDEVICE, "execute_experts: device error %d", h_err);
+  return FERRYB_OK;
+}
