@@ -15,6 +15,35 @@ LIB_PATH = Path(__file__).resolve().parent / 'libferryb.so'
 _i64, _i32, _vp, _u64 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64
 _dbl, _f32 = ctypes.c_double, ctypes.c_float
 
+_i32c, _u8p = ctypes.c_int32, ctypes.c_void_p
+
+
+class Planner(ctypes.Structure):
+    """ferryb_planner (include/ferryb.h)."""
+    _fields_ = [('world', _i32c), ('experts', _i32c), ('layers', _i32c), ('topk', _i32c),
+                ('window', _i32c), ('policy', _i32c), ('balance_tol_bps', _i64), ('salt', _i64),
+                ('maxcap', _i32c), ('total_slots', _i32c), ('n_domains', _i32c),
+                ('lut_rows', _i32c)] + [(n, _vp) for n in (
+                    'capacities', 'slot_rank', 'slot_index', 'lut', 'masks', 'seconds', 'slots',
+                    'owner', 'last', 'scores', 'ring', 'ring_p', 'hist_count', 'hist_head')]
+
+
+class LayoutSummary(ctypes.Structure):
+    """ferryb_layout_summary (include/ferryb.h)."""
+    _fields_ = [(n, _i32c) for n in ('n_fetch_mine', 'n_hit', 'n_groups', 'n_recv', 'n_send',
+                                      'n_routes', 'err', 'reserved')] + [
+        ('fetch_keys', _i32c * 256), ('fetch_slots', _i32c * 256)]
+
+
+class LayoutArgs(ctypes.Structure):
+    """ferryb_layout_args (include/ferryb.h)."""
+    _fields_ = [('ids', _vp), ('dest', _vp), ('world', _i32c), ('tokens_per_rank', _i32c),
+                ('topk', _i32c), ('experts', _i32c), ('rank', _i32c)] + [(n, _vp) for n in (
+                    'fetches', 'n_fetches', 'layer_slot', 'send_idx', 'send_ids', 'send_counts',
+                    'recv_counts', 'starts', 'rows', 'cols', 'n_send', 'n_recv', 'recv_token',
+                    'csr_pos', 'peer_row', 'groups', 'summary', 'err')]
+
+
 # name -> (restype, argtypes); every symbol declared in include/ferryb.h.
 SIGNATURES = {
     'ferryb_last_error': (ctypes.c_char_p, []),
@@ -23,6 +52,16 @@ SIGNATURES = {
     'ferryb_execute_experts_workspace': (_i64, [_i64, _i64, _i64, _i64]),
     'ferryb_execute_experts': (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp,
                                       _i64, _i64, _vp, _vp, _i64, _vp]),
+    'ferryb_plan_layer': (_i32, [ctypes.POINTER(Planner), _i64, _i32c, _vp, _i32c, _i32c, _vp, _vp,
+                                 _vp, _i32c, _vp, _vp, _vp, _vp, _vp, _vp]),
+    'ferryb_greedy_quota_rows': (_i32, [_i32c, _vp, _vp, _i32c, _vp, _i32c, _i32c, _vp, _vp, _vp]),
+    'ferryb_demand': (_i32, [_vp, _vp, _i32c, _i32c, _i32c, _i32c, _vp, _vp, _vp]),
+    'ferryb_admission_capacity': (_i32, [_vp, _i32c, _vp, _i32c, _i32c, _vp, _i32c, _vp, _vp]),
+    'ferryb_load_balanced_assignment': (_i32, [_vp, _i32c, _i32c, _vp, _i32c, _vp, _i32c, _vp,
+                                               _i64, _vp, _vp]),
+    'ferryb_choose_slot': (_i32, [_i32c, _i32c, _vp, _vp, _i32c, _vp, _vp, _vp, _i32c, _vp, _vp]),
+    'ferryb_build_layout': (_i32, [ctypes.POINTER(LayoutArgs), _vp]),
+    'ferryb_layer_slots': (_i32, [_vp, _i32c, _i32c, _i32c, _vp, _vp]),
 }
 
 _lib = None
@@ -56,6 +95,27 @@ def call(name, *args):
 def ptr(t):
     """Device/host address of a tensor (None -> NULL)."""
     return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def addr(t):
+    """Integer address for ctypes structure fields (None -> 0)."""
+    return 0 if t is None else t.data_ptr()
+
+
+DEVICE_ERRORS = {1: 'a bounded device wait timed out', 2: 'missing experts exceed the total admission capacity',
+                 3: 'no cache slot available for an expert scheduled on this rank',
+                 4: 'an expert id or index is out of range', 5: 'a layout buffer is too small'}
+
+
+def check_device_error(err_tensor, what):
+    """Raise like the reference would (AssertionError for its asserts)."""
+    code = int(err_tensor.item())
+    if code == 2:
+        raise AssertionError('missing experts exceed the total admission capacity')
+    if code == 3:
+        raise AssertionError(f'{what}: ' + DEVICE_ERRORS[3])
+    if code:
+        raise FerrybError(f'{what}: ' + DEVICE_ERRORS.get(code, f'device error {code}'))
 
 
 def stream_ptr(device=None):

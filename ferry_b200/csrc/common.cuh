@@ -46,6 +46,15 @@ enum DeviceError : int {
   DEV_LAYOUT_OVERFLOW = 5,  // a layout buffer was too small
 };
 
+// One expert's work in the grouped GEMM: its routes are rows
+// [start, start + count) of the route-ordered operands.
+struct GemmGroup {
+  int32_t slot;    // cache slot holding the expert's weights
+  int32_t start;   // first route row
+  int32_t count;   // number of routes
+  int32_t expert;  // expert id (informational)
+};
+
 // ---------------------------------------------------------------------------
 // Driver entry points fetched through the runtime (the library must load on a
 // machine without the CUDA driver, so it does not link libcuda).

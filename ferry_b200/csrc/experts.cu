@@ -44,13 +44,6 @@ constexpr uint32_t kTileBytesA = kBlockM * kBlockK * 2;  // 16 KB
 constexpr uint32_t kTileBytesB = kMaxN * kBlockK * 2;    // 16 KB (max)
 constexpr uint64_t kWaitNs = 2000000000ull;               // 2 s bound on any wait
 
-struct GemmGroup {
-  int32_t slot;   // cache slot holding the expert's weights
-  int32_t start;  // first route row in X / A / OUT
-  int32_t count;  // number of routes
-  int32_t pad;
-};
-
 // Tensor maps of the B operand for box heights 16, 32, 64, 128.
 struct BMaps {
   CUtensorMap m[4];
@@ -452,7 +445,7 @@ extern "C" int ferryb_execute_experts(const void* cache, int64_t cache_slots, co
                  (long long)slots[i], (long long)cache_slots);
     FB_CHECK_ARG(group_sizes[i] >= 0, "negative group size");
     host_groups[i] = GemmGroup{static_cast<int32_t>(slots[i]), static_cast<int32_t>(total),
-                               static_cast<int32_t>(group_sizes[i]), 0};
+                               static_cast<int32_t>(group_sizes[i]), static_cast<int32_t>(i)};
     total += group_sizes[i];
   }
   if (total == 0) return FERRYB_OK;

@@ -1,0 +1,306 @@
+// layout.cu -- the expert-parallel layout of one MoE layer for one rank,
+// computed on the GPU from the planner's destinations (no host round trip).
+//
+// Replaces ferry/layout.py:12-75 (build_layout) and :78-94 (device_layout,
+// whose blocking H2D upload disappears) plus ferry/policy.py:197-205
+// (layer_slots).  Orders are the reference's:
+//   send packets by (peer, local token), ids ascending inside a packet;
+//   receive packets by (source peer, token) = global token order;
+//   per-expert CSR of (row, col) with rows ascending inside an expert.
+// The CSR position of a route is a stable counting sort by expert; inside a
+// chunk of 1024 tokens it is found with per-expert token bitmasks and popc.
+//
+// Extra outputs drive the fused dispatch / GEMM / combine:
+//   recv_token[row]  global token of receive row `row`
+//   csr_pos[row, j]  route position of column j of receive row `row`
+//   peer_row[t, p]   receive row of local token t at peer p (-1: no packet)
+//   groups           GEMM groups: experts cached before this layer (ascending),
+//                    then the experts this rank fetched (in fetch order)
+//   summary          counts and this rank's fetch list, copied to the host.
+#include "common.cuh"
+#include "layout.cuh"
+
+namespace ferryb {
+
+constexpr int kLayThreads = 1024;
+constexpr int kChunk = 1024;  // tokens per pass
+
+struct LaySmem {
+  uint32_t mask[kMaxExpertsL][kChunk / 32];  // expert -> token bitmask of the chunk
+  int expert_count[kMaxExpertsL];            // running per-expert route count
+  int starts[kMaxExpertsL + 1];
+  int warp_sum[32];
+  int run;                                   // running scan carry
+  int fetched_rank[kMaxExpertsL];            // fetch order of expert on this rank, or -1
+  int n_groups, n_hit;
+};
+
+// Exclusive block scan of one int per thread (1024 threads); returns the
+// exclusive prefix and writes the total to *total.
+__device__ int block_scan(int v, int* warp_sum, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_sum[lane];
+    int wx = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wx, o);
+      if (lane >= o) wx += y;
+    }
+    warp_sum[lane] = wx - w;  // exclusive per warp
+    if (lane == 31) *total = wx;
+  }
+  __syncthreads();
+  const int res = warp_sum[warp] + x - v;
+  __syncthreads();
+  return res;
+}
+
+// Sorted ids of token g's routes that go to `peer` (ascending, insertion sort
+// as in ferry/layout.py:27-33).  Returns the count.
+__device__ __forceinline__ int packet_ids(const uint8_t* ids, const int32_t* dest, int g, int K,
+                                          int peer, int* out) {
+  int size = 0;
+  for (int j = 0; j < K; ++j) {
+    if (dest[g * K + j] == peer) {
+      const int e = ids[g * K + j];
+      int pos = size;
+      while (pos > 0 && out[pos - 1] > e) { out[pos] = out[pos - 1]; --pos; }
+      out[pos] = e;
+      ++size;
+    }
+  }
+  return size;
+}
+
+__global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs a) {
+  __shared__ LaySmem sm;
+  __shared__ int total_sh;
+  const int tid = threadIdx.x;
+  const int R = a.world, T = a.tokens_per_rank, K = a.topk, E = a.experts, rank = a.rank;
+  const int n_tok = R * T;
+  int ids_buf[16];
+
+  // ---- fetched experts of this rank, in fetch order -----------------------
+  for (int e = tid; e < E; e += blockDim.x) { sm.fetched_rank[e] = -1; sm.expert_count[e] = 0; }
+  __syncthreads();
+  if (tid == 0) {
+    int j = 0;
+    const int nf = a.n_fetches ? *a.n_fetches : 0;
+    for (int i = 0; i < nf; ++i) {
+      if (a.fetches[i * 3 + 0] != rank) continue;
+      const int key = a.fetches[i * 3 + 1];
+      sm.fetched_rank[key % E] = j;
+      if (a.summary) {
+        a.summary->fetch_keys[j] = key;
+        a.summary->fetch_slots[j] = a.fetches[i * 3 + 2];
+      }
+      ++j;
+    }
+    if (a.summary) a.summary->n_fetch_mine = j;
+    sm.run = 0;
+  }
+  __syncthreads();
+
+  // ---- send side: packets by (peer, token) --------------------------------
+  int sent = 0;
+  for (int peer = 0; peer < R; ++peer) {
+    int peer_sent = 0;
+    for (int t0 = 0; t0 < T; t0 += kChunk) {
+      const int t = t0 + tid;
+      const int g = rank * T + t;
+      int size = 0;
+      if (t < T) size = packet_ids(a.ids, a.dest, g, K, peer, ids_buf);
+      const int has = size > 0;
+      const int pos = sent + block_scan(has, sm.warp_sum, &total_sh);
+      if (has) {
+        a.send_idx[pos] = t;
+        for (int j = 0; j < K; ++j) a.send_ids[(size_t)pos * K + j] = j < size ? ids_buf[j] : -1;
+      }
+      sent += total_sh;
+      peer_sent += total_sh;
+      __syncthreads();
+    }
+    if (tid == 0) a.send_counts[peer] = peer_sent;
+  }
+  if (tid == 0) *a.n_send = sent;
+
+  // ---- receive rows of every peer (peer_row) -----------------------------
+  // Receive row of global token g at peer p = #{g' < g : g' sends to p}.
+  if (a.peer_row) {
+    for (int p = 0; p < R; ++p) {
+      int carry = 0;
+      for (int g0 = 0; g0 < n_tok; g0 += kChunk) {
+        const int g = g0 + tid;
+        int has = 0;
+        if (g < n_tok)
+          for (int j = 0; j < K; ++j) has |= a.dest[g * K + j] == p;
+        const int row = carry + block_scan(has, sm.warp_sum, &total_sh);
+        if (g < n_tok && g / T == rank) a.peer_row[(g % T) * R + p] = has ? row : -1;
+        carry += total_sh;
+        __syncthreads();
+      }
+    }
+  }
+
+  // ---- receive side pass 1: receive rows, per-expert counts --------------
+  int received = 0;
+  for (int g0 = 0; g0 < n_tok; g0 += kChunk) {
+    const int g = g0 + tid;
+    int size = 0;
+    if (g < n_tok) size = packet_ids(a.ids, a.dest, g, K, rank, ids_buf);
+    const int has = size > 0;
+    const int row = received + block_scan(has, sm.warp_sum, &total_sh);
+    if (has) {
+      if (a.recv_token) a.recv_token[row] = g;
+      for (int j = 0; j < size; ++j) atomicAdd(&sm.expert_count[ids_buf[j]], 1);
+    }
+    received += total_sh;
+    __syncthreads();
+  }
+  if (tid < R) {
+    int cnt = 0;
+    for (int t = 0; t < T; ++t) {
+      const int g = tid * T + t;
+      int has = 0;
+      for (int j = 0; j < K; ++j) has |= a.dest[g * K + j] == rank;
+      cnt += has;
+    }
+    a.recv_counts[tid] = cnt;
+  }
+  __syncthreads();
+  // starts = exclusive scan of expert counts (E <= 256 < 1024 threads)
+  {
+    const int v = tid < E ? sm.expert_count[tid] : 0;
+    const int ex = block_scan(v, sm.warp_sum, &total_sh);
+    if (tid < E) sm.starts[tid] = ex;
+    if (tid == 0) sm.starts[E] = total_sh;
+  }
+  __syncthreads();
+  for (int e = tid; e <= E; e += blockDim.x) a.starts[e] = sm.starts[e];
+  for (int e = tid; e < E; e += blockDim.x) sm.expert_count[e] = 0;  // becomes the running cursor
+  __syncthreads();
+
+  // ---- receive side pass 2: CSR positions ---------------------------------
+  int row_base = 0;
+  for (int g0 = 0; g0 < n_tok; g0 += kChunk) {
+    for (int i = tid; i < E * (kChunk / 32); i += blockDim.x) (&sm.mask[0][0])[i] = 0;
+    __syncthreads();
+    const int g = g0 + tid;
+    int size = 0;
+    if (g < n_tok) size = packet_ids(a.ids, a.dest, g, K, rank, ids_buf);
+    for (int j = 0; j < size; ++j) atomicOr(&sm.mask[ids_buf[j]][tid >> 5], 1u << (tid & 31));
+    const int has = size > 0;
+    const int row = row_base + block_scan(has, sm.warp_sum, &total_sh);
+    __syncthreads();
+    if (has) {
+      for (int j = 0; j < K; ++j) {
+        int pos = -1;
+        if (j < size) {
+          const int e = ids_buf[j];
+          int before = __popc(sm.mask[e][tid >> 5] & ((1u << (tid & 31)) - 1u));
+          for (int w = 0; w < (tid >> 5); ++w) before += __popc(sm.mask[e][w]);
+          pos = sm.starts[e] + sm.expert_count[e] + before;
+          a.rows[pos] = row;
+          a.cols[pos] = j;
+        }
+        if (a.csr_pos) a.csr_pos[(size_t)row * K + j] = pos;
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += blockDim.x) {
+      int tot = 0;
+      for (int w = 0; w < kChunk / 32; ++w) tot += __popc(sm.mask[e][w]);
+      sm.expert_count[e] += tot;
+    }
+    row_base += total_sh;
+    __syncthreads();
+  }
+  if (tid == 0) *a.n_recv = received;
+
+  // ---- GEMM groups: cached experts (ascending), then fetched (fetch order) --
+  if (tid == 0 && a.groups && a.summary) {
+    GemmGroup* groups = reinterpret_cast<GemmGroup*>(a.groups);
+    int ng = 0;
+    for (int e = 0; e < E; ++e) {
+      const int cnt = sm.starts[e + 1] - sm.starts[e];
+      if (cnt > 0 && sm.fetched_rank[e] < 0) {
+        const int slot = a.layer_slot ? a.layer_slot[e] : -1;
+        groups[ng++] = GemmGroup{slot, sm.starts[e], cnt, e};
+      }
+    }
+    const int n_hit = ng;
+    const int nf = a.summary->n_fetch_mine;
+    for (int j = 0; j < nf; ++j) {
+      const int e = a.summary->fetch_keys[j] % E;
+      const int cnt = sm.starts[e + 1] - sm.starts[e];
+      groups[ng++] = GemmGroup{a.summary->fetch_slots[j], sm.starts[e], cnt, e};
+    }
+    a.summary->n_groups = ng;
+    a.summary->n_hit = n_hit;
+    a.summary->n_recv = received;
+    a.summary->n_send = sent;
+    a.summary->n_routes = sm.starts[E];
+    for (int e = 0; e < E; ++e) {
+      const int cnt = sm.starts[e + 1] - sm.starts[e];
+      if (cnt > 0 && (a.layer_slot == nullptr || a.layer_slot[e] < 0) && sm.fetched_rank[e] < 0)
+        atomicCAS(a.err, 0, DEV_NO_SLOT);  // scheduled here but not cached (ferry/layout.py:91)
+    }
+    a.summary->err = *a.err;
+  }
+}
+
+// layer_slots (ferry/policy.py:197-205) for one rank's slots row.
+__global__ void layer_slots_kernel(const int32_t* slots_row, int capacity, int layer, int experts,
+                                   int32_t* lookup) {
+  for (int e = threadIdx.x; e < experts; e += blockDim.x) lookup[e] = -1;
+  __syncthreads();
+  for (int i = threadIdx.x; i < capacity; i += blockDim.x) {
+    const int key = slots_row[i];
+    if (key >= 0 && key / experts == layer) lookup[key % experts] = i;
+  }
+}
+
+int layout_launch(const LayoutArgs& a, cudaStream_t stream) {
+  FB_CHECK_ARG(a.experts <= kMaxExpertsL && a.topk <= 16 && a.world >= 1,
+               "layout: experts <= %d and topk <= 16 required", kMaxExpertsL);
+  layout_kernel<<<1, kLayThreads, 0, stream>>>(a);
+  FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}
+
+int layer_slots_launch(const int32_t* slots_row, int capacity, int layer, int experts,
+                       int32_t* lookup, cudaStream_t stream) {
+  layer_slots_kernel<<<1, 1024, 0, stream>>>(slots_row, capacity, layer, experts, lookup);
+  FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}
+
+}  // namespace ferryb
+
+using namespace ferryb;
+
+extern "C" int ferryb_build_layout(const ferryb_layout_args* args, cudaStream_t stream) {
+  FB_CHECK_ARG(args && args->ids && args->dest && args->err, "layout: null arguments");
+  FB_CHECK_ARG(args->world >= 1 && args->world <= kMaxWorldL && args->tokens_per_rank >= 0 &&
+                   args->rank >= 0 && args->rank < args->world,
+               "layout: bad world/rank");
+  FB_CHECK_ARG(args->send_idx && args->send_ids && args->send_counts && args->recv_counts &&
+                   args->starts && args->rows && args->cols && args->n_send && args->n_recv,
+               "layout: build_layout outputs are required");
+  return layout_launch(*args, stream);
+}
+
+extern "C" int ferryb_layer_slots(const int32_t* slots_row, int32_t capacity, int32_t layer,
+                                  int32_t experts, int32_t* lookup, cudaStream_t stream) {
+  FB_CHECK_ARG(slots_row && lookup && capacity >= 0 && experts > 0, "layer_slots: bad arguments");
+  return layer_slots_launch(slots_row, capacity, layer, experts, lookup, stream);
+}

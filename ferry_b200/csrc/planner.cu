@@ -1,0 +1,783 @@
+// planner.cu -- kernel 2: the per-layer placement planner as one CTA on the
+// GPU, bit-exact with the reference's decisions.
+//
+// Replaces, per MoE layer invocation (ferry/runtime.py:281-284):
+//   GateHistory.update / scores        ferry/metadata.py:24-38
+//   _demand                            ferry/policy.py:25-33
+//   _admission_capacity                ferry/policy.py:36-46
+//   quota LUT lookup + greedy_quota    ferry/policy.py:155-158, ferry/quota.py:25-67
+//   load_balanced_assignment           ferry/policy.py:49-106
+//   RANDOM branch (MT19937 randint)    ferry/policy.py:160-170
+//   _choose_slot + commit loop         ferry/policy.py:109-127, :171-193
+//
+// Exactness notes.
+//  * greedy_quota compares float64 makespans with 1e-12 relative tie rules;
+//    products and sums use __dmul_rn/__dadd_rn (no FMA contraction) and the
+//    per-rank domain sum runs g = 0..G-1 in order, as the reference does.
+//  * The eviction of _choose_slot, applied once per miss in miss order, takes
+//    on each rank first the empty slots in index order, then the eligible
+//    slots (not holding an expert active in this layer) by ascending
+//    (score, last use, key); scores and last uses do not change during the
+//    commit loop and an installed slot becomes ineligible.  The planner
+//    therefore sorts all slots once by (rank, class, score, last, key) and
+//    hands the j-th victim of rank r to the j-th miss assigned to r.
+//  * Step 3 picks, among ranks with quota left inside the tolerance window,
+//    the lexicographic maximum of (d_{r,e}, -P_r, -N_r) with the lowest rank
+//    winning ties -- the same rank the reference's sequential scan keeps.
+//  * Gate scores are float32(float64 count / max(1, n)) (frequency) or the
+//    float64 sum of the ring slots 0..W-1 in order (probability).
+#include <math_constants.h>
+
+#include <cstring>
+
+#include "common.cuh"
+#include "planner.cuh"
+
+namespace ferryb {
+
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanWarps = kPlanThreads / 32;
+
+struct SlotRec {
+  uint64_t k0;  // rank << 56 | class << 48 | ... (see make_rec)
+  uint64_t k1;
+  uint32_t slot;  // index into slots[] (rank * maxcap + i)
+  uint32_t pad;
+};
+
+__device__ __forceinline__ bool rec_less(const SlotRec& a, const SlotRec& b) {
+  return a.k0 < b.k0 || (a.k0 == b.k0 && a.k1 < b.k1);
+}
+
+// MT19937 as seeded by numba's np.random.seed (init_genrand) and drawn by
+// np.random.randint(0, n) (masked rejection on the low bits; n == 1 draws
+// nothing).  Published algorithm: Matsumoto & Nishimura (1998).
+struct MT {
+  uint32_t mt[624];
+  int index;
+  __device__ void seed(uint32_t s) {
+    mt[0] = s;
+    for (int i = 1; i < 624; ++i) mt[i] = 1812433253u * (mt[i - 1] ^ (mt[i - 1] >> 30)) + (uint32_t)i;
+    index = 624;
+  }
+  __device__ uint32_t next() {
+    if (index >= 624) {
+      for (int i = 0; i < 624; ++i) {
+        uint32_t y = (mt[i] & 0x80000000u) | (mt[(i + 1) % 624] & 0x7fffffffu);
+        mt[i] = mt[(i + 397) % 624] ^ (y >> 1) ^ ((y & 1u) ? 0x9908b0dfu : 0u);
+      }
+      index = 0;
+    }
+    uint32_t y = mt[index++];
+    y ^= y >> 11;
+    y ^= (y << 7) & 0x9d2c5680u;
+    y ^= (y << 15) & 0xefc60000u;
+    y ^= y >> 18;
+    return y;
+  }
+  __device__ int randint(int n) {
+    if (n == 1) return 0;
+    int bits = 32 - __clz(n - 1);
+    uint32_t mask = bits >= 32 ? 0xffffffffu : ((1u << bits) - 1u);
+    for (;;) {
+      uint32_t r = next() & mask;
+      if (r < (uint32_t)n) return (int)r;
+    }
+  }
+};
+
+struct PlanSmem {
+  int demand_total[kMaxExperts];
+  int active[kMaxExperts];
+  int misses[kMaxExperts];
+  int64_t totals[kMaxExperts];
+  int order[kMaxExperts];
+  int assignment[kMaxExperts];
+  int victim_pos[kMaxExperts];
+  int m;
+  int capacity[kMaxWorld];
+  int64_t quota[kMaxWorld];
+  int64_t loads[kMaxWorld];
+  int n_assigned[kMaxWorld];
+  int seg_start[kMaxWorld + 1];
+  float gate[kMaxExperts];
+  int status;
+  MT rng;
+};
+
+__device__ __forceinline__ void set_err(int* err, int code) { atomicCAS(err, 0, code); }
+
+// ---------------------------------------------------------------------------
+// GateHistory.update + scores for `layer` (ferry/metadata.py:24-38).
+// Frequency rows come from the gathered ids: the last `tail` tokens of every
+// rank, rank-major (ferry/metadata.py:57, :80-82).  Probability rows come in
+// prob_rows [n_rows, E] (float32).
+__device__ void history_step(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
+                             float* gate_out) {
+  const int W = c.window, E = c.experts, K = c.topk;
+  const int L = in.layer;
+  const int T = in.tokens_per_rank;
+  const int tail = min(T, (W + c.world - 1) / c.world);
+  const int n_rows = in.prob_rows ? in.n_prob_rows : c.world * tail;
+  int* count = s.hist_count + L;
+  int* head = s.hist_head + L;
+  uint8_t* ring = s.ring + (size_t)L * W * K;
+  float* ring_p = s.ring_p ? s.ring_p + (size_t)L * W * E : nullptr;
+  // The ring positions written by this update: replace (n >= W) or append.
+  const int h0 = *head;
+  __syncthreads();
+  if (n_rows >= W) {
+    // rows[-W:] -> slots 0..W-1
+    for (int i = threadIdx.x; i < W * (ring_p ? E : K); i += blockDim.x) {
+      const int slot = ring_p ? i / E : i / K;
+      const int row = n_rows - W + slot;
+      if (ring_p) {
+        ring_p[i] = in.prob_rows[(size_t)row * E + i % E];
+      } else {
+        const int r = row / tail, t = T - tail + row % tail;
+        ring[i] = in.ids[((size_t)r * T + t) * K + i % K];
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < n_rows * (ring_p ? E : K); i += blockDim.x) {
+      const int row = ring_p ? i / E : i / K;
+      const int slot = (h0 + row) % W;
+      if (ring_p) {
+        ring_p[(size_t)slot * E + i % E] = in.prob_rows[(size_t)row * E + i % E];
+      } else {
+        const int r = row / tail, t = T - tail + row % tail;
+        ring[(size_t)slot * K + i % K] = in.ids[((size_t)r * T + t) * K + i % K];
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (n_rows >= W) {
+      *count = W;
+      *head = 0;
+    } else {
+      *head = (h0 + n_rows) % W;
+      *count = min(W, *count + n_rows);
+    }
+  }
+  __syncthreads();
+  __threadfence_block();
+  const int n = max(1, *count);
+  if (ring_p) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      double acc = 0.0;
+      for (int slot = 0; slot < *count; ++slot) acc = __dadd_rn(acc, (double)ring_p[(size_t)slot * E + e]);
+      gate_out[e] = __double2float_rn(__ddiv_rn(acc, (double)n));
+    }
+  } else {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int cnt = 0;
+      for (int slot = 0; slot < *count; ++slot) {
+        bool hit = false;
+        for (int k = 0; k < K; ++k) hit |= ring[(size_t)slot * K + k] == (uint8_t)e;
+        cnt += hit;
+      }
+      gate_out[e] = __double2float_rn(__ddiv_rn((double)cnt, (double)n));
+    }
+  }
+  __syncthreads();
+}
+
+// greedy_quota (ferry/quota.py:25-67) on one warp; lane r owns rank r.
+__device__ bool greedy_quota_warp(const PlanConfig& c, int m, const int* capacity,
+                                  int64_t* quota, int64_t* load /*[G] scratch*/) {
+  const int lane = threadIdx.x & 31;
+  const int R = c.world, G = c.n_domains;
+  for (int g = lane; g < G; g += 32) load[g] = 0;
+  double single = 0.0;
+  if (lane < R)
+    for (int g = 0; g < G; ++g)
+      if (c.masks[g] == ((int64_t)1 << lane)) single = c.seconds[g];
+  int64_t q = 0;
+  __syncwarp();
+  for (int step = 0; step < m; ++step) {
+    double t = 0.0, total = 0.0, own = 0.0;
+    const bool can = lane < R && q < capacity[lane];
+    if (can) {
+      for (int g = 0; g < G; ++g) {
+        const double v = __dmul_rn((double)(load[g] + ((c.masks[g] >> lane) & 1)), c.seconds[g]);
+        total = __dadd_rn(total, v);
+        if (v > t) t = v;
+      }
+      own = __dmul_rn((double)(q + 1), single);
+    }
+    // Sequential tie-break scan over ranks 0..R-1 (lane 0 holds the winner).
+    int best = -1;
+    double best_t = CUDART_INF, best_sum = CUDART_INF, best_own = CUDART_INF;
+    for (int r = 0; r < R; ++r) {
+      const int cr = __shfl_sync(0xffffffffu, (int)can, r);
+      const double tr = __shfl_sync(0xffffffffu, t, r);
+      const double sr = __shfl_sync(0xffffffffu, total, r);
+      const double orr = __shfl_sync(0xffffffffu, own, r);
+      if (!cr) continue;
+      bool better = false;
+      if (tr < __dmul_rn(best_t, 1 - 1e-12)) {
+        better = true;
+      } else if (tr <= __dmul_rn(best_t, 1 + 1e-12)) {
+        if (sr < __dmul_rn(best_sum, 1 - 1e-12)) better = true;
+        else if (sr <= __dmul_rn(best_sum, 1 + 1e-12) && orr < __dmul_rn(best_own, 1 - 1e-12))
+          better = true;
+      }
+      if (better) { best = r; best_t = tr; best_sum = sr; best_own = orr; }
+    }
+    if (best < 0) return false;
+    if (lane == best) q += 1;
+    __syncwarp();
+    for (int g = lane; g < G; g += 32) load[g] += (c.masks[g] >> best) & 1;
+    __syncwarp();
+  }
+  if (lane < R) quota[lane] = q;
+  __syncwarp();
+  return true;
+}
+
+// load_balanced_assignment (ferry/policy.py:49-106) on one warp.
+__device__ void assignment_warp(const PlanConfig& c, PlanSmem& sm, const int* demand /*[E*R]*/,
+                                const int* owner_layer /*[E]*/) {
+  const int lane = threadIdx.x & 31;
+  const int R = c.world, E = c.experts, m = sm.m;
+  // N_r: tokens routed to experts already cached on r.
+  int64_t load = 0, remaining = 0;
+  if (lane < R) {
+    for (int e = 0; e < E; ++e)
+      if (owner_layer[e] == lane) load += sm.demand_total[e];
+    remaining = sm.quota[lane];
+  }
+  for (int oi = 0; oi < m; ++oi) {
+    const int i = sm.order[oi];
+    const int e = sm.misses[i];
+    const int64_t total = sm.totals[i];
+    int64_t peak = (lane < R) ? load : INT64_MIN;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int64_t v = __shfl_xor_sync(0xffffffffu, peak, o);
+      peak = v > peak ? v : peak;
+    }
+    const bool has = lane < R && remaining > 0;
+    const int64_t projected = has ? (peak > load + total ? peak : load + total) : ((int64_t)1 << 60);
+    int64_t lowest = projected;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int64_t v = __shfl_xor_sync(0xffffffffu, lowest, o);
+      lowest = v < lowest ? v : lowest;
+    }
+    int64_t slack = 0;
+    if (c.bps > 0) {
+      const int64_t prod = (int64_t)((uint64_t)lowest * (uint64_t)c.bps);
+      int64_t qd = prod / 10000;
+      if ((prod % 10000 != 0) && (prod < 0)) qd -= 1;  // floor division
+      slack = qd > 1 ? qd : 1;
+    }
+    const int64_t limit = lowest + slack;
+    const bool eligible = has && projected <= limit;
+    const int a = (lane < R) ? demand[e * R + lane] : 0;
+    // lexicographic max of (a, -projected, -load), lowest lane on ties
+    int best = eligible ? lane : -1;
+    int ba = a;
+    int64_t bp = projected, bl = load;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oa = __shfl_xor_sync(0xffffffffu, ba, o);
+      const int64_t op = __shfl_xor_sync(0xffffffffu, bp, o);
+      const int64_t ol = __shfl_xor_sync(0xffffffffu, bl, o);
+      bool take;
+      if (ob < 0) take = false;
+      else if (best < 0) take = true;
+      else if (oa != ba) take = oa > ba;
+      else if (op != bp) take = op < bp;
+      else if (ol != bl) take = ol < bl;
+      else take = ob < best;
+      if (take) { best = ob; ba = oa; bp = op; bl = ol; }
+    }
+    if (lane == 0) sm.assignment[i] = best;
+    if (best >= 0 && lane == best) { remaining -= 1; load += total; }
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kPlanThreads, 1)
+    plan_kernel(const PlanConfig c, const PlanState s, const PlanInputs in, const PlanOutputs out) {
+  extern __shared__ uint8_t dsm[];
+  __shared__ PlanSmem sm;
+  const int E = c.experts, R = c.world, K = c.topk;
+  const int L = in.layer;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_tok = in.n_tokens;
+  int* demand = reinterpret_cast<int*>(dsm);                            // [E*R]
+  SlotRec* recs = reinterpret_cast<SlotRec*>(dsm + c.sort_offset);       // [sort_n]
+  int64_t* greedy_load = reinterpret_cast<int64_t*>(dsm + c.greedy_offset);  // [G]
+
+  if (tid == 0) { sm.status = 0; sm.m = 0; }
+  for (int i = tid; i < E * R; i += blockDim.x) demand[i] = 0;
+  __syncthreads();
+
+  // -- gate scores: given, or from the device GateHistory -------------------
+  if (in.gate_scores) {
+    for (int e = tid; e < E; e += blockDim.x) sm.gate[e] = in.gate_scores[e];
+  } else {
+    history_step(c, s, in, sm.gate);
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) s.scores[(size_t)L * E + e] = sm.gate[e];
+
+  // -- Step 1: demand d[e, r] ----------------------------------------------
+  for (int i = tid; i < n_tok * K; i += blockDim.x) {
+    const int t = i / K;
+    const int e = in.ids[i];
+    const int r = in.origins ? (int)in.origins[t] : t / in.tokens_per_rank;
+    if (e >= E || r < 0 || r >= R) { sm.status = DEV_BAD_INPUT; continue; }
+    atomicAdd(&demand[e * R + r], 1);
+  }
+  __syncthreads();
+  const int base = L * E;
+  for (int e = tid; e < E; e += blockDim.x) {
+    int tot = 0;
+    for (int r = 0; r < R; ++r) tot += demand[e * R + r];
+    sm.demand_total[e] = tot;
+    sm.active[e] = tot > 0;
+  }
+  if (tid < R) { sm.capacity[tid] = 0; sm.n_assigned[tid] = 0; }
+  __syncthreads();
+  // misses in ascending expert order (warp 0 ballot compaction)
+  if (warp == 0) {
+    int m = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const bool miss = e < E && sm.active[e] && s.owner[base + e] < 0;
+      const unsigned bal = __ballot_sync(0xffffffffu, miss);
+      if (miss) sm.misses[m + __popc(bal & ((1u << lane) - 1))] = e;
+      m += __popc(bal);
+    }
+    if (lane == 0) sm.m = m;
+  }
+  // admission capacity u_r (ferry/policy.py:36-46)
+  for (int i = tid; i < c.total_slots; i += blockDim.x) {
+    const int r = c.slot_rank[i];
+    const int key = s.slots[c.slot_index[i]];
+    const bool free_ = key < 0 || !(key / E == L && sm.active[key % E]);
+    if (free_) atomicAdd(&sm.capacity[r], 1);
+  }
+  __syncthreads();
+  const int m = sm.m;
+
+  // -- Steps 2-3 (FERRY) or the random draw (RANDOM) ----------------------
+  if (c.policy == 0) {
+    if (warp == 0) {
+      bool over = false;
+      if (m >= c.lut_rows) {
+        if (lane == 0) sm.status = DEV_BAD_INPUT;
+      } else if (lane < R) {
+        sm.quota[lane] = c.lut[(size_t)m * R + lane];
+        over = sm.quota[lane] > sm.capacity[lane];
+      }
+      over = __any_sync(0xffffffffu, over);
+      __syncwarp();
+      if (over && sm.status == 0) {
+        if (!greedy_quota_warp(c, m, sm.capacity, sm.quota, greedy_load) && lane == 0)
+          sm.status = DEV_CAPACITY;
+      }
+    }
+    // totals and the stable descending order (np.argsort(-totals, 'mergesort'))
+    for (int i = tid; i < m; i += blockDim.x) sm.totals[i] = sm.demand_total[sm.misses[i]];
+    __syncthreads();
+    for (int i = tid; i < m; i += blockDim.x) {
+      int rank_i = 0;
+      const int64_t ti = sm.totals[i];
+      for (int j = 0; j < m; ++j) {
+        const int64_t tj = sm.totals[j];
+        rank_i += (tj > ti) || (tj == ti && j < i);
+      }
+      sm.order[rank_i] = i;
+    }
+    __syncthreads();
+    if (warp == 0 && sm.status == 0) assignment_warp(c, sm, demand, s.owner + base);
+  } else {
+    if (tid == 0) {
+      int room = 0, left[kMaxWorld];
+      for (int r = 0; r < R; ++r) { left[r] = sm.capacity[r]; room += left[r]; }
+      if (m > room) {
+        sm.status = DEV_CAPACITY;  // the reference would retry forever here
+      } else {
+        sm.rng.seed((uint32_t)(uint64_t)(c.salt * 1000003 + in.event));
+        for (int i = 0; i < m; ++i) {
+          int r = sm.rng.randint(R);
+          while (left[r] <= 0) r = sm.rng.randint(R);
+          sm.assignment[i] = r;
+          left[r] -= 1;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (sm.status) {
+    if (tid == 0) {
+      set_err(out.err, sm.status);
+      *out.n_fetches = 0;
+    }
+    return;
+  }
+
+  // -- Step 4: victims (one sort of every slot) and the commit -------------
+  if (m > 0) {
+    const int n = c.sort_n;  // power of two >= total_slots
+    for (int i = tid; i < n; i += blockDim.x) {
+      SlotRec rec;
+      if (i < c.total_slots) {
+        const int r = c.slot_rank[i];
+        const int idx = c.slot_index[i];
+        const int key = s.slots[idx];
+        uint64_t cls, k0lo, k1;
+        if (key < 0) {
+          cls = 0; k0lo = 0; k1 = (uint64_t)(idx - r * c.maxcap);
+        } else if (key / E == L && sm.active[key % E]) {
+          cls = 2; k0lo = 0; k1 = 0;
+        } else {
+          cls = 1;
+          k0lo = __float_as_uint(s.scores[key]);
+          k1 = ((uint64_t)s.last[key] << 24) | (uint64_t)key;
+        }
+        rec.k0 = ((uint64_t)r << 56) | (cls << 48) | k0lo;
+        rec.k1 = k1;
+        rec.slot = (uint32_t)idx;
+      } else {
+        rec.k0 = ~0ull; rec.k1 = ~0ull; rec.slot = 0xffffffffu;
+      }
+      recs[i] = rec;
+    }
+    __syncthreads();
+    // bitonic sort, ascending
+    for (int size = 2; size <= n; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = tid; i < n / 2; i += blockDim.x) {
+          const int lo = 2 * i - (i & (stride - 1));
+          const int hi = lo + stride;
+          const bool up = (lo & size) == 0;
+          SlotRec a = recs[lo], b = recs[hi];
+          if (rec_less(b, a) == up) { recs[lo] = b; recs[hi] = a; }
+        }
+        __syncthreads();
+      }
+    }
+    // j-th miss of rank r takes the j-th record of rank r's segment
+    if (tid == 0) {
+      int pos = 0;
+      for (int r = 0; r < R; ++r) { sm.seg_start[r] = pos; pos += c.capacities[r]; }
+      for (int i = 0; i < m; ++i) {
+        const int r = sm.assignment[i];
+        sm.victim_pos[i] = sm.seg_start[r] + sm.n_assigned[r];
+        sm.n_assigned[r] += 1;
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < m; i += blockDim.x) {
+      const int r = sm.assignment[i];
+      const SlotRec rec = recs[sm.victim_pos[i]];
+      const uint64_t cls = (rec.k0 >> 48) & 0xff;
+      const bool ok = rec.slot != 0xffffffffu && (int)(rec.k0 >> 56) == r && cls < 2 &&
+                      sm.victim_pos[i] < sm.seg_start[r] + c.capacities[r];
+      if (!ok) { set_err(out.err, DEV_NO_SLOT); continue; }
+      const int idx = (int)rec.slot;
+      const int key = base + sm.misses[i];
+      const int victim = s.slots[idx];
+      if (victim >= 0) s.owner[victim] = -1;
+      s.slots[idx] = key;
+      s.owner[key] = r;
+      out.fetches[i * 3 + 0] = r;
+      out.fetches[i * 3 + 1] = key;
+      out.fetches[i * 3 + 2] = idx - r * c.maxcap;
+    }
+  }
+  __syncthreads();
+  const int64_t tick = in.event + 1;
+  for (int e = tid; e < E; e += blockDim.x)
+    if (sm.active[e]) s.last[base + e] = tick;
+  if (tid < R) out.counts[tid] = 0;
+  __syncthreads();
+  if (tid == 0) *out.n_fetches = m;
+  for (int i = tid; i < m; i += blockDim.x) atomicAdd(&out.counts[sm.assignment[i]], 1);
+  for (int i = tid; i < n_tok * K; i += blockDim.x) {
+    const int e = in.ids[i];
+    out.dest[i] = e < E ? s.owner[base + e] : -1;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Single-step kernels: the planner's device functions exposed one by one, for
+// the reference's helper names (quota.py:25/70, policy.py:25/36/49/109).
+
+// greedy_quota for m in [m_begin, m_end), one warp per m.  capacity NULL =
+// unlimited (build_lut, ferry/quota.py:70-74).
+__global__ void greedy_rows_kernel(const PlanConfig c, const int32_t* capacity, int m_begin,
+                                   int m_end, int64_t* quota_out, int* err) {
+  extern __shared__ uint8_t dsm[];
+  __shared__ int cap[kMaxWorld];
+  __shared__ int64_t qsm[32][kMaxWorld];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  int64_t* load = reinterpret_cast<int64_t*>(dsm) + (size_t)warp * (c.n_domains > 0 ? c.n_domains : 1);
+  if (threadIdx.x < c.world) cap[threadIdx.x] = capacity ? capacity[threadIdx.x] : (1 << 30);
+  __syncthreads();
+  for (int m = m_begin + blockIdx.x * nw + warp; m < m_end; m += gridDim.x * nw) {
+    const bool ok = greedy_quota_warp(c, m, cap, qsm[warp], load);
+    if (!ok) {
+      if (lane == 0) set_err(err, DEV_CAPACITY);
+    } else if (lane < c.world) {
+      quota_out[(size_t)(m - m_begin) * c.world + lane] = qsm[warp][lane];
+    }
+  }
+}
+
+__global__ void demand_kernel(const int64_t* selected, const int64_t* origins, int n_tokens,
+                              int topk, int experts, int world, int64_t* d, int* err) {
+  for (int i = threadIdx.x + blockIdx.x * blockDim.x; i < n_tokens * topk; i += blockDim.x * gridDim.x) {
+    const int64_t e = selected[i], r = origins[i / topk];
+    if (e < 0 || e >= experts || r < 0 || r >= world) { set_err(err, DEV_BAD_INPUT); continue; }
+    atomicAdd(reinterpret_cast<unsigned long long*>(&d[e * world + r]), 1ull);
+  }
+}
+
+__global__ void admission_kernel(const int32_t* slots, int maxcap, const int32_t* capacities,
+                                 int world, int layer, const uint8_t* active, int experts,
+                                 int64_t* u) {
+  const int r = blockIdx.x;
+  __shared__ int cnt;
+  if (threadIdx.x == 0) cnt = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < capacities[r]; i += blockDim.x) {
+    const int key = slots[r * maxcap + i];
+    if (key < 0 || !(key / experts == layer && active[key % experts])) atomicAdd(&cnt, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) u[r] = cnt;
+}
+
+__global__ void assignment_kernel(const PlanConfig c, const int64_t* demand, const int64_t* misses,
+                                  int m, const int32_t* owner, int layer, const int64_t* quota,
+                                  int64_t* answer) {
+  __shared__ PlanSmem sm;
+  extern __shared__ uint8_t dsm[];
+  int* dem = reinterpret_cast<int*>(dsm);
+  const int E = c.experts, R = c.world, tid = threadIdx.x;
+  for (int i = tid; i < E * R; i += blockDim.x) dem[i] = (int)demand[i];
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) {
+    int tot = 0;
+    for (int r = 0; r < R; ++r) tot += dem[e * R + r];
+    sm.demand_total[e] = tot;
+  }
+  if (tid < R) sm.quota[tid] = quota[tid];
+  if (tid == 0) sm.m = m;
+  for (int i = tid; i < m; i += blockDim.x) sm.misses[i] = (int)misses[i];
+  __syncthreads();
+  for (int i = tid; i < m; i += blockDim.x) sm.totals[i] = sm.demand_total[sm.misses[i]];
+  __syncthreads();
+  for (int i = tid; i < m; i += blockDim.x) {
+    int rank_i = 0;
+    const int64_t ti = sm.totals[i];
+    for (int j = 0; j < m; ++j) rank_i += (sm.totals[j] > ti) || (sm.totals[j] == ti && j < i);
+    sm.order[rank_i] = i;
+  }
+  __syncthreads();
+  if ((tid >> 5) == 0) assignment_warp(c, sm, dem, owner + (size_t)layer * E);
+  __syncthreads();
+  for (int i = tid; i < m; i += blockDim.x) answer[i] = sm.assignment[i];
+}
+
+// _choose_slot for one rank: the minimum slot record of that rank (empty
+// slots by index first, then eligible ones by (score, last use, key)).
+__global__ void choose_slot_kernel(int rank, int layer, const uint8_t* active, const int32_t* slots,
+                                   int maxcap, const int32_t* capacities, const int64_t* last,
+                                   const float* scores, int experts, int64_t* result) {
+  __shared__ SlotRec best[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  SlotRec mine;
+  mine.k0 = ~0ull; mine.k1 = ~0ull; mine.slot = 0xffffffffu; mine.pad = 0;
+  for (int i = threadIdx.x; i < capacities[rank]; i += blockDim.x) {
+    const int key = slots[rank * maxcap + i];
+    SlotRec r;
+    r.slot = (uint32_t)i; r.pad = 0;
+    if (key < 0) { r.k0 = 0; r.k1 = (uint64_t)i; }
+    else if (key / experts == layer && active[key % experts]) { r.k0 = ~0ull; r.k1 = ~0ull; r.slot = 0xffffffffu; }
+    else { r.k0 = (1ull << 48) | __float_as_uint(scores[key]); r.k1 = ((uint64_t)last[key] << 24) | (uint64_t)key; }
+    if (rec_less(r, mine)) mine = r;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    SlotRec other;
+    other.k0 = __shfl_xor_sync(0xffffffffu, mine.k0, o);
+    other.k1 = __shfl_xor_sync(0xffffffffu, mine.k1, o);
+    other.slot = __shfl_xor_sync(0xffffffffu, mine.slot, o);
+    if (rec_less(other, mine)) mine = other;
+  }
+  if (lane == 0) best[warp] = mine;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    SlotRec b = best[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) if (rec_less(best[w], b)) b = best[w];
+    *result = b.slot == 0xffffffffu ? -1 : (int64_t)b.slot;
+  }
+}
+
+// ---------------------------------------------------------------------------
+int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
+                const PlanOutputs& out, cudaStream_t stream) {
+  const size_t dyn = c.dyn_smem;
+  static int configured_bytes = -1;
+  if ((int)dyn > configured_bytes) {
+    FB_CUDA(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
+    configured_bytes = (int)dyn;
+  }
+  plan_kernel<<<1, kPlanThreads, dyn, stream>>>(c, s, in, out);
+  FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}
+
+size_t plan_dyn_smem(int experts, int world, int total_slots, int n_domains, size_t* sort_off,
+                     size_t* greedy_off, int* sort_n) {
+  size_t off = (size_t)experts * world * sizeof(int);
+  off = (off + 15) & ~size_t(15);
+  int n = 1;
+  while (n < total_slots) n <<= 1;
+  *sort_n = n;
+  *sort_off = off;
+  off += (size_t)n * sizeof(SlotRec);
+  *greedy_off = off;
+  off += (size_t)(n_domains > 0 ? n_domains : 1) * sizeof(int64_t);
+  return off;
+}
+
+size_t plan_static_smem() { return sizeof(PlanSmem); }
+
+}  // namespace ferryb
+
+using namespace ferryb;
+
+extern "C" int ferryb_plan_layer(const ferryb_planner* p, int64_t event, int32_t layer,
+                                 const uint8_t* ids, int32_t n_tokens, int32_t tokens_per_rank,
+                                 const int64_t* origins, const float* gate_scores,
+                                 const float* prob_rows, int32_t n_prob_rows, int32_t* fetches,
+                                 int32_t* n_fetches, int32_t* dest, int32_t* counts, int32_t* err,
+                                 cudaStream_t stream) {
+  FB_CHECK_ARG(p != nullptr, "planner is NULL");
+  FB_CHECK_ARG(p->world >= 1 && p->world <= kMaxWorld, "world must be in [1, %d]", kMaxWorld);
+  FB_CHECK_ARG(p->experts >= 1 && p->experts <= kMaxExperts, "experts must be in [1, %d]",
+               kMaxExperts);
+  FB_CHECK_ARG(layer >= 0 && layer < p->layers, "layer %d out of range", layer);
+  FB_CHECK_ARG((int64_t)p->layers * p->experts < (1 << 24), "layers * experts must be < 2^24");
+  FB_CHECK_ARG(event >= 0 && event < ((int64_t)1 << 39), "event out of range");
+  FB_CHECK_ARG(p->policy == 0 || p->policy == 1, "policy must be 0 (ferry) or 1 (random)");
+  FB_CHECK_ARG(n_tokens >= 0 && p->topk >= 1 && p->window >= 1, "bad sizes");
+  FB_CHECK_ARG(origins != nullptr || (tokens_per_rank > 0 && n_tokens == tokens_per_rank * p->world),
+               "without origins, n_tokens must be world * tokens_per_rank");
+  FB_CHECK_ARG(gate_scores != nullptr || origins == nullptr,
+               "the device history needs rank-major tokens (origins NULL)");
+  FB_CHECK_ARG(p->slots && p->owner && p->last && p->scores && p->capacities && p->slot_rank &&
+                   p->slot_index && (p->policy == 1 || (p->lut && p->masks && p->seconds)),
+               "planner state/config pointers missing");
+  FB_CHECK_ARG(gate_scores || (p->ring && p->hist_count && p->hist_head),
+               "history state missing");
+  FB_CHECK_ARG(fetches && n_fetches && dest && counts && err, "output pointers missing");
+  PlanConfig c{};
+  c.world = p->world; c.experts = p->experts; c.layers = p->layers; c.topk = p->topk;
+  c.window = p->window; c.policy = p->policy; c.bps = p->balance_tol_bps; c.salt = p->salt;
+  c.maxcap = p->maxcap; c.total_slots = p->total_slots; c.n_domains = p->n_domains;
+  c.lut_rows = p->lut_rows; c.capacities = p->capacities; c.slot_rank = p->slot_rank;
+  c.slot_index = p->slot_index; c.lut = p->lut; c.masks = p->masks; c.seconds = p->seconds;
+  c.dyn_smem = plan_dyn_smem(c.experts, c.world, c.total_slots, c.n_domains, &c.sort_offset,
+                             &c.greedy_offset, &c.sort_n);
+  FB_CHECK_ARG(c.dyn_smem + plan_static_smem() <= 225 * 1024,
+               "cache too large for the one-CTA planner (%d slots)", c.total_slots);
+  PlanState s{p->slots, p->owner, p->last, p->scores, p->ring, p->ring_p, p->hist_count,
+              p->hist_head};
+  PlanInputs in{};
+  in.ids = ids; in.n_tokens = n_tokens; in.tokens_per_rank = tokens_per_rank;
+  in.origins = origins; in.gate_scores = gate_scores; in.prob_rows = prob_rows;
+  in.n_prob_rows = n_prob_rows; in.event = event; in.layer = layer;
+  PlanOutputs out{fetches, n_fetches, dest, counts, err};
+  return plan_launch(c, s, in, out, stream);
+}
+
+static PlanConfig config_of(const ferryb_planner* p) {
+  PlanConfig c{};
+  c.world = p->world; c.experts = p->experts; c.layers = p->layers; c.topk = p->topk;
+  c.window = p->window; c.policy = p->policy; c.bps = p->balance_tol_bps; c.salt = p->salt;
+  c.maxcap = p->maxcap; c.total_slots = p->total_slots; c.n_domains = p->n_domains;
+  c.lut_rows = p->lut_rows; c.capacities = p->capacities; c.slot_rank = p->slot_rank;
+  c.slot_index = p->slot_index; c.lut = p->lut; c.masks = p->masks; c.seconds = p->seconds;
+  return c;
+}
+
+extern "C" int ferryb_greedy_quota_rows(int32_t world, const int64_t* masks, const double* seconds,
+                                        int32_t n_domains, const int32_t* capacity, int32_t m_begin,
+                                        int32_t m_end, int64_t* quota_out, int32_t* err,
+                                        cudaStream_t stream) {
+  FB_CHECK_ARG(world >= 1 && world <= kMaxWorld && n_domains >= 0 && m_begin >= 0 && m_end >= m_begin,
+               "greedy_quota: bad arguments");
+  FB_CHECK_ARG(masks && seconds && quota_out && err, "greedy_quota: null pointer");
+  if (m_end == m_begin) return FERRYB_OK;
+  PlanConfig c{};
+  c.world = world; c.masks = masks; c.seconds = seconds; c.n_domains = n_domains;
+  const int warps = 8;
+  const size_t dyn = (size_t)warps * (n_domains > 0 ? n_domains : 1) * sizeof(int64_t);
+  int blocks = (m_end - m_begin + warps - 1) / warps;
+  if (blocks > 148) blocks = 148;
+  greedy_rows_kernel<<<blocks, warps * 32, dyn, stream>>>(c, capacity, m_begin, m_end, quota_out, err);
+  FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_demand(const int64_t* selected, const int64_t* origins, int32_t n_tokens,
+                             int32_t topk, int32_t experts, int32_t world, int64_t* demand,
+                             int32_t* err, cudaStream_t stream) {
+  FB_CHECK_ARG(selected && origins && demand && err && n_tokens >= 0 && topk > 0, "demand: bad arguments");
+  FB_CUDA(cudaMemsetAsync(demand, 0, sizeof(int64_t) * experts * world, stream));
+  if (n_tokens == 0) return FERRYB_OK;
+  demand_kernel<<<(n_tokens * topk + 255) / 256, 256, 0, stream>>>(selected, origins, n_tokens, topk,
+                                                                   experts, world, demand, err);
+  FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_admission_capacity(const int32_t* slots, int32_t maxcap,
+                                         const int32_t* capacities, int32_t world, int32_t layer,
+                                         const uint8_t* active, int32_t experts, int64_t* u,
+                                         cudaStream_t stream) {
+  FB_CHECK_ARG(slots && capacities && active && u && world >= 1, "admission: bad arguments");
+  admission_kernel<<<world, 256, 0, stream>>>(slots, maxcap, capacities, world, layer, active, experts, u);
+  FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_load_balanced_assignment(const int64_t* demand, int32_t experts, int32_t world,
+                                               const int64_t* misses, int32_t m,
+                                               const int32_t* owner, int32_t layer,
+                                               const int64_t* quota, int64_t balance_tol_bps,
+                                               int64_t* answer, cudaStream_t stream) {
+  FB_CHECK_ARG(world >= 1 && world <= kMaxWorld && experts >= 1 && experts <= kMaxExperts &&
+                   m >= 0 && m <= experts,
+               "assignment: bad sizes");
+  if (m == 0) return FERRYB_OK;
+  PlanConfig c{};
+  c.world = world; c.experts = experts; c.bps = balance_tol_bps;
+  assignment_kernel<<<1, 1024, (size_t)experts * world * sizeof(int), stream>>>(
+      c, demand, misses, m, owner, layer, quota, answer);
+  FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_choose_slot(int32_t rank, int32_t layer, const uint8_t* active,
+                                  const int32_t* slots, int32_t maxcap, const int32_t* capacities,
+                                  const int64_t* last, const float* scores, int32_t experts,
+                                  int64_t* result, cudaStream_t stream) {
+  FB_CHECK_ARG(active && slots && capacities && last && scores && result && rank >= 0,
+               "choose_slot: bad arguments");
+  choose_slot_kernel<<<1, 1024, 0, stream>>>(rank, layer, active, slots, maxcap, capacities, last,
+                                             scores, experts, result);
+  FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}

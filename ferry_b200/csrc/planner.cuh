@@ -1,0 +1,63 @@
+// planner.cuh -- kernel-side view of the planner's configuration and state.
+#pragma once
+#include <stdint.h>
+
+#include "../../include/ferryb.h"
+
+namespace ferryb {
+
+constexpr int kMaxExperts = 256;  // ids travel as uint8 (ferry/metadata.py:70)
+constexpr int kMaxWorld = 32;     // ranks handled by one warp's lanes
+
+struct PlanConfig {
+  int world, experts, layers, topk, window, policy;
+  int64_t bps, salt;
+  int maxcap, total_slots, n_domains, lut_rows;
+  const int32_t* capacities;  // [world]
+  const int32_t* slot_rank;   // [total_slots]
+  const int32_t* slot_index;  // [total_slots] = rank * maxcap + i
+  const int64_t* lut;         // [lut_rows, world]
+  const int64_t* masks;       // [n_domains]
+  const double* seconds;      // [n_domains]
+  // derived launch geometry
+  size_t dyn_smem, sort_offset, greedy_offset;
+  int sort_n;
+};
+
+struct PlanState {
+  int32_t* slots;   // [world, maxcap]
+  int32_t* owner;   // [layers * experts]
+  int64_t* last;    // [layers * experts]
+  float* scores;    // [layers, experts]
+  uint8_t* ring;    // [layers, window, topk]
+  float* ring_p;    // [layers, window, experts] (probability score) or null
+  int32_t* hist_count;
+  int32_t* hist_head;
+};
+
+struct PlanInputs {
+  const uint8_t* ids;  // [n_tokens, topk] gathered expert ids
+  int n_tokens, tokens_per_rank;
+  const int64_t* origins;     // [n_tokens] or null (rank-major)
+  const float* gate_scores;   // [experts] or null (use the device history)
+  const float* prob_rows;     // [n_prob_rows, experts] or null
+  int n_prob_rows;
+  int64_t event;
+  int layer;
+};
+
+struct PlanOutputs {
+  int32_t* fetches;    // [experts, 3] (rank, key, slot)
+  int32_t* n_fetches;  // [1]
+  int32_t* dest;       // [n_tokens, topk]
+  int32_t* counts;     // [world]
+  int* err;            // [1]
+};
+
+int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
+                const PlanOutputs& out, cudaStream_t stream);
+size_t plan_dyn_smem(int experts, int world, int total_slots, int n_domains, size_t* sort_off,
+                     size_t* greedy_off, int* sort_n);
+size_t plan_static_smem();
+
+}  // namespace ferryb

@@ -1,0 +1,222 @@
+"""Drop-in for ferry/policy.py: the global placement controller on the GPU.
+
+Controller keeps the reference's constructor and plan() signature
+(ferry/policy.py:208-228); its cache state (slots, owner, last, scores) and
+the GateHistory ring live in device memory and are updated by kernel 2
+(ferryb_plan_layer) in one CTA, bit-exact with the reference's decisions.
+plan() takes and returns numpy arrays like the reference; plan_device() is
+the fused path's asynchronous variant (device ids in, device outputs, no
+host synchronisation).
+
+The step functions (_demand, _admission_capacity, load_balanced_assignment,
+_choose_slot, layer_slots, plan_layer) keep their reference signatures and
+run the same device code one step at a time.
+"""
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import addr, call, ptr, stream_ptr
+
+FERRY, RANDOM = 0, 1
+POLICIES = {'ferry': FERRY, 'random': RANDOM}
+
+
+def _dev(device=None):
+    return torch.device('cuda', torch.cuda.current_device()) if device is None else torch.device(device)
+
+
+def _t(a, dtype, dev):
+    return torch.as_tensor(np.ascontiguousarray(a), device=dev).to(dtype)
+
+
+def _demand(selected, origins, experts, world):
+    """ferry/policy.py:25-33."""
+    dev = _dev()
+    sel, org = _t(selected, torch.int64, dev), _t(origins, torch.int64, dev)
+    d = torch.zeros((experts, world), dtype=torch.int64, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    call('ferryb_demand', ptr(sel), ptr(org), sel.shape[0], sel.shape[1], experts, world, ptr(d),
+         ptr(err), stream_ptr(dev))
+    _lib.check_device_error(err, '_demand')
+    return d.cpu().numpy()
+
+
+def _admission_capacity(slots, capacities, layer, active, experts):
+    """ferry/policy.py:36-46."""
+    dev = _dev()
+    sl = _t(slots, torch.int32, dev)
+    caps = _t(capacities, torch.int32, dev)
+    act = _t(np.asarray(active, np.uint8), torch.uint8, dev)
+    u = torch.zeros(len(capacities), dtype=torch.int64, device=dev)
+    call('ferryb_admission_capacity', ptr(sl), sl.shape[1], ptr(caps), len(capacities), layer,
+         ptr(act), experts, ptr(u), stream_ptr(dev))
+    return u.cpu().numpy()
+
+
+def load_balanced_assignment(demand, misses, owner, layer, quota, balance_tol_bps):
+    """ferry/policy.py:49-106."""
+    dev = _dev()
+    demand = np.asarray(demand, np.int64)
+    experts, world = demand.shape
+    m = len(misses)
+    ans = torch.zeros(max(m, 1), dtype=torch.int64, device=dev)
+    call('ferryb_load_balanced_assignment', ptr(_t(demand, torch.int64, dev)), experts, world,
+         ptr(_t(np.asarray(misses, np.int64).reshape(-1) if m else np.zeros(1, np.int64), torch.int64, dev)),
+         m, ptr(_t(owner, torch.int32, dev)), layer, ptr(_t(quota, torch.int64, dev)),
+         int(balance_tol_bps), ptr(ans), stream_ptr(dev))
+    return ans[:m].cpu().numpy()
+
+
+def _choose_slot(rank, layer, active, slots, capacities, last, scores, experts):
+    """ferry/policy.py:109-127 -> slot index or -1."""
+    dev = _dev()
+    slots = np.asarray(slots)
+    res = torch.zeros(1, dtype=torch.int64, device=dev)
+    call('ferryb_choose_slot', rank, layer, ptr(_t(np.asarray(active, np.uint8), torch.uint8, dev)),
+         ptr(_t(slots, torch.int32, dev)), slots.shape[1], ptr(_t(capacities, torch.int32, dev)),
+         ptr(_t(last, torch.int64, dev)), ptr(_t(scores, torch.float32, dev)), experts, ptr(res),
+         stream_ptr(dev))
+    return int(res.item())
+
+
+def layer_slots(slots_row, capacity, layer, experts):
+    """ferry/policy.py:197-205."""
+    dev = _dev()
+    row = _t(slots_row, torch.int32, dev)
+    out = torch.empty(experts, dtype=torch.int32, device=dev)
+    call('ferryb_layer_slots', ptr(row), int(capacity), int(layer), int(experts), ptr(out),
+         stream_ptr(dev))
+    return out.cpu().numpy().astype(np.int64)
+
+
+class _Spec:
+    def __init__(self, layers, experts, topk):
+        self.layers, self.experts, self.topk = layers, experts, topk
+
+
+class Controller:
+    """Replicated placement controller (ferry/policy.py:208-228) with device state."""
+
+    def __init__(self, spec, capacities, policy, topology, balance_tol_bps=200, salt=1, *,
+                 device=None, window=128, score='frequency', topk=None):
+        self.spec = spec
+        self.policy = POLICIES[policy] if isinstance(policy, str) else int(policy)
+        self.capacities = np.asarray(capacities, np.int64)
+        self.balance_tol_bps, self.salt = int(balance_tol_bps), int(salt)
+        self.masks, self.seconds, self.lut = topology.masks, topology.seconds, topology.lut
+        self.device = _dev(device)
+        self.window = int(window)
+        self.score = score
+        self.topk = int(topk if topk is not None else getattr(spec, 'topk', 8))
+        dev = self.device
+        world = len(self.capacities)
+        self.world = world
+        self.maxcap = int(self.capacities.max())
+        rank_of = np.concatenate([np.full(c, r, np.int32) for r, c in enumerate(self.capacities)])
+        index_of = np.concatenate([r * self.maxcap + np.arange(c, dtype=np.int32)
+                                   for r, c in enumerate(self.capacities)])
+        self._caps = torch.as_tensor(self.capacities.astype(np.int32), device=dev)
+        self._slot_rank = torch.as_tensor(rank_of, device=dev)
+        self._slot_index = torch.as_tensor(index_of, device=dev)
+        self._lut = torch.as_tensor(np.asarray(self.lut, np.int64), device=dev)
+        self._masks = torch.as_tensor(np.asarray(self.masks, np.int64), device=dev)
+        self._seconds = torch.as_tensor(np.asarray(self.seconds, np.float64), device=dev)
+        E = spec.experts
+        self._fetches = torch.zeros((E, 3), dtype=torch.int32, device=dev)
+        self._n_fetches = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._counts = torch.zeros(world, dtype=torch.int32, device=dev)
+        self._err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.reset()
+
+    def reset(self):
+        dev, L, E, W, K = self.device, self.spec.layers, self.spec.experts, self.window, self.topk
+        self._slots = torch.full((self.world, self.maxcap), -1, dtype=torch.int32, device=dev)
+        self._owner = torch.full((L * E,), -1, dtype=torch.int32, device=dev)
+        self._last = torch.zeros(L * E, dtype=torch.int64, device=dev)
+        self._scores = torch.zeros((L, E), dtype=torch.float32, device=dev)
+        self._ring = torch.zeros((L, W, K), dtype=torch.uint8, device=dev)
+        self._ring_p = (torch.zeros((L, W, E), dtype=torch.float32, device=dev)
+                        if self.score == 'probability' else None)
+        self._hist_count = torch.zeros(L, dtype=torch.int32, device=dev)
+        self._hist_head = torch.zeros(L, dtype=torch.int32, device=dev)
+        s = _lib.Planner()
+        s.world, s.experts, s.layers, s.topk, s.window = self.world, E, L, K, W
+        s.policy, s.balance_tol_bps, s.salt = self.policy, self.balance_tol_bps, self.salt
+        s.maxcap, s.total_slots = self.maxcap, int(self.capacities.sum())
+        s.n_domains, s.lut_rows = len(self._masks), int(self._lut.shape[0])
+        for name, t in (('capacities', self._caps), ('slot_rank', self._slot_rank),
+                        ('slot_index', self._slot_index), ('lut', self._lut), ('masks', self._masks),
+                        ('seconds', self._seconds), ('slots', self._slots), ('owner', self._owner),
+                        ('last', self._last), ('scores', self._scores), ('ring', self._ring),
+                        ('ring_p', self._ring_p), ('hist_count', self._hist_count),
+                        ('hist_head', self._hist_head)):
+            setattr(s, name, addr(t))
+        self._struct = s
+
+    # host views of the device state (the reference exposes numpy arrays)
+    @property
+    def slots(self):
+        return self._slots.cpu().numpy().astype(np.int64)
+
+    @property
+    def owner(self):
+        return self._owner.cpu().numpy().astype(np.int64)
+
+    @property
+    def last(self):
+        return self._last.cpu().numpy()
+
+    @property
+    def scores(self):
+        return self._scores.cpu().numpy()
+
+    def plan_device(self, event, layer, ids, dest, *, tokens_per_rank=0, origins=None,
+                    gate_scores=None, prob_rows=None, stream=None):
+        """Asynchronous plan on `stream`: ids [n, k] uint8 (device), dest [n, k]
+        int32 (device, written).  Outputs stay in self._fetches/_n_fetches/
+        _counts/_err.  gate_scores None = use the device GateHistory."""
+        st = stream if stream is not None else stream_ptr(self.device)
+        call('ferryb_plan_layer', ctypes.byref(self._struct), int(event), int(layer), ptr(ids),
+             ids.shape[0], int(tokens_per_rank), ptr(origins), ptr(gate_scores), ptr(prob_rows),
+             0 if prob_rows is None else prob_rows.shape[0], ptr(self._fetches),
+             ptr(self._n_fetches), ptr(dest), ptr(self._counts), ptr(self._err), st)
+
+    def plan(self, event, layer, selected, origins, gate_scores):
+        """ferry/policy.py:225-228 -> (fetches [m, 3], destinations, counts), numpy int64."""
+        dev = self.device
+        sel = np.asarray(selected)
+        ids = torch.as_tensor(sel.astype(np.uint8), device=dev)
+        org = torch.as_tensor(np.asarray(origins, np.int64), device=dev)
+        gs = torch.as_tensor(np.asarray(gate_scores, np.float32), device=dev)
+        dest = torch.empty(ids.shape, dtype=torch.int32, device=dev)
+        self._err.zero_()
+        self.plan_device(event, layer, ids, dest, origins=org, gate_scores=gs)
+        _lib.check_device_error(self._err, 'plan')
+        n = int(self._n_fetches.item())
+        return (self._fetches[:n].cpu().numpy().astype(np.int64),
+                dest.cpu().numpy().astype(np.int64), self._counts.cpu().numpy().astype(np.int64))
+
+
+def plan_layer(event, layer, selected, origins, gate_scores, policy, slots, capacities, owner,
+               last, scores, quota_lut, masks, seconds, balance_tol_bps, salt):
+    """ferry/policy.py:130-194 on host arrays: uploads the state, plans on the
+    device, writes the state back in place, returns (fetches, destinations, counts)."""
+    from .quota import Topology
+    layers, experts = scores.shape
+    spec = _Spec(layers, experts, np.asarray(selected).shape[1])
+    ctl = Controller(spec, capacities, policy, Topology.from_arrays(masks, seconds, quota_lut),
+                     balance_tol_bps, salt)
+    dev = ctl.device
+    ctl._slots.copy_(torch.as_tensor(np.asarray(slots), device=dev).to(torch.int32))
+    ctl._owner.copy_(torch.as_tensor(np.asarray(owner), device=dev).to(torch.int32))
+    ctl._last.copy_(torch.as_tensor(np.asarray(last), device=dev))
+    ctl._scores.copy_(torch.as_tensor(np.asarray(scores), device=dev))
+    result = ctl.plan(event, layer, selected, origins, gate_scores)
+    slots[...] = ctl.slots
+    owner[...] = ctl.owner
+    last[...] = ctl.last
+    scores[...] = ctl.scores
+    return result

@@ -1,0 +1,125 @@
+"""Kernel 2 (device planner) and the device layout against the reference's
+own outputs (tests/golden/, from the reference's numba code).  Bit-exact:
+fetch lists, destinations, counts, cache state, gate scores, layouts."""
+import numpy as np
+import pytest
+import torch
+
+from tests.goldens import PLAN_CASES, PlanCase, load
+
+pytestmark = pytest.mark.gpu
+
+
+def _controller(c):
+    from ferry_b200.policy import Controller, _Spec
+    from ferry_b200.quota import Topology
+    topo = Topology.from_arrays(c.masks, c.seconds, c.lut)
+    score = 'probability' if c.step(0)['rows'].size else 'frequency'
+    return Controller(_Spec(c.layers, c.experts, c.topk), c.caps, c.policy, topo, c.bps, c.salt,
+                      window=c.window, score=score)
+
+
+@pytest.mark.parametrize('name', PLAN_CASES)
+def test_plan_with_host_scores(name):
+    """Controller.plan(event, layer, selected, origins, gate_scores) as the reference calls it."""
+    from ferry_b200.layout import build_layout
+    from ferry_b200.policy import layer_slots
+    c = PlanCase(name)
+    ctl = _controller(c)
+    for i in range(c.steps):
+        s = c.step(i)
+        if not s['ok']:
+            with pytest.raises(AssertionError):
+                ctl.plan(s['event'], s['layer'], s['selected'], c.origins(), s['scores'])
+            break
+        f, d, n = ctl.plan(s['event'], s['layer'], s['selected'], c.origins(), s['scores'])
+        np.testing.assert_array_equal(f, s['fetches'], err_msg=f'{name} step {i} fetches')
+        np.testing.assert_array_equal(d, s['dest'], err_msg=f'{name} step {i} destinations')
+        np.testing.assert_array_equal(n, s['counts'], err_msg=f'{name} step {i} counts')
+        if 'slots' in s:
+            np.testing.assert_array_equal(ctl.slots, s['slots'], err_msg=f'{name} step {i} slots')
+            np.testing.assert_array_equal(ctl.owner, s['owner'], err_msg=f'{name} step {i} owner')
+            np.testing.assert_array_equal(ctl.last, s['last'], err_msg=f'{name} step {i} last')
+        if i % 3 == 0 or i == c.steps - 1:  # layouts: every few steps keeps the test quick
+            slots = ctl.slots
+            for r in range(c.world):
+                lay = build_layout(s['selected'], d, c.tokens, r, c.experts)
+                exp = s['layout'][r]
+                for got, key in zip(lay, ('send_idx', 'send_ids', 'send_counts', 'recv_counts',
+                                          'starts', 'rows', 'cols')):
+                    np.testing.assert_array_equal(got, exp[key], err_msg=f'{name} {i} r{r} {key}')
+                np.testing.assert_array_equal(layer_slots(slots[r], c.caps[r], s['layer'], c.experts),
+                                              exp['layer_slots'])
+
+
+@pytest.mark.parametrize('name', [n for n in PLAN_CASES if n not in ('overflow', 'cfg0_caps5554')])
+def test_plan_with_device_history(name):
+    """The fused path: GateHistory update and scores computed on the device."""
+    c = PlanCase(name)
+    ctl = _controller(c)
+    dev = ctl.device
+    for i in range(c.steps):
+        s = c.step(i)
+        if not s['ok']:
+            break
+        ids = torch.as_tensor(s['selected'].astype(np.uint8), device=dev)
+        dest = torch.empty(ids.shape, dtype=torch.int32, device=dev)
+        prob = torch.as_tensor(s['rows'], device=dev) if s['rows'].size else None
+        ctl._err.zero_()
+        ctl.plan_device(s['event'], s['layer'], ids, dest, tokens_per_rank=c.tokens, prob_rows=prob)
+        torch.cuda.synchronize()
+        assert int(ctl._err.item()) == 0
+        np.testing.assert_array_equal(ctl.scores[s['layer']], s['scores'], err_msg=f'{name} {i} scores')
+        n = int(ctl._n_fetches.item())
+        np.testing.assert_array_equal(ctl._fetches[:n].cpu().numpy(), s['fetches'], err_msg=f'{name} {i}')
+        np.testing.assert_array_equal(dest.cpu().numpy(), s['dest'], err_msg=f'{name} {i} dest')
+
+
+def test_greedy_quota_and_build_lut():
+    from ferry_b200 import quota
+    d = load('quota')
+    for i in range(int(d['n'])):
+        args = (int(d[f'c{i}_m']), d[f'c{i}_cap'], d[f'c{i}_masks'], d[f'c{i}_seconds'])
+        if int(d[f'c{i}_ok']):
+            np.testing.assert_array_equal(quota.greedy_quota(*args), d[f'c{i}_quota'], err_msg=f'case {i}')
+        else:
+            with pytest.raises(AssertionError):
+                quota.greedy_quota(*args)
+    for key in d.files:
+        if key.startswith('lut') and not key.endswith(('_masks', '_seconds')):
+            world = d[key].shape[1]
+            np.testing.assert_array_equal(
+                quota.build_lut(64, world, d[key + '_masks'], d[key + '_seconds']), d[key], err_msg=key)
+
+
+def test_load_balanced_assignment():
+    from ferry_b200.policy import load_balanced_assignment
+    d = load('assignment')
+    for i in range(int(d['n'])):
+        got = load_balanced_assignment(d[f'c{i}_demand'], d[f'c{i}_misses'], d[f'c{i}_owner'],
+                                       int(d[f'c{i}_layer']), d[f'c{i}_quota'], int(d[f'c{i}_bps']))
+        np.testing.assert_array_equal(got, d[f'c{i}_ans'], err_msg=f'case {i}')
+
+
+def test_choose_slot():
+    from ferry_b200.policy import _choose_slot
+    d = load('choose_slot')
+    for i in range(int(d['n'])):
+        got = _choose_slot(int(d[f'c{i}_rank']), int(d[f'c{i}_layer']), d[f'c{i}_active'],
+                           d[f'c{i}_slots'], d[f'c{i}_caps'], d[f'c{i}_last'], d[f'c{i}_scores'],
+                           int(d[f'c{i}_experts']))
+        assert got == int(d[f'c{i}_slot']), f'case {i}'
+
+
+def test_demand_and_admission_capacity():
+    from oracle import planner as op
+    from ferry_b200.policy import _admission_capacity, _demand
+    c = PlanCase('qwen_r4')
+    s = c.step(0)
+    np.testing.assert_array_equal(_demand(s['selected'], c.origins(), c.experts, c.world),
+                                  op.demand(s['selected'], c.origins(), c.experts, c.world))
+    s5 = c.step(5)
+    active = op.demand(s5['selected'], c.origins(), c.experts, c.world).sum(1) > 0
+    np.testing.assert_array_equal(
+        _admission_capacity(s['slots'], c.caps, s5['layer'], active, c.experts),
+        op.admission_capacity(s['slots'], c.caps, s5['layer'], active, c.experts))
