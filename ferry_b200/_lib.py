@@ -32,7 +32,8 @@ class LayoutSummary(ctypes.Structure):
     """ferryb_layout_summary (include/ferryb.h)."""
     _fields_ = [(n, _i32c) for n in ('n_fetch_mine', 'n_hit', 'n_groups', 'n_recv', 'n_send',
                                       'n_routes', 'err', 'reserved')] + [
-        ('fetch_keys', _i32c * 256), ('fetch_slots', _i32c * 256)]
+        ('fetch_keys', _i32c * 256), ('fetch_slots', _i32c * 256),
+        ('send_counts', _i32c * 32), ('recv_counts', _i32c * 32), ('fetch_counts', _i32c * 32)]
 
 
 class LayoutArgs(ctypes.Structure):
@@ -42,6 +43,20 @@ class LayoutArgs(ctypes.Structure):
                     'fetches', 'n_fetches', 'layer_slot', 'send_idx', 'send_ids', 'send_counts',
                     'recv_counts', 'starts', 'rows', 'cols', 'n_send', 'n_recv', 'recv_token',
                     'csr_pos', 'peer_row', 'groups', 'summary', 'err')]
+
+
+class LayerConfig(ctypes.Structure):
+    """ferryb_layer_config (include/ferryb.h)."""
+    _fields_ = [(n, _i32c) for n in ('world', 'rank', 'tokens_per_rank', 'topk', 'experts', 'hidden',
+                                      'intermediate', 'router_mode', 'norm_topk')] + [
+        ('scaling', ctypes.c_float), ('probability_score', _i32c), ('timing', _i32c)]
+
+
+class LayerStats(ctypes.Structure):
+    """ferryb_layer_stats (include/ferryb.h)."""
+    _fields_ = [(n, _i64) for n in ('layers', 'fetches', 'routes', 'recv_rows', 'dispatch_bytes',
+                                     'combine_bytes')] + [
+        ('host_wait_us', _dbl), ('phase_us', _dbl * 5)]
 
 
 # name -> (restype, argtypes); every symbol declared in include/ferryb.h.
@@ -62,6 +77,34 @@ SIGNATURES = {
     'ferryb_choose_slot': (_i32, [_i32c, _i32c, _vp, _vp, _i32c, _vp, _vp, _vp, _i32c, _vp, _vp]),
     'ferryb_build_layout': (_i32, [ctypes.POINTER(LayoutArgs), _vp]),
     'ferryb_layer_slots': (_i32, [_vp, _i32c, _i32c, _i32c, _vp, _vp]),
+    'ferryb_h2d_create': (_i32, [_vp, _i64, _i64, _vp, _i64, _i32c, ctypes.POINTER(_vp)]),
+    'ferryb_h2d_fetch': (_i32, [_vp, _vp, _vp, _i64]),
+    'ferryb_h2d_wait_host': (_i32, [_vp, _vp, _i64]),
+    'ferryb_h2d_wait_device': (_i32, [_vp, _vp, _i64, _vp]),
+    'ferryb_h2d_mark_used': (_i32, [_vp, _vp, _i64, _vp]),
+    'ferryb_h2d_synchronize': (_i32, [_vp]),
+    'ferryb_h2d_copies': (_i64, [_vp]),
+    'ferryb_h2d_destroy': (_i32, [_vp]),
+    'ferryb_pack_dispatch': (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _vp, _vp,
+                                    _vp]),
+    'ferryb_unpack_dispatch': (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
+    'ferryb_segment_sum_workspace': (_i64, [_i64, _i64]),
+    'ferryb_reduce_partials': (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp]),
+    'ferryb_scatter_returned': (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp]),
+    'ferryb_symm_alloc': (_i32, [_i64, ctypes.POINTER(_vp), _vp]),
+    'ferryb_symm_open': (_i32, [_vp, ctypes.POINTER(_vp)]),
+    'ferryb_symm_close': (_i32, [_vp]),
+    'ferryb_symm_free': (_i32, [_vp]),
+    'ferryb_layer_workspace_bytes': (_i64, [ctypes.POINTER(LayerConfig)]),
+    'ferryb_layer_symm_bytes': (_i64, [ctypes.POINTER(LayerConfig), _i32c]),
+    'ferryb_layer_create': (_i32, [ctypes.POINTER(LayerConfig), ctypes.POINTER(Planner), _vp, _i64,
+                                   _vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_vp)]),
+    'ferryb_layer_forward': (_i32, [_vp, _i64, _i32c, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    'ferryb_layer_execute': (_i32, [_vp, _i64, _i32c, _vp, _vp, _vp, _vp, _i32c, _vp, _vp]),
+    'ferryb_layer_get_stats': (_i32, [_vp, ctypes.POINTER(LayerStats)]),
+    'ferryb_layer_reset_stats': (_i32, [_vp]),
+    'ferryb_layer_last_summary': (_i32, [_vp, ctypes.POINTER(LayoutSummary)]),
+    'ferryb_layer_destroy': (_i32, [_vp]),
 }
 
 _lib = None

@@ -240,6 +240,30 @@ __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait until flags[0..n) all reach `seq` (system-scope acquire), giving up
+// after `limit_ns` with DEV_WAIT_TIMEOUT in *err.  Called by one thread.
+__device__ __forceinline__ bool wait_flags_bounded(const uint64_t* flags, int n, uint64_t seq,
+                                                   int* err, uint64_t limit_ns = 2000000000ull) {
+  for (int i = 0; i < n; ++i) {
+    if (ld_acquire_sys(flags + i) >= seq) continue;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(flags + i) < seq) {
+      __nanosleep(64);
+      if (globaltimer_ns() - t0 > limit_ns) {
+        atomicCAS(err, 0, 1 /* DEV_WAIT_TIMEOUT */);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

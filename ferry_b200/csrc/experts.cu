@@ -33,6 +33,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "experts.cuh"
 
 namespace ferryb {
 
@@ -44,10 +45,6 @@ constexpr uint32_t kTileBytesA = kBlockM * kBlockK * 2;  // 16 KB
 constexpr uint32_t kTileBytesB = kMaxN * kBlockK * 2;    // 16 KB (max)
 constexpr uint64_t kWaitNs = 2000000000ull;               // 2 s bound on any wait
 
-// Tensor maps of the B operand for box heights 16, 32, 64, 128.
-struct BMaps {
-  CUtensorMap m[4];
-};
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -353,54 +350,69 @@ static int make_bmaps(BMaps* maps, const void* base, int64_t rows, int64_t cols)
   return FERRYB_OK;
 }
 
+int make_gemm_maps(GemmMaps* m, const void* cache, int64_t cache_slots, const void* x,
+                   const void* act, int64_t rows_cap, int64_t hidden, int64_t inter) {
+  FB_CHECK_ARG(hidden % kBlockM == 0 && inter % kBlockM == 0,
+               "hidden (%lld) and intermediate (%lld) must be multiples of 128",
+               (long long)hidden, (long long)inter);
+  int s;
+  if ((s = make_map_2d_bf16(&m->w1, cache, cache_slots * 3 * inter, hidden, hidden * 2, kBlockM,
+                            kBlockK)))
+    return s;
+  if ((s = make_map_2d_bf16(&m->w2, cache, cache_slots * 3 * hidden, inter, inter * 2, kBlockM,
+                            kBlockK)))
+    return s;
+  if ((s = make_bmaps(&m->bx, x, rows_cap, hidden))) return s;
+  if ((s = make_bmaps(&m->ba, act, rows_cap, inter))) return s;
+  m->hidden = hidden;
+  m->inter = inter;
+  return FERRYB_OK;
+}
+
+// Both phases over `groups` (device array of n_groups) with precomputed maps.
+int swiglu_grouped_maps(const GemmMaps& m, const GemmGroup* groups, int n_groups,
+                        const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
+                        int* err, cudaStream_t stream) {
+  if (n_groups == 0) return FERRYB_OK;
+  int device = 0;
+  FB_CUDA(cudaGetDevice(&device));
+  GemmParams p1{};
+  p1.groups = groups;
+  p1.n_groups = n_groups;
+  p1.m_tiles = static_cast<int>(m.inter / kBlockM);
+  p1.k_blocks = static_cast<int>(m.hidden / kBlockK);
+  p1.rows_per_slot = static_cast<int>(3 * m.inter);
+  p1.up_offset = static_cast<int>(m.inter);
+  p1.out_cols = static_cast<int>(m.inter);
+  p1.out = act;
+  p1.err = err;
+  int s;
+  if ((s = launch_phase(1, m.w1, m.bx, p1, device, stream))) return s;
+  GemmParams p2{};
+  p2.groups = groups;
+  p2.n_groups = n_groups;
+  p2.m_tiles = static_cast<int>(m.hidden / kBlockM);
+  p2.k_blocks = static_cast<int>(m.inter / kBlockK);
+  p2.rows_per_slot = static_cast<int>(3 * m.hidden);
+  p2.down_offset = static_cast<int>(2 * m.hidden);
+  p2.out_cols = static_cast<int>(m.hidden);
+  p2.out = out;
+  p2.route_w = route_w;
+  p2.err = err;
+  return launch_phase(2, m.w2, m.ba, p2, device, stream);
+}
+
 // Shared by the public entry points: run both phases over `groups` (device),
 // given X (routes already gathered), route weights, and scratch A.
 int swiglu_grouped(const void* cache, int64_t cache_slots, const GemmGroup* groups,
                    int n_groups, int64_t total_routes, const __nv_bfloat16* x,
                    const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
                    int64_t hidden, int64_t inter, int* err, cudaStream_t stream) {
-  FB_CHECK_ARG(hidden % kBlockM == 0 && inter % kBlockM == 0,
-               "hidden (%lld) and intermediate (%lld) must be multiples of 128",
-               (long long)hidden, (long long)inter);
   if (n_groups == 0 || total_routes == 0) return FERRYB_OK;
-  int device = 0;
-  FB_CUDA(cudaGetDevice(&device));
-  CUtensorMap w1, w2;
-  BMaps bx, ba;
-  int s;
-  if ((s = make_map_2d_bf16(&w1, cache, cache_slots * 3 * inter, hidden, hidden * 2, kBlockM,
-                            kBlockK)))
-    return s;
-  if ((s = make_map_2d_bf16(&w2, cache, cache_slots * 3 * hidden, inter, inter * 2, kBlockM,
-                            kBlockK)))
-    return s;
-  if ((s = make_bmaps(&bx, x, total_routes, hidden))) return s;
-  if ((s = make_bmaps(&ba, act, total_routes, inter))) return s;
-
-  GemmParams p1{};
-  p1.groups = groups;
-  p1.n_groups = n_groups;
-  p1.m_tiles = static_cast<int>(inter / kBlockM);
-  p1.k_blocks = static_cast<int>(hidden / kBlockK);
-  p1.rows_per_slot = static_cast<int>(3 * inter);
-  p1.up_offset = static_cast<int>(inter);
-  p1.out_cols = static_cast<int>(inter);
-  p1.out = act;
-  p1.err = err;
-  if ((s = launch_phase(1, w1, bx, p1, device, stream))) return s;
-
-  GemmParams p2{};
-  p2.groups = groups;
-  p2.n_groups = n_groups;
-  p2.m_tiles = static_cast<int>(hidden / kBlockM);
-  p2.k_blocks = static_cast<int>(inter / kBlockK);
-  p2.rows_per_slot = static_cast<int>(3 * hidden);
-  p2.down_offset = static_cast<int>(2 * hidden);
-  p2.out_cols = static_cast<int>(hidden);
-  p2.out = out;
-  p2.route_w = route_w;
-  p2.err = err;
-  return launch_phase(2, w2, ba, p2, device, stream);
+  GemmMaps m;
+  int s = make_gemm_maps(&m, cache, cache_slots, x, act, total_routes, hidden, inter);
+  if (s) return s;
+  return swiglu_grouped_maps(m, groups, n_groups, route_w, act, out, err, stream);
 }
 
 static int64_t align256(int64_t b) { return (b + 255) & ~int64_t(255); }

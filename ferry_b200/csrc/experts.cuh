@@ -1,0 +1,24 @@
+// experts.cuh -- host interface of the grouped SwiGLU GEMM (see experts.cu).
+#pragma once
+#include "common.cuh"
+
+namespace ferryb {
+
+// Tensor maps of the B operand for box heights 16, 32, 64, 128.
+struct BMaps {
+  CUtensorMap m[4];
+};
+
+struct GemmMaps {
+  CUtensorMap w1, w2;  // cache as [slots*3I, H] and [slots*3H, I]
+  BMaps bx, ba;        // X [rows_cap, H] and A [rows_cap, I]
+  int64_t hidden, inter;
+};
+
+int make_gemm_maps(GemmMaps* m, const void* cache, int64_t cache_slots, const void* x,
+                   const void* act, int64_t rows_cap, int64_t hidden, int64_t inter);
+int swiglu_grouped_maps(const GemmMaps& m, const GemmGroup* groups, int n_groups,
+                        const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
+                        int* err, cudaStream_t stream);
+
+}  // namespace ferryb

@@ -1,0 +1,477 @@
+// layer.cu -- the per-MoE-layer executor: one call runs FERRY's whole layer
+// hot path on this rank (replaces OffloadRuntime.execute, ferry/runtime.py:64-89).
+//
+// Per layer, on the compute stream:
+//   1  router (kernel 1): top-k, ids + histogram into every rank's gather buffer
+//   2  planner (kernel 2): waits for all ranks' metadata, plans (replicated,
+//      bit-exact), updates the device GateHistory and cache state
+//   3  layer_slots + layout: this rank's packets, receive rows, expert CSR,
+//      GEMM groups and a ~2 KB summary (fetch list, counts)
+//   4  summary -> pinned host memory; the host waits for it (the only host
+//      synchronisation of the layer; the reference has three)
+//   5  this rank's fetches on the copy-engine streams (kernel 3)
+//   6  dispatch (kernel 4): packets into the owners' receive buffers, flags
+//   7  permute: routed rows into expert order (after all sources' flags)
+//   8  grouped SwiGLU (kernel 5) over the experts cached before the layer,
+//      then one launch per fetched expert gated by that slot's copy event
+//      (the GEMM of an expert starts when its own bytes have landed)
+//   9  combine + final scatter (kernel 4), output [T, H]
+// The host returns after enqueueing step 9; the next layer's steps 1-3 queue
+// behind it.  A layer's copies start only after its summary is on the host,
+// which follows every earlier compute on the stream, so a cache slot is never
+// overwritten while an earlier layer still reads it.
+#include <chrono>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "experts.cuh"
+#include "layout.cuh"
+#include "planner.cuh"
+#include "router.cuh"
+#include "transport.cuh"
+
+namespace ferryb {
+int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
+                const PlanOutputs& out, cudaStream_t stream);
+}
+
+using namespace ferryb;
+
+struct ferryb_layer {
+  ferryb_layer_config cfg{};
+  ferryb_planner planner{};
+  PlanConfig pc{};
+  PlanState ps{};
+  void* cache = nullptr;
+  int64_t cache_slots = 0;
+  ferryb_h2d* h2d = nullptr;
+  uint8_t* symm = nullptr;
+  uintptr_t* peer_base_dev = nullptr;  // inside the workspace
+  SymLayout sl{};
+  int prob_tail = 0;
+  // workspace carve-up
+  int32_t *dest, *fetches, *n_fetches, *counts, *errs, *layer_slot;
+  int64_t *send_idx, *send_ids, *send_counts, *recv_counts, *starts, *rows, *cols;
+  int32_t *n_send, *n_recv, *recv_token, *csr_pos, *peer_row;
+  GemmGroup* groups;
+  ferryb_layout_summary* summary_dev;
+  __nv_bfloat16 *x_sorted, *act, *expert_out, *route_w, *weights;
+  int64_t* selected;
+  int* hist_local;
+  unsigned* done;
+  // host side
+  ferryb_layout_summary* summary_host = nullptr;
+  int32_t* errs_host = nullptr;  // pinned copy of the device error words
+  cudaEvent_t summary_ev = nullptr;
+  cudaEvent_t tev[8] = {};
+  GemmMaps maps{};
+  ferryb_layer_stats stats{};
+};
+
+namespace {
+
+int64_t a256(int64_t b) { return (b + 255) & ~int64_t(255); }
+
+struct Carve {
+  int64_t off = 0;
+  uint8_t* base = nullptr;
+  template <class T>
+  T* take(int64_t count) {
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += a256(count * (int64_t)sizeof(T));
+    return p;
+  }
+};
+
+int prob_tail_rows(const ferryb_layer_config& c, int window) {
+  if (!c.probability_score) return 0;
+  const int tail = (window + c.world - 1) / c.world;
+  return tail < c.tokens_per_rank ? tail : c.tokens_per_rank;
+}
+
+SymLayout layout_of(const ferryb_layer_config& c, int window) {
+  SymLayout l = sym_layout(c.world, c.tokens_per_rank, c.topk, c.hidden, c.experts);
+  // probability-score tails follow the base layout
+  const int tail = prob_tail_rows(c, window);
+  l.half = a256(l.half) + a256((int64_t)c.world * tail * c.experts * 4);
+  return l;
+}
+
+size_t prob_offset(const ferryb_layer_config& c) {
+  return a256(sym_layout(c.world, c.tokens_per_rank, c.topk, c.hidden, c.experts).half);
+}
+
+template <class F>
+int64_t carve_all(const ferryb_layer_config& c, uint8_t* base, F&& assign) {
+  Carve cv;
+  cv.base = base;
+  const int64_t R = c.world, T = c.tokens_per_rank, K = c.topk, E = c.experts, H = c.hidden,
+                I = c.intermediate;
+  const int64_t n_tok = R * T, routes = n_tok * K;
+  assign(cv, R, T, K, E, H, I, n_tok, routes);
+  return cv.off;
+}
+
+}  // namespace
+
+static int check_config(const ferryb_layer_config* c) {
+  FB_CHECK_ARG(c && c->world >= 1 && c->world <= 32 && c->rank >= 0 && c->rank < c->world,
+               "layer: bad world/rank");
+  FB_CHECK_ARG(c->tokens_per_rank >= 1 && c->topk >= 1 && c->topk <= 16 && c->experts >= c->topk &&
+                   c->experts <= 256,
+               "layer: bad tokens/topk/experts");
+  FB_CHECK_ARG(c->hidden % 256 == 0 && c->intermediate % 128 == 0,
+               "layer: hidden must be a multiple of 256 and intermediate of 128");
+  FB_CHECK_ARG(c->router_mode >= 0 && c->router_mode <= 1, "layer: router_mode must be 0 or 1");
+  return FERRYB_OK;
+}
+
+static int64_t workspace_bytes(const ferryb_layer_config& c, uint8_t* base, ferryb_layer* L) {
+  return carve_all(c, base, [&](Carve& cv, int64_t R, int64_t T, int64_t K, int64_t E, int64_t H,
+                                int64_t I, int64_t n_tok, int64_t routes) {
+    auto dest = cv.take<int32_t>(n_tok * K);
+    auto fetches = cv.take<int32_t>(E * 3);
+    auto n_fetches = cv.take<int32_t>(1);
+    auto counts = cv.take<int32_t>(R);
+    auto errs = cv.take<int32_t>(8);
+    auto layer_slot = cv.take<int32_t>(E);
+    auto send_idx = cv.take<int64_t>(T * R);
+    auto send_ids = cv.take<int64_t>(T * R * K);
+    auto send_counts = cv.take<int64_t>(R);
+    auto recv_counts = cv.take<int64_t>(R);
+    auto starts = cv.take<int64_t>(E + 1);
+    auto rows = cv.take<int64_t>(routes);
+    auto cols = cv.take<int64_t>(routes);
+    auto n_send = cv.take<int32_t>(1);
+    auto n_recv = cv.take<int32_t>(1);
+    auto recv_token = cv.take<int32_t>(n_tok);
+    auto csr_pos = cv.take<int32_t>(n_tok * K);
+    auto peer_row = cv.take<int32_t>(T * R);
+    auto groups = cv.take<GemmGroup>(E);
+    auto summary = cv.take<ferryb_layout_summary>(1);
+    auto x_sorted = cv.take<__nv_bfloat16>(routes * H);
+    auto act = cv.take<__nv_bfloat16>(routes * I);
+    auto expert_out = cv.take<__nv_bfloat16>(routes * H);
+    auto route_w = cv.take<__nv_bfloat16>(routes);
+    auto weights = cv.take<__nv_bfloat16>(T * K);
+    auto selected = cv.take<int64_t>(T * K);
+    auto hist_local = cv.take<int>(E);
+    auto done = cv.take<unsigned>(1);
+    auto peer_base = cv.take<uintptr_t>(R);
+    if (L) {
+      L->dest = dest; L->fetches = fetches; L->n_fetches = n_fetches; L->counts = counts;
+      L->errs = errs; L->layer_slot = layer_slot; L->send_idx = send_idx; L->send_ids = send_ids;
+      L->send_counts = send_counts; L->recv_counts = recv_counts; L->starts = starts;
+      L->rows = rows; L->cols = cols; L->n_send = n_send; L->n_recv = n_recv;
+      L->recv_token = recv_token; L->csr_pos = csr_pos; L->peer_row = peer_row;
+      L->groups = groups; L->summary_dev = summary; L->x_sorted = x_sorted; L->act = act;
+      L->expert_out = expert_out; L->route_w = route_w; L->weights = weights;
+      L->selected = selected; L->hist_local = hist_local; L->done = done;
+      L->peer_base_dev = peer_base;
+    }
+  });
+}
+
+extern "C" int64_t ferryb_layer_workspace_bytes(const ferryb_layer_config* cfg) {
+  if (check_config(cfg)) return -1;
+  return workspace_bytes(*cfg, nullptr, nullptr);
+}
+
+extern "C" int64_t ferryb_layer_symm_bytes(const ferryb_layer_config* cfg, int32_t window) {
+  if (check_config(cfg)) return -1;
+  return (int64_t)layout_of(*cfg, window).half * 2;
+}
+
+extern "C" int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_planner* planner,
+                                   void* cache, int64_t cache_slots, ferryb_h2d* h2d,
+                                   void* symm_local, const uint64_t* peer_bases, void* workspace,
+                                   int64_t workspace_size, ferryb_layer** out) {
+  int s = check_config(cfg);
+  if (s) return s;
+  FB_CHECK_ARG(planner && cache && h2d && symm_local && peer_bases && workspace && out,
+               "layer_create: null argument");
+  FB_CHECK_ARG(planner->world == cfg->world && planner->experts == cfg->experts &&
+                   planner->topk == cfg->topk,
+               "layer_create: planner and layer disagree on world/experts/topk");
+  FB_CHECK_ARG(planner->capacities != nullptr, "planner not initialised");
+  FB_CHECK_ARG(workspace_size >= workspace_bytes(*cfg, nullptr, nullptr),
+               "layer_create: workspace too small");
+  FB_CHECK_ARG((cfg->probability_score != 0) == (planner->ring_p != nullptr),
+               "layer_create: probability score needs the planner's probability ring");
+  auto* L = new ferryb_layer();
+  L->cfg = *cfg;
+  L->planner = *planner;
+  L->cache = cache;
+  L->cache_slots = cache_slots;
+  L->h2d = h2d;
+  L->symm = static_cast<uint8_t*>(symm_local);
+  L->sl = layout_of(*cfg, planner->window);
+  L->prob_tail = prob_tail_rows(*cfg, planner->window);
+  workspace_bytes(*cfg, static_cast<uint8_t*>(workspace), L);
+  // planner config (same derivation as ferryb_plan_layer)
+  PlanConfig& c = L->pc;
+  c.world = planner->world; c.experts = planner->experts; c.layers = planner->layers;
+  c.topk = planner->topk; c.window = planner->window; c.policy = planner->policy;
+  c.bps = planner->balance_tol_bps; c.salt = planner->salt; c.maxcap = planner->maxcap;
+  c.total_slots = planner->total_slots; c.n_domains = planner->n_domains;
+  c.lut_rows = planner->lut_rows; c.capacities = planner->capacities;
+  c.slot_rank = planner->slot_rank; c.slot_index = planner->slot_index; c.lut = planner->lut;
+  c.masks = planner->masks; c.seconds = planner->seconds;
+  c.dyn_smem = plan_dyn_smem(c.experts, c.world, c.total_slots, c.n_domains, &c.sort_offset,
+                             &c.greedy_offset, &c.sort_n);
+  L->ps = PlanState{planner->slots, planner->owner, planner->last, planner->scores,
+                    planner->ring, planner->ring_p, planner->hist_count, planner->hist_head};
+  FB_CUDA(cudaMemset(workspace, 0, (size_t)workspace_size));
+  FB_CUDA(cudaMemcpy(L->peer_base_dev, peer_bases, sizeof(uint64_t) * cfg->world,
+                     cudaMemcpyHostToDevice));
+  FB_CUDA(cudaHostAlloc(&L->summary_host, sizeof(ferryb_layout_summary), cudaHostAllocDefault));
+  FB_CUDA(cudaHostAlloc(&L->errs_host, 8 * sizeof(int32_t), cudaHostAllocDefault));
+  FB_CUDA(cudaEventCreateWithFlags(&L->summary_ev, cudaEventDisableTiming));
+  for (auto& e : L->tev) FB_CUDA(cudaEventCreate(&e));
+  const int64_t routes = (int64_t)cfg->world * cfg->tokens_per_rank * cfg->topk;
+  s = make_gemm_maps(&L->maps, cache, cache_slots, L->x_sorted, L->act, routes, cfg->hidden,
+                     cfg->intermediate);
+  if (s) { delete L; return s; }
+  *out = L;
+  return FERRYB_OK;
+}
+
+static FusedArgs fused_args(ferryb_layer* L, int parity, const __nv_bfloat16* hidden,
+                            __nv_bfloat16* out) {
+  const ferryb_layer_config& c = L->cfg;
+  FusedArgs a{};
+  a.world = c.world; a.rank = c.rank; a.tokens_per_rank = c.tokens_per_rank; a.topk = c.topk;
+  a.hdim = c.hidden; a.experts = c.experts; a.parity = parity;
+  a.peer_base = L->peer_base_dev;
+  a.local_base = L->symm;
+  a.buf_stride = L->sl.half;
+  a.off_recv_x = L->sl.recv_x; a.off_recv_w = L->sl.recv_w; a.off_recv_ids = L->sl.recv_ids;
+  a.off_ret = L->sl.ret; a.off_dflag = L->sl.dflag; a.off_cflag = L->sl.cflag;
+  a.hidden = hidden;
+  a.weights = L->weights;
+  a.ids = L->symm + parity * L->sl.half + L->sl.gather_ids;
+  a.dest = L->dest;
+  a.peer_row = L->peer_row;
+  a.rows = L->rows;
+  a.cols = L->cols;
+  a.n_routes_dev = &L->summary_dev->n_routes;
+  a.n_recv_dev = L->n_recv;
+  a.recv_token = L->recv_token;
+  a.csr_pos = L->csr_pos;
+  a.x_sorted = L->x_sorted;
+  a.route_w = L->route_w;
+  a.expert_out = L->expert_out;
+  a.out = out;
+  a.err = L->errs + 3;
+  return a;
+}
+
+static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const void* hidden,
+                         const void* gate_weight, const float* gate_bias,
+                         const int64_t* given_selected, const void* given_weights,
+                         const float* given_probs, int32_t n_given_probs, void* out,
+                         int64_t* selected_out, void* weights_out, cudaStream_t stream) {
+  const ferryb_layer_config& c = L->cfg;
+  FB_CHECK_ARG(layer >= 0 && layer < L->planner.layers, "layer %d out of range", layer);
+  FB_CHECK_ARG(event >= 0 && event < ((int64_t)1 << 39), "event out of range");
+  const int parity = (int)(event & 1);
+  const uint64_t seq = (uint64_t)event + 1;
+  const bool timing = c.timing != 0;
+  uint8_t* half = L->symm + parity * L->sl.half;
+  if (timing) FB_CUDA(cudaEventRecord(L->tev[0], stream));
+
+  // 1 router + all-gather
+  RouterArgs ra{};
+  ra.world = c.world; ra.rank = c.rank; ra.tokens_per_rank = c.tokens_per_rank; ra.topk = c.topk;
+  ra.hdim = c.hidden; ra.experts = c.experts; ra.parity = parity;
+  ra.mode = given_selected ? 2 : c.router_mode;
+  ra.norm_topk = c.norm_topk; ra.scaling = c.scaling;
+  ra.hidden = static_cast<const __nv_bfloat16*>(hidden);
+  ra.gate = static_cast<const __nv_bfloat16*>(gate_weight);
+  ra.bias = gate_bias;
+  ra.weights = L->weights;
+  ra.selected = L->selected;
+  ra.hist_local = L->hist_local;
+  ra.done = L->done;
+  ra.given_selected = given_selected;
+  ra.given_weights = static_cast<const __nv_bfloat16*>(given_weights);
+  ra.given_probs = given_probs;
+  ra.n_given_probs = n_given_probs;
+  ra.prob_tail = L->prob_tail;
+  ra.peer_base = L->peer_base_dev;
+  ra.buf_stride = L->sl.half;
+  ra.off_ids = L->sl.gather_ids;
+  ra.off_hist = L->sl.gather_hist;
+  ra.off_flag = L->sl.gflag;
+  ra.off_prob = prob_offset(c);
+  int s = router_launch(ra, seq, stream);
+  if (s) return s;
+
+  // 2 planner
+  PlanInputs in{};
+  in.ids = half + L->sl.gather_ids;
+  in.n_tokens = c.world * c.tokens_per_rank;
+  in.tokens_per_rank = c.tokens_per_rank;
+  in.prob_rows = L->prob_tail ? reinterpret_cast<const float*>(half + prob_offset(c)) : nullptr;
+  in.n_prob_rows = c.world * L->prob_tail;
+  in.event = event;
+  in.layer = layer;
+  in.gflags = c.world > 1 ? reinterpret_cast<const uint64_t*>(half + L->sl.gflag) : nullptr;
+  in.seq = seq;
+  in.hist = reinterpret_cast<const int*>(half + L->sl.gather_hist);
+  PlanOutputs po{L->fetches, L->n_fetches, L->dest, L->counts, L->errs + 0};
+  if ((s = plan_launch(L->pc, L->ps, in, po, stream))) return s;
+
+  // 3 layer slots + layout
+  // slots past a rank's capacity are never filled, so scanning maxcap is exact
+  if ((s = layer_slots_launch(L->planner.slots + (size_t)c.rank * L->planner.maxcap,
+                              L->planner.maxcap, layer, c.experts, L->layer_slot, stream)))
+    return s;
+  ferryb_layout_args la{};
+  la.ids = in.ids; la.dest = L->dest;
+  la.world = c.world; la.tokens_per_rank = c.tokens_per_rank; la.topk = c.topk;
+  la.experts = c.experts; la.rank = c.rank;
+  la.fetches = L->fetches; la.n_fetches = L->n_fetches; la.layer_slot = L->layer_slot;
+  la.send_idx = L->send_idx; la.send_ids = L->send_ids; la.send_counts = L->send_counts;
+  la.recv_counts = L->recv_counts; la.starts = L->starts; la.rows = L->rows; la.cols = L->cols;
+  la.n_send = L->n_send; la.n_recv = L->n_recv; la.recv_token = L->recv_token;
+  la.csr_pos = L->csr_pos; la.peer_row = L->peer_row; la.groups = L->groups;
+  la.summary = L->summary_dev; la.err = L->errs + 1;
+  if ((s = layout_launch(la, stream))) return s;
+  if (timing) FB_CUDA(cudaEventRecord(L->tev[1], stream));
+
+  // 4 summary to the host
+  FB_CUDA(cudaMemcpyAsync(L->summary_host, L->summary_dev, sizeof(ferryb_layout_summary),
+                          cudaMemcpyDeviceToHost, stream));
+  FB_CUDA(cudaMemcpyAsync(L->errs_host, L->errs, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                          stream));
+  FB_CUDA(cudaEventRecord(L->summary_ev, stream));
+  const auto t0 = std::chrono::steady_clock::now();
+  FB_CUDA(cudaEventSynchronize(L->summary_ev));
+  L->stats.host_wait_us +=
+      std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
+  const ferryb_layout_summary sum = *L->summary_host;
+  // error words: [0] planner, [1] layout, [2] GEMM, [3] transport (earlier layers)
+  const int plan_err = L->errs_host[0];
+  if (sum.err || plan_err || L->errs_host[2] || L->errs_host[3]) {
+    if (L->errs_host[2] || L->errs_host[3])
+      return fail(FERRYB_EDEVICE, "device error in an earlier layer (GEMM %d, transport %d)",
+                  L->errs_host[2], L->errs_host[3]);
+    if (plan_err == DEV_CAPACITY || sum.err == DEV_CAPACITY)
+      return fail(FERRYB_ECAPACITY, "missing experts exceed the total admission capacity");
+    if (plan_err == DEV_WAIT_TIMEOUT)
+      return fail(FERRYB_ETIMEOUT, "timed out waiting for the routing metadata of a peer rank");
+    return fail(FERRYB_EDEVICE, "planner/layout device error %d/%d", plan_err, sum.err);
+  }
+  // 5 fetches (copy engines)
+  std::vector<int64_t> fslots(sum.n_fetch_mine), fkeys(sum.n_fetch_mine);
+  for (int i = 0; i < sum.n_fetch_mine; ++i) {
+    fslots[i] = sum.fetch_slots[i];
+    fkeys[i] = sum.fetch_keys[i];
+  }
+  if (sum.n_fetch_mine) {
+    if ((s = ferryb_h2d_fetch(L->h2d, fslots.data(), fkeys.data(), sum.n_fetch_mine))) return s;
+  }
+
+  // 6-7 dispatch + permute
+  const FusedArgs fa = fused_args(L, parity, static_cast<const __nv_bfloat16*>(hidden),
+                                  static_cast<__nv_bfloat16*>(out));
+  if ((s = fused_dispatch(fa, seq, stream))) return s;
+  if ((s = fused_permute(fa, seq, sum.n_routes, stream))) return s;
+  if (timing) FB_CUDA(cudaEventRecord(L->tev[2], stream));
+
+  // 8 grouped SwiGLU: cached experts, then each fetched expert after its copy
+  if ((s = swiglu_grouped_maps(L->maps, L->groups, sum.n_hit, L->route_w, L->act,
+                               L->expert_out, L->errs + 2, stream)))
+    return s;
+  if (timing) FB_CUDA(cudaEventRecord(L->tev[3], stream));
+  for (int i = 0; i < sum.n_fetch_mine; ++i) {
+    if ((s = ferryb_h2d_wait_device(L->h2d, &fslots[i], 1, stream))) return s;
+    if ((s = swiglu_grouped_maps(L->maps, L->groups + sum.n_hit + i, 1, L->route_w, L->act,
+                                 L->expert_out, L->errs + 2, stream)))
+      return s;
+  }
+  if (timing) FB_CUDA(cudaEventRecord(L->tev[4], stream));
+
+  // 9 combine
+  if ((s = fused_combine(fa, seq, sum.n_recv, stream))) return s;
+  if (timing) FB_CUDA(cudaEventRecord(L->tev[5], stream));
+
+  if (selected_out)
+    FB_CUDA(cudaMemcpyAsync(selected_out, L->selected, sizeof(int64_t) * c.tokens_per_rank * c.topk,
+                            cudaMemcpyDeviceToDevice, stream));
+  if (weights_out)
+    FB_CUDA(cudaMemcpyAsync(weights_out, L->weights, 2 * (size_t)c.tokens_per_rank * c.topk,
+                            cudaMemcpyDeviceToDevice, stream));
+
+  // counters (the reference's fetches_per_rank, copies, dispatch/combine bytes)
+  L->stats.layers += 1;
+  L->stats.fetches += sum.n_fetch_mine;
+  L->stats.routes += sum.n_routes;
+  L->stats.recv_rows += sum.n_recv;
+  int64_t sent_remote = 0, recv_remote = 0;
+  for (int p = 0; p < c.world && p < 32; ++p) {
+    if (p == c.rank) continue;
+    sent_remote += sum.send_counts[p];
+    recv_remote += sum.recv_counts[p];
+  }
+  L->stats.dispatch_bytes += sent_remote * (2 * (int64_t)c.hidden + 3 * c.topk);
+  L->stats.combine_bytes += recv_remote * 2 * (int64_t)c.hidden;
+  if (timing) {
+    FB_CUDA(cudaEventSynchronize(L->tev[5]));
+    float ms[5];
+    for (int i = 0; i < 5; ++i) FB_CUDA(cudaEventElapsedTime(&ms[i], L->tev[i], L->tev[i + 1]));
+    for (int i = 0; i < 5; ++i) L->stats.phase_us[i] += ms[i] * 1000.0;
+  }
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_layer_forward(ferryb_layer* L, int64_t event, int32_t layer,
+                                    const void* hidden, const void* gate_weight,
+                                    const float* gate_bias, void* out, int64_t* selected_out,
+                                    void* weights_out, cudaStream_t stream) {
+  FB_CHECK_ARG(L && hidden && gate_weight && out, "layer_forward: null argument");
+  return layer_forward(L, event, layer, hidden, gate_weight, gate_bias, nullptr, nullptr, nullptr,
+                       0, out, selected_out, weights_out, stream);
+}
+
+extern "C" int ferryb_layer_execute(ferryb_layer* L, int64_t event, int32_t layer,
+                                    const void* hidden, const int64_t* selected,
+                                    const void* weights, const float* probs_tail,
+                                    int32_t n_probs_tail, void* out, cudaStream_t stream) {
+  FB_CHECK_ARG(L && hidden && selected && weights && out, "layer_execute: null argument");
+  FB_CHECK_ARG(!L->prob_tail || (probs_tail && n_probs_tail >= L->prob_tail),
+               "layer_execute: probability score needs probs_tail rows");
+  return layer_forward(L, event, layer, hidden, nullptr, nullptr, selected, weights, probs_tail,
+                       n_probs_tail, out, nullptr, nullptr, stream);
+}
+
+extern "C" int ferryb_layer_get_stats(const ferryb_layer* L, ferryb_layer_stats* out) {
+  FB_CHECK_ARG(L && out, "layer_get_stats: null argument");
+  *out = L->stats;
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_layer_last_summary(const ferryb_layer* L, ferryb_layout_summary* out) {
+  FB_CHECK_ARG(L && out && L->summary_host, "layer_last_summary: null argument");
+  *out = *L->summary_host;
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_layer_reset_stats(ferryb_layer* L) {
+  FB_CHECK_ARG(L, "layer_reset_stats: null argument");
+  L->stats = ferryb_layer_stats{};
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_layer_destroy(ferryb_layer* L) {
+  if (!L) return FERRYB_OK;
+  if (L->summary_host) cudaFreeHost(L->summary_host);
+  if (L->errs_host) cudaFreeHost(L->errs_host);
+  if (L->summary_ev) cudaEventDestroy(L->summary_ev);
+  for (auto e : L->tev)
+    if (e) cudaEventDestroy(e);
+  delete L;
+  return FERRYB_OK;
+}

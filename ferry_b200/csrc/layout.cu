@@ -67,11 +67,15 @@ __device__ int block_scan(int v, int* warp_sum, int* total) {
 // Sorted ids of token g's routes that go to `peer` (ascending, insertion sort
 // as in ferry/layout.py:27-33).  Returns the count.
 __device__ __forceinline__ int packet_ids(const uint8_t* ids, const int32_t* dest, int g, int K,
-                                          int peer, int* out) {
+                                          int peer, int* out, int E, int* err) {
   int size = 0;
   for (int j = 0; j < K; ++j) {
     if (dest[g * K + j] == peer) {
       const int e = ids[g * K + j];
+      if (e >= E) {  // never index per-expert tables with an invalid id
+        atomicCAS(err, 0, DEV_BAD_INPUT);
+        continue;
+      }
       int pos = size;
       while (pos > 0 && out[pos - 1] > e) { out[pos] = out[pos - 1]; --pos; }
       out[pos] = e;
@@ -118,7 +122,7 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
       const int t = t0 + tid;
       const int g = rank * T + t;
       int size = 0;
-      if (t < T) size = packet_ids(a.ids, a.dest, g, K, peer, ids_buf);
+      if (t < T) size = packet_ids(a.ids, a.dest, g, K, peer, ids_buf, E, a.err);
       const int has = size > 0;
       const int pos = sent + block_scan(has, sm.warp_sum, &total_sh);
       if (has) {
@@ -156,7 +160,7 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
   for (int g0 = 0; g0 < n_tok; g0 += kChunk) {
     const int g = g0 + tid;
     int size = 0;
-    if (g < n_tok) size = packet_ids(a.ids, a.dest, g, K, rank, ids_buf);
+    if (g < n_tok) size = packet_ids(a.ids, a.dest, g, K, rank, ids_buf, E, a.err);
     const int has = size > 0;
     const int row = received + block_scan(has, sm.warp_sum, &total_sh);
     if (has) {
@@ -196,7 +200,7 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
     __syncthreads();
     const int g = g0 + tid;
     int size = 0;
-    if (g < n_tok) size = packet_ids(a.ids, a.dest, g, K, rank, ids_buf);
+    if (g < n_tok) size = packet_ids(a.ids, a.dest, g, K, rank, ids_buf, E, a.err);
     for (int j = 0; j < size; ++j) atomicOr(&sm.mask[ids_buf[j]][tid >> 5], 1u << (tid & 31));
     const int has = size > 0;
     const int row = row_base + block_scan(has, sm.warp_sum, &total_sh);
@@ -253,6 +257,16 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
       const int cnt = sm.starts[e + 1] - sm.starts[e];
       if (cnt > 0 && (a.layer_slot == nullptr || a.layer_slot[e] < 0) && sm.fetched_rank[e] < 0)
         atomicCAS(a.err, 0, DEV_NO_SLOT);  // scheduled here but not cached (ferry/layout.py:91)
+    }
+    for (int p = 0; p < 32; ++p) {
+      a.summary->send_counts[p] = p < R ? (int)a.send_counts[p] : 0;
+      a.summary->recv_counts[p] = p < R ? (int)a.recv_counts[p] : 0;
+      a.summary->fetch_counts[p] = 0;
+    }
+    const int nf_all = a.n_fetches ? *a.n_fetches : 0;
+    for (int i = 0; i < nf_all; ++i) {
+      const int r = a.fetches[i * 3 + 0];
+      if (r >= 0 && r < 32) a.summary->fetch_counts[r] += 1;
     }
     a.summary->err = *a.err;
   }

@@ -313,9 +313,18 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   SlotRec* recs = reinterpret_cast<SlotRec*>(dsm + c.sort_offset);       // [sort_n]
   int64_t* greedy_load = reinterpret_cast<int64_t*>(dsm + c.greedy_offset);  // [G]
 
-  if (tid == 0) { sm.status = 0; sm.m = 0; }
+  if (tid == 0) {
+    sm.status = 0;
+    sm.m = 0;
+    // fused path: wait (bounded) until every rank's routing metadata landed
+    if (in.gflags && !wait_flags_bounded(in.gflags, R, in.seq, out.err)) sm.status = DEV_WAIT_TIMEOUT;
+  }
   for (int i = tid; i < E * R; i += blockDim.x) demand[i] = 0;
   __syncthreads();
+  if (sm.status) {
+    if (tid == 0) *out.n_fetches = 0;
+    return;
+  }
 
   // -- gate scores: given, or from the device GateHistory -------------------
   if (in.gate_scores) {
@@ -327,7 +336,9 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   for (int e = tid; e < E; e += blockDim.x) s.scores[(size_t)L * E + e] = sm.gate[e];
 
   // -- Step 1: demand d[e, r] ----------------------------------------------
-  for (int i = tid; i < n_tok * K; i += blockDim.x) {
+  if (in.hist) {
+    for (int i = tid; i < E * R; i += blockDim.x) demand[(i % E) * R + i / E] = in.hist[i];
+  } else for (int i = tid; i < n_tok * K; i += blockDim.x) {
     const int t = i / K;
     const int e = in.ids[i];
     const int r = in.origins ? (int)in.origins[t] : t / in.tokens_per_rank;

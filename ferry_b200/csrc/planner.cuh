@@ -44,6 +44,10 @@ struct PlanInputs {
   int n_prob_rows;
   int64_t event;
   int layer;
+  // fused path: gathered metadata from the router kernel (optional)
+  const uint64_t* gflags;  // [world] gather flags to wait for (>= seq)
+  uint64_t seq;
+  const int* hist;         // [world, experts] per-rank demand histograms
 };
 
 struct PlanOutputs {

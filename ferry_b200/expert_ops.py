@@ -4,6 +4,8 @@ and error behaviour (RuntimeError on bad input), backed by libferryb's sm_100a
 kernels through the C ABI.  Outputs are allocated by the torch caching
 allocator; inputs are borrowed.
 """
+import ctypes
+
 import torch
 
 from . import _lib
@@ -48,3 +50,136 @@ def execute_experts(cache, input, routing_weights, slots, rows, cols, hidden, in
              ptr(rows_c), ptr(cols_c), hidden, intermediate, ptr(out), ptr(ws), ws_bytes,
              stream_ptr(input.device))
     return list(out.split(sizes)) if sizes else []
+
+
+def pack_dispatch(hidden, selected, weights, send_idx, send_ids, experts):
+    """ferry/csrc/expert_ops.cpp:50-66 -> uint8 [n, 2H + 3k] packets."""
+    require_cuda(hidden, selected, weights, send_idx, send_ids)
+    _check(hidden.dtype == BF16 and weights.dtype == BF16, 'hidden and weights must be bf16')
+    n, h, k = send_idx.shape[0], hidden.shape[1], send_ids.shape[1]
+    payload = torch.empty((n, 2 * h + 3 * k), dtype=torch.uint8, device=hidden.device)
+    if n:
+        hid = hidden.contiguous()
+        sel = selected.contiguous().long()
+        w = weights.contiguous()
+        si, sids = send_idx.contiguous().long(), send_ids.contiguous().long()
+        err = torch.zeros(1, dtype=torch.int32, device=hidden.device)
+        _check(sel.shape[1] == k, 'selected and send_ids must have the same top-k width')
+        call('ferryb_pack_dispatch', ptr(hid), hid.shape[0], h, ptr(sel), ptr(w), k, ptr(si),
+             ptr(sids), n, experts, ptr(payload), ptr(err), stream_ptr(hidden.device))
+        _lib.check_device_error(err, 'pack_dispatch')
+    return payload
+
+
+def unpack_dispatch(raw, hidden, topk):
+    """ferry/csrc/expert_ops.cpp:68-73 -> (x [m, H] bf16, w [m, k] bf16)."""
+    require_cuda(raw)
+    m = raw.shape[0]
+    x = torch.empty((m, hidden), dtype=BF16, device=raw.device)
+    w = torch.empty((m, topk), dtype=BF16, device=raw.device)
+    if m:
+        r = raw.contiguous()
+        call('ferryb_unpack_dispatch', ptr(r), m, hidden, topk, ptr(x), ptr(w), stream_ptr(raw.device))
+    return x, w
+
+
+def _segment_sum(src, keys, n_keys, hidden, name):
+    out = torch.empty((n_keys, hidden), dtype=BF16, device=src.device)
+    n = src.shape[0]
+    ws_bytes = _lib.lib().ferryb_segment_sum_workspace(n, n_keys)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=src.device)
+    s, k = src.contiguous(), keys.contiguous().long()
+    call(name, ptr(s), ptr(k), n, n_keys, hidden, ptr(out), ptr(ws), ws_bytes, stream_ptr(src.device))
+    return out
+
+
+def reduce_partials(parts, rows, received, hidden, like):
+    """ferry/csrc/expert_ops.cpp:76-83: float32 sum of the groups' outputs per
+    receive row (in group order), returned as bf16 [received, hidden]."""
+    require_cuda(like)
+    if not parts:
+        return torch.zeros((received, hidden), dtype=BF16, device=like.device)
+    src = torch.cat([p.to(BF16) for p in parts])
+    keys = torch.cat([r.reshape(-1) for r in rows])
+    if src.shape[0] == 0:
+        return torch.zeros((received, hidden), dtype=BF16, device=like.device)
+    out = torch.empty((received, hidden), dtype=BF16, device=like.device)
+    ws_bytes = _lib.lib().ferryb_segment_sum_workspace(src.shape[0], received)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=like.device)
+    call('ferryb_reduce_partials', ptr(src), ptr(keys.long()), src.shape[0], received, hidden,
+         ptr(out), ptr(ws), ws_bytes, stream_ptr(like.device))
+    return out
+
+
+def scatter_returned(returned, send_idx, tokens):
+    """ferry/csrc/expert_ops.cpp:86-92: float32 sum of returned partials per
+    token (in packet order), bf16 [tokens, hidden]."""
+    require_cuda(returned, send_idx)
+    hidden = returned.shape[1]
+    if returned.shape[0] == 0:
+        return torch.zeros((tokens, hidden), dtype=returned.dtype, device=returned.device)
+    out = torch.empty((tokens, hidden), dtype=BF16, device=returned.device)
+    ret = returned.contiguous().to(BF16)
+    idx = send_idx.contiguous().long()
+    ws_bytes = _lib.lib().ferryb_segment_sum_workspace(ret.shape[0], tokens)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=returned.device)
+    call('ferryb_scatter_returned', ptr(ret), ptr(idx), ret.shape[0], tokens, hidden, ptr(out),
+         ptr(ws), ws_bytes, stream_ptr(returned.device))
+    return out.to(returned.dtype)
+
+
+class H2DEngine:
+    """ferry/csrc/expert_ops.cpp:97-142: pinned-pool -> cache-slot copies on
+    copy-engine streams, per-slot events, last-use ordering."""
+
+    def __init__(self, cache, pool, n_streams=1):
+        require_cuda(cache)
+        _check(pool.is_pinned() and pool.shape[1] == cache.shape[1],
+               'pool must be pinned with the cache row size')
+        self.cache, self.pool = cache, pool
+        h = ctypes.c_void_p()
+        call('ferryb_h2d_create', ptr(cache), cache.shape[0], cache.shape[1] * cache.element_size(),
+             ptr(pool), pool.shape[0], int(n_streams), ctypes.byref(h))
+        self._h = h
+
+    def _arr(self, values):
+        return _lib.host_i64(values), len(values)
+
+    def fetch(self, slots, keys):
+        s, n = self._arr(slots)
+        k, _ = self._arr(keys)
+        call('ferryb_h2d_fetch', self._h, s, k, n)
+
+    def wait_host(self, slots):
+        s, n = self._arr(slots)
+        call('ferryb_h2d_wait_host', self._h, s, n)
+
+    def wait_device(self, slots):
+        s, n = self._arr(slots)
+        call('ferryb_h2d_wait_device', self._h, s, n, stream_ptr(self.cache.device))
+
+    def mark_used(self, slots):
+        s, n = self._arr(slots)
+        call('ferryb_h2d_mark_used', self._h, s, n, stream_ptr(self.cache.device))
+
+    def synchronize(self):
+        call('ferryb_h2d_synchronize', self._h)
+
+    @property
+    def copies(self):
+        return int(_lib.lib().ferryb_h2d_copies(self._h))
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if self._h:
+            _lib.lib().ferryb_h2d_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

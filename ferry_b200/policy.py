@@ -63,10 +63,13 @@ def load_balanced_assignment(demand, misses, owner, layer, quota, balance_tol_bp
     experts, world = demand.shape
     m = len(misses)
     ans = torch.zeros(max(m, 1), dtype=torch.int64, device=dev)
-    call('ferryb_load_balanced_assignment', ptr(_t(demand, torch.int64, dev)), experts, world,
-         ptr(_t(np.asarray(misses, np.int64).reshape(-1) if m else np.zeros(1, np.int64), torch.int64, dev)),
-         m, ptr(_t(owner, torch.int32, dev)), layer, ptr(_t(quota, torch.int64, dev)),
-         int(balance_tol_bps), ptr(ans), stream_ptr(dev))
+    # keep every argument tensor referenced until the kernel has run
+    d_t = _t(demand, torch.int64, dev)
+    m_t = _t(np.asarray(misses, np.int64).reshape(-1) if m else np.zeros(1, np.int64), torch.int64, dev)
+    o_t = _t(owner, torch.int32, dev)
+    q_t = _t(quota, torch.int64, dev)
+    call('ferryb_load_balanced_assignment', ptr(d_t), experts, world, ptr(m_t), m, ptr(o_t), layer,
+         ptr(q_t), int(balance_tol_bps), ptr(ans), stream_ptr(dev))
     return ans[:m].cpu().numpy()
 
 
@@ -75,10 +78,13 @@ def _choose_slot(rank, layer, active, slots, capacities, last, scores, experts):
     dev = _dev()
     slots = np.asarray(slots)
     res = torch.zeros(1, dtype=torch.int64, device=dev)
-    call('ferryb_choose_slot', rank, layer, ptr(_t(np.asarray(active, np.uint8), torch.uint8, dev)),
-         ptr(_t(slots, torch.int32, dev)), slots.shape[1], ptr(_t(capacities, torch.int32, dev)),
-         ptr(_t(last, torch.int64, dev)), ptr(_t(scores, torch.float32, dev)), experts, ptr(res),
-         stream_ptr(dev))
+    a_t = _t(np.asarray(active, np.uint8), torch.uint8, dev)
+    s_t = _t(slots, torch.int32, dev)
+    c_t = _t(capacities, torch.int32, dev)
+    l_t = _t(last, torch.int64, dev)
+    sc_t = _t(scores, torch.float32, dev)
+    call('ferryb_choose_slot', rank, layer, ptr(a_t), ptr(s_t), slots.shape[1], ptr(c_t), ptr(l_t),
+         ptr(sc_t), experts, ptr(res), stream_ptr(dev))
     return int(res.item())
 
 
@@ -132,6 +138,19 @@ class Controller:
         self.reset()
 
     def reset(self):
+        """Empty cache state and history.  The device arrays keep their
+        addresses (an executor built on this controller stays valid)."""
+        if getattr(self, '_struct', None) is not None:
+            self._slots.fill_(-1)
+            self._owner.fill_(-1)
+            self._last.zero_()
+            self._scores.zero_()
+            self._ring.zero_()
+            if self._ring_p is not None:
+                self._ring_p.zero_()
+            self._hist_count.zero_()
+            self._hist_head.zero_()
+            return
         dev, L, E, W, K = self.device, self.spec.layers, self.spec.experts, self.window, self.topk
         self._slots = torch.full((self.world, self.maxcap), -1, dtype=torch.int32, device=dev)
         self._owner = torch.full((L * E,), -1, dtype=torch.int32, device=dev)

@@ -176,6 +176,9 @@ typedef struct ferryb_layout_summary {
   int32_t n_fetch_mine, n_hit, n_groups, n_recv, n_send, n_routes, err, reserved;
   int32_t fetch_keys[256];  /* this rank's fetches, in fetch order */
   int32_t fetch_slots[256];
+  int32_t send_counts[32];  /* packets this rank sends to each peer */
+  int32_t recv_counts[32];  /* packets this rank receives from each peer */
+  int32_t fetch_counts[32]; /* fetches of every rank this layer (the planner's counts) */
 } ferryb_layout_summary;
 
 typedef struct ferryb_layout_args {
@@ -208,6 +211,128 @@ FERRYB_API int ferryb_build_layout(const ferryb_layout_args* args, ferryb_stream
  * `layer` in slots_row[0:capacity], else -1.  Device pointers. */
 FERRYB_API int ferryb_layer_slots(const int32_t* slots_row, int32_t capacity, int32_t layer,
                                   int32_t experts, int32_t* lookup, ferryb_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Kernel 3: expert fetch from pinned host memory into HBM cache slots on
+ * copy-engine streams.  Replaces H2DEngine (ferry/csrc/expert_ops.cpp:97-142):
+ * fetch (:107-117), wait_host (:119-122), mark_used (:124-128),
+ * synchronize (:130-133), copies (:135).  Adds wait_device (a compute stream
+ * waits for given slots' copies without blocking the host).  Slot and key
+ * arrays are host arrays.  A pool with fewer rows than keys is read
+ * cyclically (row = key mod pool_rows).
+ */
+typedef struct ferryb_h2d ferryb_h2d;
+FERRYB_API int ferryb_h2d_create(void* cache, int64_t cache_slots, int64_t row_bytes,
+                                 const void* pool, int64_t pool_rows, int32_t n_streams,
+                                 ferryb_h2d** out);
+FERRYB_API int ferryb_h2d_fetch(ferryb_h2d* h2d, const int64_t* slots, const int64_t* keys,
+                                int64_t n);
+FERRYB_API int ferryb_h2d_wait_host(ferryb_h2d* h2d, const int64_t* slots, int64_t n);
+FERRYB_API int ferryb_h2d_wait_device(ferryb_h2d* h2d, const int64_t* slots, int64_t n,
+                                      ferryb_stream_t stream);
+FERRYB_API int ferryb_h2d_mark_used(ferryb_h2d* h2d, const int64_t* slots, int64_t n,
+                                    ferryb_stream_t stream);
+FERRYB_API int ferryb_h2d_synchronize(ferryb_h2d* h2d);
+FERRYB_API int64_t ferryb_h2d_copies(const ferryb_h2d* h2d);
+FERRYB_API int ferryb_h2d_destroy(ferryb_h2d* h2d);
+
+/* ------------------------------------------------------------------------
+ * Kernel 4 (reference-compatible ops): packets and partial sums.
+ * pack_dispatch (ferry/csrc/expert_ops.cpp:50-66): payload [n_packets,
+ *   2*hidden + 3*topk] bytes = hidden bf16 | routing weights bf16 (one per
+ *   packet id, 0 for -1 padding) | ids u8.
+ * unpack_dispatch (:68-73): x [m, hidden] bf16, w [m, topk] bf16.
+ * reduce_partials (:76-83): partial[r] = bf16(sum over parts rows with
+ *   rows[p] == r, in part order, in float32).
+ * scatter_returned (:86-92): out[t] = bf16(sum of returned rows with
+ *   send_idx[p] == t, in packet order, in float32).
+ * The two sums synchronise `stream` to report out-of-range indices.
+ */
+FERRYB_API int ferryb_pack_dispatch(const void* hidden, int64_t tokens, int64_t hidden_dim,
+                                    const int64_t* selected, const void* weights, int64_t topk,
+                                    const int64_t* send_idx, const int64_t* send_ids,
+                                    int64_t n_packets, int64_t experts, void* payload,
+                                    int32_t* err, ferryb_stream_t stream);
+FERRYB_API int ferryb_unpack_dispatch(const void* raw, int64_t m, int64_t hidden_dim,
+                                      int64_t topk, void* x, void* w, ferryb_stream_t stream);
+FERRYB_API int64_t ferryb_segment_sum_workspace(int64_t n, int64_t n_keys);
+FERRYB_API int ferryb_reduce_partials(const void* parts, const int64_t* rows, int64_t total,
+                                      int64_t received, int64_t hidden_dim, void* partial,
+                                      void* workspace, int64_t workspace_bytes,
+                                      ferryb_stream_t stream);
+FERRYB_API int ferryb_scatter_returned(const void* returned, const int64_t* send_idx, int64_t n,
+                                       int64_t tokens, int64_t hidden_dim, void* out,
+                                       void* workspace, int64_t workspace_bytes,
+                                       ferryb_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Symmetric device buffers for the P2P transport: ferryb_symm_alloc
+ * allocates (cudaMalloc, zeroed) and exports a 64-byte CUDA IPC handle
+ * (handle_out NULL: no export, single rank); peers map it with ferryb_symm_open.  Replaces the process-group plumbing of the
+ * reference's all-to-all (ferry/transport.py:17-20).
+ */
+FERRYB_API int ferryb_symm_alloc(int64_t bytes, void** ptr, void* handle_out);
+FERRYB_API int ferryb_symm_open(const void* handle, void** ptr);
+FERRYB_API int ferryb_symm_close(void* peer_ptr);
+FERRYB_API int ferryb_symm_free(void* ptr);
+
+/* ------------------------------------------------------------------------
+ * The fused per-layer executor.  Replaces OffloadRuntime.execute
+ * (ferry/runtime.py:64-89) together with the MoE hook's router
+ * (ferry/model.py:137-148).  One call runs, on this rank: router + all-gather
+ * (kernel 1), planner (kernel 2), layout, one host wait for the ~2 KB plan
+ * summary, this rank's fetches (kernel 3), P2P dispatch (kernel 4), the
+ * grouped SwiGLU (kernel 5, cached experts first, then each fetched expert as
+ * soon as its copy lands) and the combine (kernel 4).  The workspace and the
+ * symmetric buffer are caller-allocated (sizes from the *_bytes queries); the
+ * executor allocates only a pinned host summary and CUDA events.
+ */
+typedef struct ferryb_layer_config {
+  int32_t world, rank, tokens_per_rank, topk, experts, hidden, intermediate;
+  int32_t router_mode;       /* 0: Qwen3 (bf16 logits), 1: DeepSeek-V2 (float32 logits) */
+  int32_t norm_topk;         /* Qwen3 norm_topk_prob */
+  float scaling;             /* DeepSeek-V2 routed_scaling_factor */
+  int32_t probability_score; /* eviction score 'probability' (ferry/metadata.py:59-60) */
+  int32_t timing;            /* record per-phase CUDA-event times (synchronises each layer) */
+} ferryb_layer_config;
+
+typedef struct ferryb_layer_stats {
+  int64_t layers, fetches, routes, recv_rows, dispatch_bytes, combine_bytes;
+  double host_wait_us; /* host time blocked on the plan summary */
+  double phase_us[5];  /* timing mode: route+plan+layout, summary+dispatch+permute,
+                          cached-expert GEMM, fetched-expert GEMMs (incl. copy waits),
+                          combine */
+} ferryb_layer_stats;
+
+typedef struct ferryb_layer ferryb_layer;
+FERRYB_API int64_t ferryb_layer_workspace_bytes(const ferryb_layer_config* cfg);
+FERRYB_API int64_t ferryb_layer_symm_bytes(const ferryb_layer_config* cfg, int32_t window);
+/* peer_bases: host [world] device addresses of every rank's symmetric buffer
+ * as mapped in this process (its own at index rank). */
+FERRYB_API int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_planner* planner,
+                                   void* cache, int64_t cache_slots, ferryb_h2d* h2d,
+                                   void* symm_local, const uint64_t* peer_bases, void* workspace,
+                                   int64_t workspace_bytes, ferryb_layer** out);
+/* Router in the loop: hidden [T, H] bf16, gate_weight [E, H] bf16, gate_bias
+ * [E] float32 or NULL; out [T, H] bf16; optional selected_out [T, K] int64
+ * and weights_out [T, K] bf16. `event` counts layer invocations from 0 and
+ * must advance identically on every rank. */
+FERRYB_API int ferryb_layer_forward(ferryb_layer* layer, int64_t event, int32_t moe_layer,
+                                    const void* hidden, const void* gate_weight,
+                                    const float* gate_bias, void* out, int64_t* selected_out,
+                                    void* weights_out, ferryb_stream_t stream);
+/* Reference signature (ferry/runtime.py:64): routing given by the caller:
+ * selected [T, K] int64, weights [T, K] bf16, probs_tail [n, E] float32
+ * (probability score only, else NULL). */
+FERRYB_API int ferryb_layer_execute(ferryb_layer* layer, int64_t event, int32_t moe_layer,
+                                    const void* hidden, const int64_t* selected,
+                                    const void* weights, const float* probs_tail,
+                                    int32_t n_probs_tail, void* out, ferryb_stream_t stream);
+FERRYB_API int ferryb_layer_get_stats(const ferryb_layer* layer, ferryb_layer_stats* out);
+/* The plan summary of the last layer run (fetch list, per-rank counts). */
+FERRYB_API int ferryb_layer_last_summary(const ferryb_layer* layer, ferryb_layout_summary* out);
+FERRYB_API int ferryb_layer_reset_stats(ferryb_layer* layer);
+FERRYB_API int ferryb_layer_destroy(ferryb_layer* layer);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,118 @@
+"""The fused per-layer executor (kernels 1-5 chained by ferryb_layer_*) on one
+GPU against the CPU oracle of the reference's OffloadRuntime.execute:
+cache decisions bit-exact, layer outputs within the BF16 tolerance."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import expert_ops as ref_ops
+from oracle.layer import OracleRuntime
+from tests.tolerance import assert_bf16_close
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device('cuda', 0)
+
+
+def _spec(layers, experts, topk, hidden, inter, kind='qwen3_moe'):
+    from ferry_b200.model import ModelSpec
+    return ModelSpec(kind, tuple(range(layers)), experts, topk, hidden, inter)
+
+
+def _setup(spec, caps, seed=0, policy='ferry', score='frequency'):
+    from ferry_b200.quota import Topology
+    from ferry_b200.runtime import OffloadRuntime
+    from ferry_b200.workload import cpu_pool, zipf_bias
+    torch.manual_seed(seed)
+    pool = cpu_pool(spec, spec.layers, seed).pin_memory()
+    topo = Topology.uniform(len(caps), spec.experts)
+    rt = OffloadRuntime(spec, pool, caps, policy, topo, eviction_score=score)
+    orc = OracleRuntime(spec, pool, caps, policy, topo.masks, topo.seconds, topo.lut, score=score)
+    g = torch.Generator().manual_seed(seed + 7)
+    gates = [(torch.randn(spec.experts, spec.hidden, generator=g) * 0.02).to(torch.bfloat16)
+             for _ in range(spec.layers)]
+    biases = [zipf_bias(spec.experts, 1.1, g) for _ in range(spec.layers)]
+    return rt, orc, gates, biases, g
+
+
+CASES = [
+    # layers, experts, topk, hidden, inter, tokens, capacity
+    (3, 16, 4, 256, 128, 8, 10),
+    (2, 128, 8, 2048, 768, 64, 180),     # Qwen3 layer shape, decode batch 64
+    (2, 64, 6, 2048, 1408, 16, 60),      # DeepSeek-V2-Lite layer shape
+]
+
+
+@pytest.mark.parametrize('case', CASES, ids=lambda c: f'E{c[1]}_k{c[2]}_H{c[3]}_T{c[5]}')
+def test_execute_matches_oracle(case):
+    layers, E, K, H, I, T, cap = case
+    spec = _spec(layers, E, K, H, I)
+    rt, orc, gates, biases, g = _setup(spec, [cap])
+    for step in range(3 * layers):
+        layer = step % layers
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        sel, w, _ = ref_ops.route_qwen3(x, gates[layer], K, True, biases[layer])
+        want, fetches, dest = orc.execute(layer, [x], [sel], [w])
+        got = rt.execute(layer, x.to(DEV), sel.to(DEV), w.to(DEV), None)
+        torch.cuda.synchronize()
+        assert_bf16_close(got.cpu(), want[0], f'step {step}')
+        np.testing.assert_array_equal(rt.controller.slots, orc.ctl.slots, err_msg=f'step {step}')
+        np.testing.assert_array_equal(rt.controller.owner, orc.ctl.owner)
+        np.testing.assert_array_equal(rt.controller.last, orc.ctl.last)
+    np.testing.assert_array_equal(rt.fetches_per_rank, orc.fetches_per_rank)
+    assert rt.h2d.copies == int(orc.fetches_per_rank[0])
+    rt.close()
+
+
+def test_forward_router_and_layer():
+    """Kernel 1 in the loop: routing against a torch GPU router, then the layer
+    output against the oracle fed the kernel's own routing."""
+    layers, E, K, H, I, T, cap = CASES[1]
+    spec = _spec(layers, E, K, H, I)
+    rt, orc, gates, biases, g = _setup(spec, [cap], seed=3)
+    n_mismatch = 0
+    for step in range(4):
+        layer = step % layers
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        sel_out = torch.empty((T, K), dtype=torch.int64, device=DEV)
+        w_out = torch.empty((T, K), dtype=torch.bfloat16, device=DEV)
+        got = rt.forward(layer, x.to(DEV), gates[layer].to(DEV), biases[layer].to(DEV), sel_out, w_out)
+        torch.cuda.synchronize()
+        # torch reference of the hook's router on the same GPU (cuBLAS bf16 logits)
+        logits = torch.nn.functional.linear(x.to(DEV), gates[layer].to(DEV),
+                                            biases[layer].to(DEV).to(torch.bfloat16))
+        probs = torch.softmax(logits.float(), -1)
+        ref_w, ref_sel = torch.topk(probs, K, -1)
+        ref_w = ref_w / ref_w.sum(-1, keepdim=True)
+        # same expert sets except where probabilities tie within rounding
+        for t in range(T):
+            a, b = set(sel_out[t].tolist()), set(ref_sel[t].tolist())
+            if a != b:
+                n_mismatch += 1
+                kth = probs[t].sort(descending=True).values
+                assert (kth[K - 1] - kth[K]).abs().item() < 1e-3, f'token {t}: {a} vs {b}'
+        same = (sel_out.sort(-1).values == ref_sel.sort(-1).values).all(-1)
+        assert_bf16_close(w_out[same].float().sort(-1).values.cpu(),
+                          ref_w[same].float().sort(-1).values.cpu(), 'router weights')
+        want, _, _ = orc.execute(layer, [x], [sel_out.cpu()], [w_out.cpu()])
+        assert_bf16_close(got.cpu(), want[0], f'forward step {step}')
+        np.testing.assert_array_equal(rt.controller.slots, orc.ctl.slots)
+    assert n_mismatch <= T  # near-ties only
+    rt.close()
+
+
+def test_reset_and_counters():
+    layers, E, K, H, I, T, cap = CASES[0]
+    spec = _spec(layers, E, K, H, I)
+    rt, orc, gates, biases, g = _setup(spec, [cap], seed=5)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    sel, w, _ = ref_ops.route_qwen3(x, gates[0], K, True, biases[0])
+    rt.execute(0, x.to(DEV), sel.to(DEV), w.to(DEV), None)
+    assert rt.event == 1 and rt.h2d.copies > 0
+    rt.reset()
+    assert rt.event == 0 and rt.h2d.copies == 0
+    assert (rt.controller.slots == -1).all()
+    got = rt.execute(0, x.to(DEV), sel.to(DEV), w.to(DEV), None)
+    want, _, _ = orc.execute(0, [x], [sel], [w])
+    assert_bf16_close(got.cpu(), want[0], 'after reset')
+    rt.close()
