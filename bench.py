@@ -1,0 +1,433 @@
+#!/usr/bin/env python
+"""Decode throughput of FERRY's per-MoE-layer hot path on B200.
+
+Workload (multi-GPU: config 4's scaling): Qwen3-30B-A3B
+MoE layers (hidden 2048, 128 experts top-8 with renormalised softmax,
+moe_intermediate 768, SwiGLU, bf16, random init N(0, 0.02)) stacked as the
+model's 48 MoE layers, decode batch of 64 tokens per GPU, Zipf(1.1) router
+bias and step-to-step hidden-state correlation rho = 0.5, expert cache = the
+reference's global 30 % budget (floor(0.3 * 48 * 128) = 1843 slots split over
+the GPUs), every expert resident in pinned host memory.  A lone 38-slot layer
+cannot be planned by the reference (~45 experts are active per step and its
+greedy quota asserts), so config 1's 38/128 is read as the per-layer share of
+the 30 % cache of the 48-layer stack.
+
+One step = one decode step through the 48 MoE layers (attention is not part
+of the hot path): layer l routes h_l = x_l + out_{l-1} (a residual
+dependency, so a layer cannot start before the previous one ends), and every
+layer runs FERRY's full path: router + metadata all-gather, planner, layout,
+copy-engine expert fetches, dispatch, grouped SwiGLU GEMM, combine.
+
+value    = tokens decoded per second by the whole job (R * 64 * K / max-over-
+           ranks time of K steps), inputs resident in HBM.
+e2e      = the same through the public API with each step's inputs copied from
+           pinned host memory and the step's output read back.
+--impl reference times the reference's CPU path (the oracle port of
+           ferry's planner/layout + the torch-CPU restatement of expert_ops)
+           on this host's cores, on a bounded sample of layers per step.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+METRIC = 'decode tokens/s through the 48-layer Qwen3-30B-A3B MoE stack (box, max over ranks)'
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=10)
+    p.add_argument('--warmup', type=int, default=3)
+    p.add_argument('--impl', default='ferry_b200', choices=['ferry_b200', 'reference'])
+    p.add_argument('--layers', type=int, default=48)
+    p.add_argument('--tokens', type=int, default=64)
+    p.add_argument('--cache-ratio', type=float, default=0.3)
+    p.add_argument('--pool-layers', type=int, default=0, help='0 = as many as host RAM allows')
+    p.add_argument('--policy', default='ferry', choices=['ferry', 'random'])
+    p.add_argument('--copy-streams', type=int, default=1)
+    p.add_argument('--no-e2e', action='store_true')
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--cpu-seconds', type=float, default=12.0)
+    return p.parse_args()
+
+
+def init_dist(n_gpus):
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group('nccl', device_id=torch.device('cuda', local),
+                                timeout=timedelta(seconds=180))
+    return rank, world, local
+
+
+def max_over_ranks(x, world):
+    t = torch.tensor([x], dtype=torch.float64, device='cuda')
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self):
+        self.rows, self.proc, self.thread = [], None, None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(',')])
+
+    def stop(self, gpu_indices):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for r in self.rows:
+            try:
+                if int(r[0]) not in gpu_indices:
+                    continue
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                for name, v in zip(names, r[5:9]):
+                    if v.lower() == 'active':
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': max(mx), 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+def measured_peaks():
+    path = ROOT / 'MEASURED_PEAKS.json'
+    if path.exists():
+        d = json.loads(path.read_text())
+        return d.get('hbm_gbs', 6650.0), d.get('bf16_tflops_sustained', 1400.0), 'measured'
+    return 6650.0, 1400.0, 'fallback'
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = ROOT / 'profiles' / 'gemm_traffic.json'
+    if path.exists():
+        try:
+            return json.loads(path.read_text())
+        except ValueError:
+            return None
+    return None
+
+
+def host_link_gbs(cache_row, pool, n=12):
+    """Pinned host -> HBM bandwidth of expert-sized copies on a copy stream."""
+    s = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        for i in range(4):
+            cache_row[i % cache_row.shape[0]].copy_(pool[i % pool.shape[0]], non_blocking=True)
+    s.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for i in range(n):
+            cache_row[i % cache_row.shape[0]].copy_(pool[(i * 7) % pool.shape[0]], non_blocking=True)
+        e1.record(s)
+    e1.synchronize()
+    return n * pool[0].numel() * 2 / (e0.elapsed_time(e1) / 1e3) / 1e9
+
+
+def auto_pool_layers(spec, world, requested):
+    if requested:
+        return min(requested, spec.layers)
+    per_layer = spec.experts * spec.expert_bytes
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except ImportError:
+        avail = 64 << 30
+    fit = int(avail * 0.55 // (per_layer * world))
+    return max(1, min(spec.layers, fit))
+
+
+def qwen3_spec(layers):
+    from ferry_b200.model import QWEN3_30B_A3B, spec_from_config
+    c = dict(QWEN3_30B_A3B)
+    c['num_hidden_layers'] = layers
+    return spec_from_config(c)
+
+
+# ---------------------------------------------------------------------------
+def run_ours(a, rank, world, local):
+    from ferry_b200.quota import Topology
+    from ferry_b200.runtime import OffloadRuntime
+    from ferry_b200.workload import SyntheticMoE
+    dev = torch.device('cuda', local)
+    spec = qwen3_spec(a.layers)
+    T, L = a.tokens, spec.layers
+    caps = spec.cache_slots(a.cache_ratio, world)
+    pool_layers = auto_pool_layers(spec, world, a.pool_layers)
+    t0 = time.time()
+    wl = SyntheticMoE(spec, seed=0, device=dev, pool_layers=pool_layers)
+    setup_s = time.time() - t0
+    topo = Topology.uniform(world, spec.experts)
+    rt = OffloadRuntime(spec, wl.pool, caps, a.policy, topo, n_copy_streams=a.copy_streams,
+                        timing=True)
+    b_host = host_link_gbs(rt.cache, wl.pool)
+    stream = wl.hidden_stream(T, seed=1, world=world, rank=rank)
+    n_steps = a.warmup + a.steps
+    inputs = [torch.stack([stream.next(l) for l in range(L)]) for _ in range(n_steps)]
+
+    def step(inp):
+        prev = None
+        for l in range(L):
+            h = inp[l] if prev is None else inp[l] + prev
+            prev = rt.forward(l, h, wl.gate[l], wl.bias[l])
+        return prev
+
+    for i in range(a.warmup):
+        step(inputs[i])
+    torch.cuda.synchronize()
+    ex = rt._executor(T)
+    from ferry_b200._lib import call
+    call('ferryb_layer_collect_timing', ex.h)
+    call('ferryb_layer_reset_stats', ex.h)
+    copies0 = rt.h2d.copies
+    barrier(world)
+    sampler = ClockSampler() if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(a.steps):
+        step(inputs[a.warmup + i])
+    ev1.record()
+    ev1.synchronize()
+    barrier(world)
+    clocks = sampler.stop([local]) if sampler else None
+    ms_local = ev0.elapsed_time(ev1)
+    call('ferryb_layer_collect_timing', ex.h)
+    st = ex.stats()
+    fetch_copies = rt.h2d.copies - copies0
+    ms = max_over_ranks(ms_local, world)
+
+    # e2e: inputs from pinned host memory each step, output read back each step
+    e2e = None
+    if not a.no_e2e:
+        host_inputs = [x.cpu().pin_memory() for x in inputs[a.warmup:]]
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(a.steps):
+            inp = host_inputs[i].to(dev, non_blocking=True)
+            out = step(inp)
+            out.cpu()
+        e1.record()
+        e1.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+        e2e = {'value': world * T * a.steps / (e2e_ms / 1e3), 'unit': 'tokens/s',
+               'h2d_bytes_per_step': int(host_inputs[0].numel() * 2),
+               'd2h_bytes_per_step': int(T * spec.hidden * 2), 'ms_per_step': e2e_ms / a.steps}
+
+    hbm_gbs, bf16_tflops, peak_kind = measured_peaks()
+    layers_timed = max(1, st.timed_layers)
+    # dominant kernel: the grouped SwiGLU over cached experts (HBM-bound at decode)
+    gemm_us = st.phase_us[2]
+    achieved = st.hit_weight_bytes / (gemm_us * 1e-6) / 1e9 if gemm_us > 0 else 0.0
+    traffic = ncu_traffic()
+    roofline = {'kernel': 'swiglu_gemm_kernel (cached experts, both phases)', 'bound': 'hbm',
+                'achieved': round(achieved, 1), 'peak': hbm_gbs, 'unit': 'GB/s',
+                'frac': round(achieved / hbm_gbs, 4), 'peak_source': peak_kind,
+                'algorithmic_bytes_per_layer': st.hit_weight_bytes / layers_timed,
+                'traffic': traffic.get('dram_bytes_per_expert') if traffic else None,
+                'traffic_note': traffic.get('note') if traffic else 'no ncu capture committed'}
+    # per-layer roofline: slowest of host-link fetch, NVLink exchange, tensor FLOPs
+    expert_bytes = spec.expert_bytes
+    fetch_bytes = st.fetches * expert_bytes
+    nvl_bytes = st.dispatch_bytes + st.combine_bytes
+    flops = st.routes * 6 * spec.hidden * spec.intermediate
+    t_host = fetch_bytes / (b_host * 1e9)
+    t_nvl = nvl_bytes / 770e9
+    t_flops = flops / (bf16_tflops * 1e12)
+    t_roof = max(t_host, t_nvl, t_flops)
+    t_meas = ms_local / 1e3
+    layer_roofline = {'bound': ['host_link', 'nvlink', 'tensor'][int(np.argmax([t_host, t_nvl, t_flops]))],
+                      'frac': round(t_roof / t_meas, 4) if t_meas > 0 else None,
+                      'host_link_gbs_measured': round(b_host, 2),
+                      'fetch_gbs_achieved': round(fetch_bytes / t_meas / 1e9, 2),
+                      'fetches_per_layer': st.fetches / max(1, st.layers),
+                      'nvlink_bytes_per_layer': nvl_bytes / max(1, st.layers),
+                      'rank': rank}
+    split = {name: round(st.phase_us[i] / layers_timed, 1) for i, name in enumerate(
+        ['route_plan_layout', 'summary_dispatch_permute', 'gemm_cached', 'gemm_fetched_incl_wait',
+         'combine'])}
+    result = {
+        'metric': METRIC, 'value': world * T * a.steps / (ms / 1e3), 'unit': 'tokens/s',
+        'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': ms / a.steps,
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
+        'data': 'synthetic: random-init N(0,0.02) weights, N(0,1) hidden states rho=0.5, Zipf(1.1) router bias',
+        'config': {'workload': 'config 1 (Qwen3-30B-A3B MoE layer, decode batch 64/GPU) in the 48-layer MoE stack, '
+                               '30% global expert cache, all experts in pinned host memory',
+                   'model': 'Qwen3-30B-A3B MoE layers', 'moe_layers': L, 'global_batch': world * T,
+                   'tokens_per_gpu': T, 'seq_len': 1, 'parallelism': f'dp{world}-ep{world}',
+                   'cache_slots_per_rank': caps, 'pool_layers': pool_layers, 'policy': a.policy,
+                   'l2': 'no flush: each layer step reads > 126 MB of expert weights (> L2)'},
+        'roofline': roofline, 'layer_roofline': layer_roofline, 'layer_split_us': split,
+        'gpu_launches': int(st.launches), 'h2d_expert_copies': int(fetch_copies),
+        'host_wait_us_per_layer': round(st.host_wait_us / max(1, st.layers), 1),
+        'setup_s': round(setup_s, 1), 'e2e': e2e, 'clocks': clocks,
+    }
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        result['cpu_baseline'] = cpu_baseline(spec, wl, caps, T, a.cpu_seconds)
+    rt.close()
+    return result
+
+
+# ---------------------------------------------------------------------------
+def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None):
+    """Run the reference's CPU path (oracle port) over consecutive layers for
+    about `seconds`; returns (layers_done, elapsed)."""
+    from oracle import expert_ops as ops
+    from oracle.layer import OracleRuntime
+    from oracle import planner as op
+    masks = np.asarray([1 << r for r in range(world)], np.int64)
+    sec = np.ones(world)
+    lut = op.build_lut(spec.experts, world, masks, sec)
+    orc = OracleRuntime(spec, wl.pool, caps, 'ferry', masks, sec, lut)
+    gates = [g.cpu() for g in wl.gate]
+    biases = [b.cpu() for b in wl.bias]
+    g = torch.Generator().manual_seed(11)
+    done, t0 = 0, time.perf_counter()
+    prev = [None] * world
+    while True:
+        layer = done % spec.layers
+        xs = []
+        for r in range(world):
+            x = torch.randn(T, spec.hidden, generator=g).to(torch.bfloat16)
+            xs.append(x if prev[r] is None else (x.float() + prev[r].float()).to(torch.bfloat16))
+        routed = [ops.route_qwen3(x, gates[layer], spec.topk, True, biases[layer]) for x in xs]
+        prev, _, _ = orc.execute(layer, xs, [r[0] for r in routed], [r[1] for r in routed])
+        done += 1
+        el = time.perf_counter() - t0
+        if (el >= seconds and done >= min_layers) or (max_layers and done >= max_layers):
+            return done, el
+
+
+def cpu_baseline(spec, wl, caps, T, seconds):
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    done, el = cpu_layers(spec, wl, caps, T, 1, seconds)
+    per_layer = el / done
+    return {'value': T / (per_layer * spec.layers), 'unit': 'tokens/s', 'cores': threads,
+            'kind': 'port',
+            'sample': f'{done} consecutive MoE layers (64 tokens, 1 rank) of the same workload through '
+                      f'the oracle port (C planner/layout + torch-CPU expert ops), '
+                      f'{per_layer * 1e3:.1f} ms/layer, scaled to 48 layers'}
+
+
+def run_reference(a, rank, world):
+    """The reference's CPU path on this host's cores (rank 0 only)."""
+    from ferry_b200.workload import SyntheticMoE
+    spec = qwen3_spec(a.layers)
+    T = a.tokens
+    caps = spec.cache_slots(a.cache_ratio, world)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+
+    class _Pool:  # the CPU path reads weights straight from a host pool
+        pass
+    wl = SyntheticMoE(spec, seed=0, device='cpu', pool_layers=1, build_pool=False)
+    g = torch.Generator().manual_seed(1)
+    wl.pool = (torch.randn(spec.experts, spec.expert_elements, generator=g) * 0.02).to(torch.bfloat16)
+    layers_per_step = 4
+    for _ in range(a.warmup):
+        cpu_layers(spec, wl, caps, T, world, 0.0, min_layers=1, max_layers=1)
+    t0 = time.perf_counter()
+    total_layers = 0
+    for _ in range(a.steps):
+        done, _ = cpu_layers(spec, wl, caps, T, world, 0.0, min_layers=layers_per_step,
+                             max_layers=layers_per_step)
+        total_layers += done
+    el = time.perf_counter() - t0
+    per_layer = el / total_layers
+    step_s = per_layer * spec.layers
+    value = world * T / step_s
+    return {'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': a.steps,
+            'warmup': a.warmup, 'ms_per_step': step_s * 1e3, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'impl': 'reference',
+            'data': 'synthetic: random-init N(0,0.02) weights, N(0,1) hidden states, Zipf(1.1) router bias',
+            'config': {'workload': 'config 1 (Qwen3-30B-A3B MoE layer, decode batch 64/GPU) in the '
+                                   '48-layer MoE stack, 30% global expert cache',
+                       'model': 'Qwen3-30B-A3B MoE layers', 'moe_layers': spec.layers,
+                       'global_batch': world * T, 'tokens_per_gpu': T, 'seq_len': 1,
+                       'parallelism': f'dp{world}-ep{world} (emulated on the host)'},
+            'cpu_baseline': {'value': value, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
+                             'sample': f'{layers_per_step} MoE layers per step x {a.steps} steps, '
+                                       f'{world} rank(s) emulated in one process, scaled to '
+                                       f'{spec.layers} layers ({per_layer * 1e3:.1f} ms/layer)'},
+            'e2e': {'value': value, 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+
+
+def main():
+    a = parse()
+    if a.impl == 'reference':
+        rank = int(os.environ.get('RANK', '0'))
+        world = int(os.environ.get('WORLD_SIZE', str(a.gpus)))
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(a, rank, world)), flush=True)
+        return 0
+    rank, world, local = init_dist(a.gpus)
+    try:
+        result = run_ours(a, rank, world, local)
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.barrier()
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == '__main__':
+    sys.exit(main())

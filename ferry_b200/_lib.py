@@ -55,7 +55,8 @@ class LayerConfig(ctypes.Structure):
 class LayerStats(ctypes.Structure):
     """ferryb_layer_stats (include/ferryb.h)."""
     _fields_ = [(n, _i64) for n in ('layers', 'fetches', 'routes', 'recv_rows', 'dispatch_bytes',
-                                     'combine_bytes')] + [
+                                     'combine_bytes', 'launches', 'hit_experts', 'hit_weight_bytes',
+                                     'timed_layers')] + [
         ('host_wait_us', _dbl), ('phase_us', _dbl * 5)]
 
 
@@ -104,6 +105,7 @@ SIGNATURES = {
     'ferryb_layer_get_stats': (_i32, [_vp, ctypes.POINTER(LayerStats)]),
     'ferryb_layer_reset_stats': (_i32, [_vp]),
     'ferryb_layer_last_summary': (_i32, [_vp, ctypes.POINTER(LayoutSummary)]),
+    'ferryb_layer_collect_timing': (_i32, [_vp]),
     'ferryb_layer_destroy': (_i32, [_vp]),
 }
 

@@ -64,7 +64,11 @@ struct ferryb_layer {
   ferryb_layout_summary* summary_host = nullptr;
   int32_t* errs_host = nullptr;  // pinned copy of the device error words
   cudaEvent_t summary_ev = nullptr;
-  cudaEvent_t tev[8] = {};
+  // timing mode: 6 events per layer, recorded without host syncs and
+  // collected by ferryb_layer_collect_timing
+  std::vector<cudaEvent_t> tev_pool;
+  size_t tev_used = 0;
+  cudaEvent_t* tev = nullptr;
   GemmMaps maps{};
   ferryb_layer_stats stats{};
 };
@@ -228,7 +232,6 @@ extern "C" int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_
   FB_CUDA(cudaHostAlloc(&L->summary_host, sizeof(ferryb_layout_summary), cudaHostAllocDefault));
   FB_CUDA(cudaHostAlloc(&L->errs_host, 8 * sizeof(int32_t), cudaHostAllocDefault));
   FB_CUDA(cudaEventCreateWithFlags(&L->summary_ev, cudaEventDisableTiming));
-  for (auto& e : L->tev) FB_CUDA(cudaEventCreate(&e));
   const int64_t routes = (int64_t)cfg->world * cfg->tokens_per_rank * cfg->topk;
   s = make_gemm_maps(&L->maps, cache, cache_slots, L->x_sorted, L->act, routes, cfg->hidden,
                      cfg->intermediate);
@@ -279,7 +282,19 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   const uint64_t seq = (uint64_t)event + 1;
   const bool timing = c.timing != 0;
   uint8_t* half = L->symm + parity * L->sl.half;
-  if (timing) FB_CUDA(cudaEventRecord(L->tev[0], stream));
+  int64_t launches = 0;
+  if (timing) {
+    if (L->tev_used + 6 > L->tev_pool.size()) {
+      for (int i = 0; i < 6 * 64; ++i) {
+        cudaEvent_t e;
+        FB_CUDA(cudaEventCreate(&e));
+        L->tev_pool.push_back(e);
+      }
+    }
+    L->tev = L->tev_pool.data() + L->tev_used;
+    L->tev_used += 6;
+    FB_CUDA(cudaEventRecord(L->tev[0], stream));
+  }
 
   // 1 router + all-gather
   RouterArgs ra{};
@@ -307,6 +322,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   ra.off_prob = prob_offset(c);
   int s = router_launch(ra, seq, stream);
   if (s) return s;
+  launches += 1;
 
   // 2 planner
   PlanInputs in{};
@@ -322,6 +338,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   in.hist = reinterpret_cast<const int*>(half + L->sl.gather_hist);
   PlanOutputs po{L->fetches, L->n_fetches, L->dest, L->counts, L->errs + 0};
   if ((s = plan_launch(L->pc, L->ps, in, po, stream))) return s;
+  launches += 1;
 
   // 3 layer slots + layout
   // slots past a rank's capacity are never filled, so scanning maxcap is exact
@@ -339,6 +356,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   la.csr_pos = L->csr_pos; la.peer_row = L->peer_row; la.groups = L->groups;
   la.summary = L->summary_dev; la.err = L->errs + 1;
   if ((s = layout_launch(la, stream))) return s;
+  launches += 2;  // layer_slots + layout
   if (timing) FB_CUDA(cudaEventRecord(L->tev[1], stream));
 
   // 4 summary to the host
@@ -379,23 +397,27 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
                                   static_cast<__nv_bfloat16*>(out));
   if ((s = fused_dispatch(fa, seq, stream))) return s;
   if ((s = fused_permute(fa, seq, sum.n_routes, stream))) return s;
+  launches += 2 + (c.world > 1 ? 1 : 0);  // dispatch (+ signal) + permute
   if (timing) FB_CUDA(cudaEventRecord(L->tev[2], stream));
 
   // 8 grouped SwiGLU: cached experts, then each fetched expert after its copy
   if ((s = swiglu_grouped_maps(L->maps, L->groups, sum.n_hit, L->route_w, L->act,
                                L->expert_out, L->errs + 2, stream)))
     return s;
+  if (sum.n_hit) launches += 2;
   if (timing) FB_CUDA(cudaEventRecord(L->tev[3], stream));
   for (int i = 0; i < sum.n_fetch_mine; ++i) {
     if ((s = ferryb_h2d_wait_device(L->h2d, &fslots[i], 1, stream))) return s;
     if ((s = swiglu_grouped_maps(L->maps, L->groups + sum.n_hit + i, 1, L->route_w, L->act,
                                  L->expert_out, L->errs + 2, stream)))
       return s;
+    launches += 2;
   }
   if (timing) FB_CUDA(cudaEventRecord(L->tev[4], stream));
 
   // 9 combine
   if ((s = fused_combine(fa, seq, sum.n_recv, stream))) return s;
+  launches += (sum.n_recv > 0 ? 1 : 0) + (c.world > 1 ? 2 : 0);  // combine (+ signal + final)
   if (timing) FB_CUDA(cudaEventRecord(L->tev[5], stream));
 
   if (selected_out)
@@ -407,6 +429,9 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
 
   // counters (the reference's fetches_per_rank, copies, dispatch/combine bytes)
   L->stats.layers += 1;
+  L->stats.launches += launches;
+  L->stats.hit_experts += sum.n_hit;
+  L->stats.hit_weight_bytes += (int64_t)sum.n_hit * 3 * (int64_t)c.hidden * c.intermediate * 2;
   L->stats.fetches += sum.n_fetch_mine;
   L->stats.routes += sum.n_routes;
   L->stats.recv_rows += sum.n_recv;
@@ -418,12 +443,22 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   }
   L->stats.dispatch_bytes += sent_remote * (2 * (int64_t)c.hidden + 3 * c.topk);
   L->stats.combine_bytes += recv_remote * 2 * (int64_t)c.hidden;
-  if (timing) {
-    FB_CUDA(cudaEventSynchronize(L->tev[5]));
-    float ms[5];
-    for (int i = 0; i < 5; ++i) FB_CUDA(cudaEventElapsedTime(&ms[i], L->tev[i], L->tev[i + 1]));
-    for (int i = 0; i < 5; ++i) L->stats.phase_us[i] += ms[i] * 1000.0;
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
+  FB_CHECK_ARG(L, "layer_collect_timing: null argument");
+  for (size_t b = 0; b + 6 <= L->tev_used; b += 6) {
+    cudaEvent_t* e = L->tev_pool.data() + b;
+    FB_CUDA(cudaEventSynchronize(e[5]));
+    for (int i = 0; i < 5; ++i) {
+      float ms = 0.0f;
+      FB_CUDA(cudaEventElapsedTime(&ms, e[i], e[i + 1]));
+      L->stats.phase_us[i] += ms * 1000.0;
+    }
+    L->stats.timed_layers += 1;
   }
+  L->tev_used = 0;
   return FERRYB_OK;
 }
 
@@ -470,8 +505,7 @@ extern "C" int ferryb_layer_destroy(ferryb_layer* L) {
   if (L->summary_host) cudaFreeHost(L->summary_host);
   if (L->errs_host) cudaFreeHost(L->errs_host);
   if (L->summary_ev) cudaEventDestroy(L->summary_ev);
-  for (auto e : L->tev)
-    if (e) cudaEventDestroy(e);
+  for (auto e : L->tev_pool) cudaEventDestroy(e);
   delete L;
   return FERRYB_OK;
 }

@@ -298,10 +298,15 @@ typedef struct ferryb_layer_config {
 
 typedef struct ferryb_layer_stats {
   int64_t layers, fetches, routes, recv_rows, dispatch_bytes, combine_bytes;
-  double host_wait_us; /* host time blocked on the plan summary */
-  double phase_us[5];  /* timing mode: route+plan+layout, summary+dispatch+permute,
-                          cached-expert GEMM, fetched-expert GEMMs (incl. copy waits),
-                          combine */
+  int64_t launches;          /* kernels launched by the executor */
+  int64_t hit_experts;       /* experts served from the cache without a fetch */
+  int64_t hit_weight_bytes;  /* their weight bytes (algorithmic GEMM traffic) */
+  int64_t timed_layers;      /* layers whose phase times are in phase_us */
+  double host_wait_us;       /* host time blocked on the plan summary */
+  double phase_us[5];        /* timing mode (CUDA events, collected by
+                                ferryb_layer_collect_timing): route+plan+layout,
+                                summary+dispatch+permute, cached-expert GEMM,
+                                fetched-expert GEMMs (incl. copy waits), combine */
 } ferryb_layer_stats;
 
 typedef struct ferryb_layer ferryb_layer;
@@ -329,6 +334,8 @@ FERRYB_API int ferryb_layer_execute(ferryb_layer* layer, int64_t event, int32_t 
                                     const void* weights, const float* probs_tail,
                                     int32_t n_probs_tail, void* out, ferryb_stream_t stream);
 FERRYB_API int ferryb_layer_get_stats(const ferryb_layer* layer, ferryb_layer_stats* out);
+/* Timing mode: wait for the recorded phase events and add them to the stats. */
+FERRYB_API int ferryb_layer_collect_timing(ferryb_layer* layer);
 /* The plan summary of the last layer run (fetch list, per-rank counts). */
 FERRYB_API int ferryb_layer_last_summary(const ferryb_layer* layer, ferryb_layout_summary* out);
 FERRYB_API int ferryb_layer_reset_stats(ferryb_layer* layer);
