@@ -40,7 +40,9 @@ class LayoutArgs(ctypes.Structure):
     """ferryb_layout_args (include/ferryb.h)."""
     _fields_ = [('ids', _vp), ('dest', _vp), ('world', _i32c), ('tokens_per_rank', _i32c),
                 ('topk', _i32c), ('experts', _i32c), ('rank', _i32c)] + [(n, _vp) for n in (
-                    'fetches', 'n_fetches', 'layer_slot', 'send_idx', 'send_ids', 'send_counts',
+                    'fetches', 'n_fetches', 'layer_slot', 'slots_row')] + [
+        ('slots_count', _i32c), ('layer', _i32c)] + [(n, _vp) for n in (
+                    'send_idx', 'send_ids', 'send_counts',
                     'recv_counts', 'starts', 'rows', 'cols', 'n_send', 'n_recv', 'recv_token',
                     'csr_pos', 'peer_row', 'groups', 'summary', 'err')]
 
@@ -106,6 +108,7 @@ SIGNATURES = {
     'ferryb_layer_reset_stats': (_i32, [_vp]),
     'ferryb_layer_last_summary': (_i32, [_vp, ctypes.POINTER(LayoutSummary)]),
     'ferryb_layer_collect_timing': (_i32, [_vp]),
+    'ferryb_debug_plan_timestamps': (_i32, [_vp]),
     'ferryb_layer_destroy': (_i32, [_vp]),
 }
 

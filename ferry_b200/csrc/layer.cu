@@ -341,22 +341,23 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   launches += 1;
 
   // 3 layer slots + layout
-  // slots past a rank's capacity are never filled, so scanning maxcap is exact
-  if ((s = layer_slots_launch(L->planner.slots + (size_t)c.rank * L->planner.maxcap,
-                              L->planner.maxcap, layer, c.experts, L->layer_slot, stream)))
-    return s;
   ferryb_layout_args la{};
   la.ids = in.ids; la.dest = L->dest;
   la.world = c.world; la.tokens_per_rank = c.tokens_per_rank; la.topk = c.topk;
   la.experts = c.experts; la.rank = c.rank;
-  la.fetches = L->fetches; la.n_fetches = L->n_fetches; la.layer_slot = L->layer_slot;
+  la.fetches = L->fetches; la.n_fetches = L->n_fetches; la.layer_slot = nullptr;
+  // layer_slots in-kernel; slots past a rank's capacity are never filled, so
+  // scanning maxcap slots is exact
+  la.slots_row = L->planner.slots + (size_t)c.rank * L->planner.maxcap;
+  la.slots_count = L->planner.maxcap;
+  la.layer = layer;
   la.send_idx = L->send_idx; la.send_ids = L->send_ids; la.send_counts = L->send_counts;
   la.recv_counts = L->recv_counts; la.starts = L->starts; la.rows = L->rows; la.cols = L->cols;
   la.n_send = L->n_send; la.n_recv = L->n_recv; la.recv_token = L->recv_token;
   la.csr_pos = L->csr_pos; la.peer_row = L->peer_row; la.groups = L->groups;
   la.summary = L->summary_dev; la.err = L->errs + 1;
   if ((s = layout_launch(la, stream))) return s;
-  launches += 2;  // layer_slots + layout
+  launches += 1;  // layout
   if (timing) FB_CUDA(cudaEventRecord(L->tev[1], stream));
 
   // 4 summary to the host

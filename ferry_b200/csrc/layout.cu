@@ -32,7 +32,10 @@ struct LaySmem {
   int warp_sum[32];
   int run;                                   // running scan carry
   int fetched_rank[kMaxExpertsL];            // fetch order of expert on this rank, or -1
-  int n_groups, n_hit;
+  int lslot[kMaxExpertsL];                   // slot of each expert of the layer on this rank
+  int fetch_key[kMaxExpertsL], fetch_slot[kMaxExpertsL];
+  int recv_cnt[kMaxWorldL];
+  int n_groups, n_hit, n_fetch_mine;
 };
 
 // Exclusive block scan of one int per thread (1024 threads); returns the
@@ -94,23 +97,47 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
   int ids_buf[16];
 
   // ---- fetched experts of this rank, in fetch order -----------------------
-  for (int e = tid; e < E; e += blockDim.x) { sm.fetched_rank[e] = -1; sm.expert_count[e] = 0; }
+  for (int e = tid; e < E; e += blockDim.x) {
+    sm.fetched_rank[e] = -1;
+    sm.expert_count[e] = 0;
+    sm.lslot[e] = a.layer_slot ? a.layer_slot[e] : -1;
+  }
+  if (tid < R) sm.recv_cnt[tid] = 0;
   __syncthreads();
-  if (tid == 0) {
-    int j = 0;
-    const int nf = a.n_fetches ? *a.n_fetches : 0;
-    for (int i = 0; i < nf; ++i) {
-      if (a.fetches[i * 3 + 0] != rank) continue;
-      const int key = a.fetches[i * 3 + 1];
+  if (a.slots_row) {  // layer_slots (ferry/policy.py:197-205) from this rank's slots row
+    for (int i = tid; i < a.slots_count; i += blockDim.x) {
+      const int key = a.slots_row[i];
+      if (key >= 0 && key / E == a.layer) sm.lslot[key % E] = i;
+    }
+  }
+  {
+    const int nf = a.n_fetches ? *a.n_fetches : 0;  // <= experts <= 1024 threads
+    int mine = 0, key = 0, slot = 0;
+    if (tid < nf) {
+      mine = a.fetches[tid * 3 + 0] == rank;
+      key = a.fetches[tid * 3 + 1];
+      slot = a.fetches[tid * 3 + 2];
+    }
+    const int j = block_scan(mine, sm.warp_sum, &total_sh);
+    if (mine) {
       sm.fetched_rank[key % E] = j;
+      sm.fetch_key[j] = key;
+      sm.fetch_slot[j] = slot;
       if (a.summary) {
         a.summary->fetch_keys[j] = key;
-        a.summary->fetch_slots[j] = a.fetches[i * 3 + 2];
+        a.summary->fetch_slots[j] = slot;
       }
-      ++j;
     }
-    if (a.summary) a.summary->n_fetch_mine = j;
-    sm.run = 0;
+    if (tid == 0) {
+      sm.n_fetch_mine = total_sh;
+      if (a.summary) a.summary->n_fetch_mine = total_sh;
+      sm.run = 0;
+    }
+  }
+  __syncthreads();
+  if (a.layer_slot == nullptr && a.slots_row == nullptr) {
+    // without a slot table, fetched experts still know their slots
+    for (int j = tid; j < sm.n_fetch_mine; j += blockDim.x) sm.lslot[sm.fetch_key[j] % E] = sm.fetch_slot[j];
   }
   __syncthreads();
 
@@ -166,21 +193,13 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
     if (has) {
       if (a.recv_token) a.recv_token[row] = g;
       for (int j = 0; j < size; ++j) atomicAdd(&sm.expert_count[ids_buf[j]], 1);
+      atomicAdd(&sm.recv_cnt[g / T], 1);
     }
     received += total_sh;
     __syncthreads();
   }
-  if (tid < R) {
-    int cnt = 0;
-    for (int t = 0; t < T; ++t) {
-      const int g = tid * T + t;
-      int has = 0;
-      for (int j = 0; j < K; ++j) has |= a.dest[g * K + j] == rank;
-      cnt += has;
-    }
-    a.recv_counts[tid] = cnt;
-  }
   __syncthreads();
+  if (tid < R) a.recv_counts[tid] = sm.recv_cnt[tid];
   // starts = exclusive scan of expert counts (E <= 256 < 1024 threads)
   {
     const int v = tid < E ? sm.expert_count[tid] : 0;
@@ -231,44 +250,42 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
   if (tid == 0) *a.n_recv = received;
 
   // ---- GEMM groups: cached experts (ascending), then fetched (fetch order) --
-  if (tid == 0 && a.groups && a.summary) {
+  if (a.groups && a.summary) {
     GemmGroup* groups = reinterpret_cast<GemmGroup*>(a.groups);
-    int ng = 0;
-    for (int e = 0; e < E; ++e) {
-      const int cnt = sm.starts[e + 1] - sm.starts[e];
-      if (cnt > 0 && sm.fetched_rank[e] < 0) {
-        const int slot = a.layer_slot ? a.layer_slot[e] : -1;
-        groups[ng++] = GemmGroup{slot, sm.starts[e], cnt, e};
-      }
-    }
-    const int n_hit = ng;
-    const int nf = a.summary->n_fetch_mine;
-    for (int j = 0; j < nf; ++j) {
-      const int e = a.summary->fetch_keys[j] % E;
-      const int cnt = sm.starts[e + 1] - sm.starts[e];
-      groups[ng++] = GemmGroup{a.summary->fetch_slots[j], sm.starts[e], cnt, e};
-    }
-    a.summary->n_groups = ng;
-    a.summary->n_hit = n_hit;
-    a.summary->n_recv = received;
-    a.summary->n_send = sent;
-    a.summary->n_routes = sm.starts[E];
-    for (int e = 0; e < E; ++e) {
-      const int cnt = sm.starts[e + 1] - sm.starts[e];
-      if (cnt > 0 && (a.layer_slot == nullptr || a.layer_slot[e] < 0) && sm.fetched_rank[e] < 0)
+    const int e = tid;
+    int cnt = 0, hit = 0;
+    if (e < E) {
+      cnt = sm.starts[e + 1] - sm.starts[e];
+      hit = cnt > 0 && sm.fetched_rank[e] < 0;
+      if (cnt > 0 && sm.lslot[e] < 0)
         atomicCAS(a.err, 0, DEV_NO_SLOT);  // scheduled here but not cached (ferry/layout.py:91)
     }
-    for (int p = 0; p < 32; ++p) {
+    const int pos = block_scan(hit, sm.warp_sum, &total_sh);
+    const int n_hit = total_sh;
+    if (hit) groups[pos] = GemmGroup{sm.lslot[e], sm.starts[e], cnt, e};
+    if (e < E && cnt > 0 && sm.fetched_rank[e] >= 0)
+      groups[n_hit + sm.fetched_rank[e]] = GemmGroup{sm.lslot[e], sm.starts[e], cnt, e};
+    if (tid < 32) {
+      const int p = tid;
       a.summary->send_counts[p] = p < R ? (int)a.send_counts[p] : 0;
-      a.summary->recv_counts[p] = p < R ? (int)a.recv_counts[p] : 0;
+      a.summary->recv_counts[p] = p < R ? sm.recv_cnt[p] : 0;
       a.summary->fetch_counts[p] = 0;
     }
+    __syncthreads();
     const int nf_all = a.n_fetches ? *a.n_fetches : 0;
-    for (int i = 0; i < nf_all; ++i) {
-      const int r = a.fetches[i * 3 + 0];
-      if (r >= 0 && r < 32) a.summary->fetch_counts[r] += 1;
+    if (tid < nf_all) {
+      const int r = a.fetches[tid * 3 + 0];
+      if (r >= 0 && r < 32) atomicAdd(&a.summary->fetch_counts[r], 1);
     }
-    a.summary->err = *a.err;
+    if (tid == 0) {
+      a.summary->n_groups = n_hit + sm.n_fetch_mine;
+      a.summary->n_hit = n_hit;
+      a.summary->n_recv = received;
+      a.summary->n_send = sent;
+      a.summary->n_routes = sm.starts[E];
+    }
+    __syncthreads();
+    if (tid == 0) a.summary->err = atomicAdd(a.err, 0);
   }
 }
 

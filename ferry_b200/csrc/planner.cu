@@ -39,8 +39,8 @@ constexpr int kPlanThreads = 1024;
 constexpr int kPlanWarps = kPlanThreads / 32;
 
 struct SlotRec {
-  uint64_t k0;  // rank << 56 | class << 48 | ... (see make_rec)
-  uint64_t k1;
+  uint64_t k0;  // rank << 56 | class << 48 | score bits (eligible) / 0
+  uint64_t k1;  // last use << 24 | key (eligible), slot index (empty)
   uint32_t slot;  // index into slots[] (rank * maxcap + i)
   uint32_t pad;
 };
@@ -101,11 +101,19 @@ struct PlanSmem {
   int n_assigned[kMaxWorld];
   int seg_start[kMaxWorld + 1];
   float gate[kMaxExperts];
+  int owner_layer[kMaxExperts];
   int status;
   MT rng;
 };
 
 __device__ __forceinline__ void set_err(int* err, int code) { atomicCAS(err, 0, code); }
+
+// Optional phase timestamps of the planner (profiling aid; NULL = off).
+__device__ unsigned long long* g_plan_ts = nullptr;
+#define PLAN_TS(k)                                              \
+  do {                                                          \
+    if (threadIdx.x == 0 && g_plan_ts) g_plan_ts[k] = globaltimer_ns(); \
+  } while (0)
 
 // ---------------------------------------------------------------------------
 // GateHistory.update + scores for `layer` (ferry/metadata.py:24-38).
@@ -113,7 +121,7 @@ __device__ __forceinline__ void set_err(int* err, int code) { atomicCAS(err, 0, 
 // rank, rank-major (ferry/metadata.py:57, :80-82).  Probability rows come in
 // prob_rows [n_rows, E] (float32).
 __device__ void history_step(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
-                             float* gate_out) {
+                             float* gate_out, int* cnt_scratch) {
   const int W = c.window, E = c.experts, K = c.topk;
   const int L = in.layer;
   const int T = in.tokens_per_rank;
@@ -161,24 +169,39 @@ __device__ void history_step(const PlanConfig& c, const PlanState& s, const Plan
     }
   }
   __syncthreads();
-  __threadfence_block();
-  const int n = max(1, *count);
+  const int filled = *count;  // slots [0, filled) hold rows (the ring never has holes)
+  const int n = max(1, filled);
   if (ring_p) {
+    // float64 sum over slots in slot order; loads batched 8 ahead
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
       double acc = 0.0;
-      for (int slot = 0; slot < *count; ++slot) acc = __dadd_rn(acc, (double)ring_p[(size_t)slot * E + e]);
+      int slot = 0;
+      for (; slot + 8 <= filled; slot += 8) {
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = ring_p[(size_t)(slot + q) * E + e];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc = __dadd_rn(acc, (double)v[q]);
+      }
+      for (; slot < filled; ++slot) acc = __dadd_rn(acc, (double)ring_p[(size_t)slot * E + e]);
       gate_out[e] = __double2float_rn(__ddiv_rn(acc, (double)n));
     }
   } else {
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-      int cnt = 0;
-      for (int slot = 0; slot < *count; ++slot) {
-        bool hit = false;
-        for (int k = 0; k < K; ++k) hit |= ring[(size_t)slot * K + k] == (uint8_t)e;
-        cnt += hit;
+    // a row counts once for each distinct id it holds (rows are 0/1 indicators)
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt_scratch[e] = 0;
+    __syncthreads();
+    for (int slot = threadIdx.x; slot < filled; slot += blockDim.x) {
+      const uint8_t* row = ring + (size_t)slot * K;
+      for (int k = 0; k < K; ++k) {
+        const int e = row[k];
+        bool dup = e >= E;
+        for (int q = 0; q < k; ++q) dup |= row[q] == e;
+        if (!dup) atomicAdd(&cnt_scratch[e], 1);
       }
-      gate_out[e] = __double2float_rn(__ddiv_rn((double)cnt, (double)n));
     }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+      gate_out[e] = __double2float_rn(__ddiv_rn((double)cnt_scratch[e], (double)n));
   }
   __syncthreads();
 }
@@ -236,56 +259,56 @@ __device__ bool greedy_quota_warp(const PlanConfig& c, int m, const int* capacit
   return true;
 }
 
-// load_balanced_assignment (ferry/policy.py:49-106) on one warp.
+// load_balanced_assignment (ferry/policy.py:49-106) on one warp; lane r
+// owns rank r.  Loads are token counts (< 2^31), so 32-bit arithmetic is
+// exact; the peak load only grows at the chosen rank, so it is kept
+// incrementally.  Reductions run over the next power of two >= R lanes.
 __device__ void assignment_warp(const PlanConfig& c, PlanSmem& sm, const int* demand /*[E*R]*/,
                                 const int* owner_layer /*[E]*/) {
   const int lane = threadIdx.x & 31;
   const int R = c.world, E = c.experts, m = sm.m;
-  // N_r: tokens routed to experts already cached on r.
-  int64_t load = 0, remaining = 0;
-  if (lane < R) {
-    for (int e = 0; e < E; ++e)
-      if (owner_layer[e] == lane) load += sm.demand_total[e];
-    remaining = sm.quota[lane];
+  int span = 1;
+  while (span < R) span <<= 1;
+  // N_r: tokens routed to experts already cached on r (owner_layer in smem).
+  int load = 0, remaining = 0;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    const int o = e < E ? owner_layer[e] : -1;
+    const int d = e < E ? sm.demand_total[e] : 0;
+    for (int r = 0; r < R; ++r) {
+      int v = (o == r) ? d : 0;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == r) load += v;
+    }
   }
+  if (lane < R) remaining = (int)sm.quota[lane];
+  int peak = lane < R ? load : 0;
+  for (int off = span >> 1; off > 0; off >>= 1) peak = max(peak, __shfl_xor_sync(0xffffffffu, peak, off));
+  const int kBig = 0x7fffffff;
   for (int oi = 0; oi < m; ++oi) {
     const int i = sm.order[oi];
     const int e = sm.misses[i];
-    const int64_t total = sm.totals[i];
-    int64_t peak = (lane < R) ? load : INT64_MIN;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const int64_t v = __shfl_xor_sync(0xffffffffu, peak, o);
-      peak = v > peak ? v : peak;
-    }
+    const int total = (int)sm.totals[i];
     const bool has = lane < R && remaining > 0;
-    const int64_t projected = has ? (peak > load + total ? peak : load + total) : ((int64_t)1 << 60);
-    int64_t lowest = projected;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const int64_t v = __shfl_xor_sync(0xffffffffu, lowest, o);
-      lowest = v < lowest ? v : lowest;
-    }
-    int64_t slack = 0;
+    const int projected = has ? max(peak, load + total) : kBig;
+    int lowest = projected;
+    for (int off = span >> 1; off > 0; off >>= 1) lowest = min(lowest, __shfl_xor_sync(0xffffffffu, lowest, off));
+    int slack = 0;
     if (c.bps > 0) {
-      const int64_t prod = (int64_t)((uint64_t)lowest * (uint64_t)c.bps);
-      int64_t qd = prod / 10000;
-      if ((prod % 10000 != 0) && (prod < 0)) qd -= 1;  // floor division
-      slack = qd > 1 ? qd : 1;
+      const int64_t prod = (int64_t)lowest * c.bps;  // lowest >= 0 here
+      const int64_t q = prod / 10000;
+      slack = q > 1 ? (int)q : 1;
     }
-    const int64_t limit = lowest + slack;
-    const bool eligible = has && projected <= limit;
+    const bool eligible = has && (int64_t)projected <= (int64_t)lowest + slack;
     const int a = (lane < R) ? demand[e * R + lane] : 0;
     // lexicographic max of (a, -projected, -load), lowest lane on ties
-    int best = eligible ? lane : -1;
-    int ba = a;
-    int64_t bp = projected, bl = load;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const int ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oa = __shfl_xor_sync(0xffffffffu, ba, o);
-      const int64_t op = __shfl_xor_sync(0xffffffffu, bp, o);
-      const int64_t ol = __shfl_xor_sync(0xffffffffu, bl, o);
+    int best = eligible ? lane : -1, ba = a, bp = projected, bl = load;
+    for (int off = span >> 1; off > 0; off >>= 1) {
+      const int ob = __shfl_xor_sync(0xffffffffu, best, off);
+      const int oa = __shfl_xor_sync(0xffffffffu, ba, off);
+      const int op = __shfl_xor_sync(0xffffffffu, bp, off);
+      const int ol = __shfl_xor_sync(0xffffffffu, bl, off);
       bool take;
       if (ob < 0) take = false;
       else if (best < 0) take = true;
@@ -295,8 +318,13 @@ __device__ void assignment_warp(const PlanConfig& c, PlanSmem& sm, const int* de
       else take = ob < best;
       if (take) { best = ob; ba = oa; bp = op; bl = ol; }
     }
+    best = __shfl_sync(0xffffffffu, best, 0);
     if (lane == 0) sm.assignment[i] = best;
-    if (best >= 0 && lane == best) { remaining -= 1; load += total; }
+    if (best >= 0) {
+      if (lane == best) { remaining -= 1; load += total; }
+      const int nb = __shfl_sync(0xffffffffu, load, best);
+      peak = max(peak, nb);
+    }
   }
   __syncwarp();
 }
@@ -313,6 +341,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   SlotRec* recs = reinterpret_cast<SlotRec*>(dsm + c.sort_offset);       // [sort_n]
   int64_t* greedy_load = reinterpret_cast<int64_t*>(dsm + c.greedy_offset);  // [G]
 
+  PLAN_TS(0);
   if (tid == 0) {
     sm.status = 0;
     sm.m = 0;
@@ -330,11 +359,13 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   if (in.gate_scores) {
     for (int e = tid; e < E; e += blockDim.x) sm.gate[e] = in.gate_scores[e];
   } else {
-    history_step(c, s, in, sm.gate);
+    history_step(c, s, in, sm.gate, sm.demand_total);  // demand_total is free until step 1
   }
   __syncthreads();
+  PLAN_TS(1);
   for (int e = tid; e < E; e += blockDim.x) s.scores[(size_t)L * E + e] = sm.gate[e];
 
+  const int base = L * E;
   // -- Step 1: demand d[e, r] ----------------------------------------------
   if (in.hist) {
     for (int i = tid; i < E * R; i += blockDim.x) demand[(i % E) * R + i / E] = in.hist[i];
@@ -346,12 +377,12 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     atomicAdd(&demand[e * R + r], 1);
   }
   __syncthreads();
-  const int base = L * E;
   for (int e = tid; e < E; e += blockDim.x) {
     int tot = 0;
     for (int r = 0; r < R; ++r) tot += demand[e * R + r];
     sm.demand_total[e] = tot;
     sm.active[e] = tot > 0;
+    sm.owner_layer[e] = s.owner[base + e];
   }
   if (tid < R) { sm.capacity[tid] = 0; sm.n_assigned[tid] = 0; }
   __syncthreads();
@@ -360,7 +391,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     int m = 0;
     for (int e0 = 0; e0 < E; e0 += 32) {
       const int e = e0 + lane;
-      const bool miss = e < E && sm.active[e] && s.owner[base + e] < 0;
+      const bool miss = e < E && sm.active[e] && sm.owner_layer[e] < 0;
       const unsigned bal = __ballot_sync(0xffffffffu, miss);
       if (miss) sm.misses[m + __popc(bal & ((1u << lane) - 1))] = e;
       m += __popc(bal);
@@ -368,13 +399,23 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     if (lane == 0) sm.m = m;
   }
   // admission capacity u_r (ferry/policy.py:36-46)
-  for (int i = tid; i < c.total_slots; i += blockDim.x) {
-    const int r = c.slot_rank[i];
-    const int key = s.slots[c.slot_index[i]];
-    const bool free_ = key < 0 || !(key / E == L && sm.active[key % E]);
-    if (free_) atomicAdd(&sm.capacity[r], 1);
+  for (int i0 = 0; i0 < c.total_slots; i0 += blockDim.x) {
+    const int i = i0 + tid;
+    int r = -1;
+    bool free_ = false;
+    if (i < c.total_slots) {
+      r = c.slot_rank[i];
+      const int key = s.slots[c.slot_index[i]];
+      free_ = key < 0 || !(key / E == L && sm.active[key % E]);
+    }
+    // warp-aggregated: one shared atomic per (warp, rank)
+    const unsigned act = __ballot_sync(0xffffffffu, free_);
+    const unsigned same = __match_any_sync(0xffffffffu, r);
+    const unsigned grp = act & same;
+    if (free_ && (__ffs(grp) - 1) == lane) atomicAdd(&sm.capacity[r], __popc(grp));
   }
   __syncthreads();
+  PLAN_TS(2);
   const int m = sm.m;
 
   // -- Steps 2-3 (FERRY) or the random draw (RANDOM) ----------------------
@@ -407,7 +448,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
       sm.order[rank_i] = i;
     }
     __syncthreads();
-    if (warp == 0 && sm.status == 0) assignment_warp(c, sm, demand, s.owner + base);
+    if (warp == 0 && sm.status == 0) assignment_warp(c, sm, demand, sm.owner_layer);
   } else {
     if (tid == 0) {
       int room = 0, left[kMaxWorld];
@@ -426,6 +467,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     }
   }
   __syncthreads();
+  PLAN_TS(3);
   if (sm.status) {
     if (tid == 0) {
       set_err(out.err, sm.status);
@@ -437,48 +479,66 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   // -- Step 4: victims (one sort of every slot) and the commit -------------
   if (m > 0) {
     const int n = c.sort_n;  // power of two >= total_slots
+    // struct-of-arrays records in dynamic shared memory
+    uint64_t* k0 = reinterpret_cast<uint64_t*>(recs);
+    uint64_t* k1 = k0 + n;
+    uint32_t* sl = reinterpret_cast<uint32_t*>(k1 + n);
     for (int i = tid; i < n; i += blockDim.x) {
-      SlotRec rec;
+      uint64_t a0 = ~0ull, a1 = ~0ull;
+      uint32_t ix = 0xffffffffu;
       if (i < c.total_slots) {
         const int r = c.slot_rank[i];
         const int idx = c.slot_index[i];
         const int key = s.slots[idx];
-        uint64_t cls, k0lo, k1;
+        uint64_t cls, lo, hi;
         if (key < 0) {
-          cls = 0; k0lo = 0; k1 = (uint64_t)(idx - r * c.maxcap);
+          cls = 0; lo = 0; hi = (uint64_t)(idx - r * c.maxcap);
         } else if (key / E == L && sm.active[key % E]) {
-          cls = 2; k0lo = 0; k1 = 0;
+          cls = 2; lo = 0; hi = 0;
         } else {
           cls = 1;
-          k0lo = __float_as_uint(s.scores[key]);
-          k1 = ((uint64_t)s.last[key] << 24) | (uint64_t)key;
+          lo = __float_as_uint(s.scores[key]);
+          hi = ((uint64_t)s.last[key] << 24) | (uint64_t)key;
         }
-        rec.k0 = ((uint64_t)r << 56) | (cls << 48) | k0lo;
-        rec.k1 = k1;
-        rec.slot = (uint32_t)idx;
-      } else {
-        rec.k0 = ~0ull; rec.k1 = ~0ull; rec.slot = 0xffffffffu;
+        a0 = ((uint64_t)r << 56) | (cls << 48) | lo;
+        a1 = hi;
+        ix = (uint32_t)idx;
       }
-      recs[i] = rec;
+      k0[i] = a0; k1[i] = a1; sl[i] = ix;
     }
     __syncthreads();
-    // bitonic sort, ascending
+    PLAN_TS(4);
+    // bitonic sort, ascending.  With one compare-exchange per thread, the
+    // pairs of a stage with stride <= 32 lie inside one warp's 64-element
+    // block, so those stages need only __syncwarp.
+    const bool one_pass = n / 2 <= (int)blockDim.x;
     for (int size = 2; size <= n; size <<= 1) {
       for (int stride = size >> 1; stride > 0; stride >>= 1) {
         for (int i = tid; i < n / 2; i += blockDim.x) {
           const int lo = 2 * i - (i & (stride - 1));
           const int hi = lo + stride;
           const bool up = (lo & size) == 0;
-          SlotRec a = recs[lo], b = recs[hi];
-          if (rec_less(b, a) == up) { recs[lo] = b; recs[hi] = a; }
+          const uint64_t a0 = k0[lo], b0 = k0[hi], a1 = k1[lo], b1 = k1[hi];
+          const bool b_less = b0 < a0 || (b0 == a0 && b1 < a1);
+          if (b_less == up) {
+            k0[lo] = b0; k0[hi] = a0; k1[lo] = b1; k1[hi] = a1;
+            const uint32_t t = sl[lo]; sl[lo] = sl[hi]; sl[hi] = t;
+          }
         }
-        __syncthreads();
+        // block-wide barrier when this stage or the next pairs elements of
+        // different warps (stride > 32); between two warp-local stages a
+        // warp barrier suffices
+        const int next_stride = stride > 1 ? stride >> 1 : size;
+        if (stride > 32 || next_stride > 32 || !one_pass) __syncthreads();
+        else __syncwarp();
       }
     }
-    // j-th miss of rank r takes the j-th record of rank r's segment
+    __syncthreads();
+    PLAN_TS(5);
+    // the j-th miss assigned to rank r takes the j-th record of r's segment
     if (tid == 0) {
       int pos = 0;
-      for (int r = 0; r < R; ++r) { sm.seg_start[r] = pos; pos += c.capacities[r]; }
+      for (int r = 0; r < R; ++r) { sm.seg_start[r] = pos; pos += c.capacities[r]; sm.n_assigned[r] = 0; }
       for (int i = 0; i < m; ++i) {
         const int r = sm.assignment[i];
         sm.victim_pos[i] = sm.seg_start[r] + sm.n_assigned[r];
@@ -488,12 +548,14 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     __syncthreads();
     for (int i = tid; i < m; i += blockDim.x) {
       const int r = sm.assignment[i];
-      const SlotRec rec = recs[sm.victim_pos[i]];
-      const uint64_t cls = (rec.k0 >> 48) & 0xff;
-      const bool ok = rec.slot != 0xffffffffu && (int)(rec.k0 >> 56) == r && cls < 2 &&
-                      sm.victim_pos[i] < sm.seg_start[r] + c.capacities[r];
+      const int vp = sm.victim_pos[i];
+      const uint64_t rk0 = k0[vp];
+      const uint32_t rslot = sl[vp];
+      const uint64_t cls = (rk0 >> 48) & 0xff;
+      const bool ok = rslot != 0xffffffffu && (int)(rk0 >> 56) == r && cls < 2 &&
+                      vp < sm.seg_start[r] + c.capacities[r];
       if (!ok) { set_err(out.err, DEV_NO_SLOT); continue; }
-      const int idx = (int)rec.slot;
+      const int idx = (int)rslot;
       const int key = base + sm.misses[i];
       const int victim = s.slots[idx];
       if (victim >= 0) s.owner[victim] = -1;
@@ -505,6 +567,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     }
   }
   __syncthreads();
+  PLAN_TS(6);
   const int64_t tick = in.event + 1;
   for (int e = tid; e < E; e += blockDim.x)
     if (sm.active[e]) s.last[base + e] = tick;
@@ -516,6 +579,8 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     const int e = in.ids[i];
     out.dest[i] = e < E ? s.owner[base + e] : -1;
   }
+  __syncthreads();
+  PLAN_TS(7);
 }
 
 // ---------------------------------------------------------------------------
@@ -594,7 +659,9 @@ __global__ void assignment_kernel(const PlanConfig c, const int64_t* demand, con
     sm.order[rank_i] = i;
   }
   __syncthreads();
-  if ((tid >> 5) == 0) assignment_warp(c, sm, dem, owner + (size_t)layer * E);
+  for (int e = tid; e < E; e += blockDim.x) sm.owner_layer[e] = owner[(size_t)layer * E + e];
+  __syncthreads();
+  if ((tid >> 5) == 0) assignment_warp(c, sm, dem, sm.owner_layer);
   __syncthreads();
   for (int i = tid; i < m; i += blockDim.x) answer[i] = sm.assignment[i];
 }
@@ -790,5 +857,10 @@ extern "C" int ferryb_choose_slot(int32_t rank, int32_t layer, const uint8_t* ac
   choose_slot_kernel<<<1, 1024, 0, stream>>>(rank, layer, active, slots, maxcap, capacities, last,
                                              scores, experts, result);
   FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_debug_plan_timestamps(void* dev_ptr) {
+  FB_CUDA(cudaMemcpyToSymbol(g_plan_ts, &dev_ptr, sizeof(void*)));
   return FERRYB_OK;
 }

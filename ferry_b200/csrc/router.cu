@@ -22,11 +22,12 @@
 
 namespace ferryb {
 
-constexpr int kRouterThreads = 256;
+constexpr int kRouterThreads = 1024;  // 32 warps: a few experts per warp
 
 __global__ void __launch_bounds__(kRouterThreads)
     router_kernel(const RouterArgs a, uint64_t seq) {
   __shared__ float logit[kMaxRouterExperts];
+  __shared__ __align__(16) __nv_bfloat16 xs[kMaxRouterHidden];
   __shared__ float red[kRouterThreads / 32];
   __shared__ int top_id[kMaxRouterK];
   __shared__ float top_p[kMaxRouterK];
@@ -58,20 +59,35 @@ __global__ void __launch_bounds__(kRouterThreads)
     __syncthreads();
   } else {
   // ---- logits ----
+  // the token row once into shared memory; then each warp takes experts
+  // e = warp, warp + 32, ...; a lane issues all its 16-byte weight loads of
+  // an expert (8 at a time) before the FMAs, so loads overlap.
+  for (int v = threadIdx.x; v < H / 8; v += blockDim.x)
+    reinterpret_cast<uint4*>(xs)[v] = reinterpret_cast<const uint4*>(x)[v];
+  __syncthreads();
+  const int nch = H / 256;  // 16-byte chunks per lane
   for (int e = warp; e < E; e += nw) {
     const __nv_bfloat16* w = a.gate + (size_t)e * H;
     float acc = 0.0f;
-    for (int c = lane * 8; c < H; c += 32 * 8) {
-      const uint4 xv = *reinterpret_cast<const uint4*>(x + c);
-      const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
-      const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv);
-      const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    for (int c0 = 0; c0 < nch; c0 += 8) {
+      uint4 wv[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 xf = __bfloat1622float2(xp[q]);
-        const float2 wf = __bfloat1622float2(wp[q]);
-        acc = fmaf(xf.x, wf.x, acc);
-        acc = fmaf(xf.y, wf.y, acc);
+      for (int q = 0; q < 8; ++q)
+        if (c0 + q < nch) wv[q] = *reinterpret_cast<const uint4*>(w + (c0 + q) * 256 + lane * 8);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (c0 + q < nch) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(xs + (c0 + q) * 256 + lane * 8);
+          const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv);
+          const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wv[q]);
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float2 xf = __bfloat1622float2(xp[h]);
+            const float2 wf = __bfloat1622float2(wp[h]);
+            acc = fmaf(xf.x, wf.x, acc);
+            acc = fmaf(xf.y, wf.y, acc);
+          }
+        }
       }
     }
 #pragma unroll
@@ -171,34 +187,39 @@ __global__ void __launch_bounds__(kRouterThreads)
     base[a.off_ids + ((size_t)a.rank * a.tokens_per_rank + t) * K + j] = (uint8_t)top_id[j];
   }
   // ---- last CTA: histogram + flags ----
-  __threadfence_system();
+  // One system-scope fence per CTA, by thread 0 after a CTA barrier (the
+  // barrier orders the CTA's peer stores before it), then the done counter.
   __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(a.done, 1u) == (unsigned)gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    is_last = atomicAdd(a.done, 1u) == (unsigned)gridDim.x - 1;
+  }
   __syncthreads();
   if (!is_last) return;
-  __threadfence();
   for (int i = threadIdx.x; i < a.world * E; i += blockDim.x) {
     const int p = i / E, e = i % E;
     uint8_t* base = reinterpret_cast<uint8_t*>(a.peer_base[p]) + a.parity * a.buf_stride;
     reinterpret_cast<int*>(base + a.off_hist)[(size_t)a.rank * E + e] =
         atomicAdd(&a.hist_local[e], 0);
   }
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x < a.world) {
-    uint8_t* base = reinterpret_cast<uint8_t*>(a.peer_base[threadIdx.x]) + a.parity * a.buf_stride;
-    st_release_sys(reinterpret_cast<uint64_t*>(base + a.off_flag) + a.rank, seq);
+  for (int e = threadIdx.x; e < E; e += blockDim.x) a.hist_local[e] = 0;  // next layer
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < a.world; ++p) {
+      uint8_t* base = reinterpret_cast<uint8_t*>(a.peer_base[p]) + a.parity * a.buf_stride;
+      st_release_sys(reinterpret_cast<uint64_t*>(base + a.off_flag) + a.rank, seq);
+    }
+    *a.done = 0;
   }
-  __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) a.hist_local[e] = 0;  // ready for the next layer
-  if (threadIdx.x == 0) *a.done = 0;
 }
 
 int router_launch(const RouterArgs& a, uint64_t seq, cudaStream_t stream) {
   FB_CHECK_ARG(a.experts >= 1 && a.experts <= kMaxRouterExperts, "router: experts must be <= %d",
                kMaxRouterExperts);
   FB_CHECK_ARG(a.topk >= 1 && a.topk <= kMaxRouterK && a.topk <= a.experts, "router: bad topk");
-  FB_CHECK_ARG(a.hdim % 256 == 0, "router: hidden must be a multiple of 256");
+  FB_CHECK_ARG(a.hdim % 256 == 0 && a.hdim <= kMaxRouterHidden,
+               "router: hidden must be a multiple of 256 and at most %d", kMaxRouterHidden);
   FB_CHECK_ARG(a.world * a.topk <= kRouterThreads, "router: world * topk too large");
   if (a.tokens_per_rank == 0) return FERRYB_OK;
   router_kernel<<<a.tokens_per_rank, kRouterThreads, 0, stream>>>(a, seq);

@@ -8,6 +8,7 @@ namespace ferryb {
 
 constexpr int kMaxRouterExperts = 256;
 constexpr int kMaxRouterK = 16;
+constexpr int kMaxRouterHidden = 8192;
 
 struct RouterArgs {
   int world, rank, tokens_per_rank, topk, hdim, experts, parity;

@@ -167,6 +167,12 @@ FERRYB_API int ferryb_choose_slot(int32_t rank, int32_t layer, const uint8_t* ac
                                   const int64_t* last, const float* scores, int32_t experts,
                                   int64_t* result, ferryb_stream_t stream);
 
+/* Profiling aid: when dev_ptr (device, 8 x uint64) is not NULL the planner
+ * writes %globaltimer stamps of its phases there (0 start, 1 gate scores,
+ * 2 demand/misses/capacity, 3 quota + assignment, 4 victim records, 5 sort,
+ * 6 commit, 7 end).  NULL turns it off. */
+FERRYB_API int ferryb_debug_plan_timestamps(void* dev_ptr);
+
 /* ------------------------------------------------------------------------
  * EP layout of one layer for one rank.  Replaces build_layout and
  * device_layout (ferry/layout.py:12-94; no blocking H2D) and layer_slots
@@ -188,6 +194,8 @@ typedef struct ferryb_layout_args {
   const int32_t* fetches;    /* planner output or NULL */
   const int32_t* n_fetches;  /* planner output or NULL */
   const int32_t* layer_slot; /* [experts] slot of each expert on this rank, or NULL */
+  const int32_t* slots_row;  /* this rank's cache slots (computes layer_slot in-kernel), or NULL */
+  int32_t slots_count, layer;
   int64_t* send_idx;         /* [T*world] */
   int64_t* send_ids;         /* [T*world, topk], -1 padded */
   int64_t* send_counts;      /* [world] */
