@@ -67,6 +67,7 @@ SIGNATURES = {
     'ferryb_last_error': (ctypes.c_char_p, []),
     'ferryb_version': (_i32, []),
     'ferryb_device_sm_count': (_i32, [_i32]),
+    'ferryb_stream_mem_ops_supported': (_i32, [_i32]),
     'ferryb_execute_experts_workspace': (_i64, [_i64, _i64, _i64, _i64]),
     'ferryb_execute_experts': (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp,
                                       _i64, _i64, _vp, _vp, _i64, _vp]),
@@ -82,6 +83,7 @@ SIGNATURES = {
     'ferryb_layer_slots': (_i32, [_vp, _i32c, _i32c, _i32c, _vp, _vp]),
     'ferryb_h2d_create': (_i32, [_vp, _i64, _i64, _vp, _i64, _i32c, ctypes.POINTER(_vp)]),
     'ferryb_h2d_fetch': (_i32, [_vp, _vp, _vp, _i64]),
+    'ferryb_h2d_fetch_flagged': (_i32, [_vp, _vp, _vp, _i64, _vp, ctypes.c_uint32]),
     'ferryb_h2d_wait_host': (_i32, [_vp, _vp, _i64]),
     'ferryb_h2d_wait_device': (_i32, [_vp, _vp, _i64, _vp]),
     'ferryb_h2d_mark_used': (_i32, [_vp, _vp, _i64, _vp]),

@@ -57,7 +57,61 @@ int make_map_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
   return FERRYB_OK;
 }
 
+
+PFN_writeValue32 write_value32_fn() {
+  static PFN_writeValue32 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_writeValue32>(p);
+  });
+  return fn;
+}
+
+// Functional probe, once per device: a flag write by cuStreamWriteValue32 into
+// a 4-byte buffer of our own, read back after a stream synchronisation.  Any
+// failing call returns a status (the probe only touches its own memory).
+int stream_mem_ops_supported(int device) {
+  static int cached[64];
+  static bool done[64];
+  static std::mutex mu;
+  if (device < 0 || device >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[device]) return cached[device];
+  done[device] = true;
+  cached[device] = 0;
+  PFN_writeValue32 wv = write_value32_fn();
+  if (!wv) return 0;
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) return 0;
+  if (prev != device && cudaSetDevice(device) != cudaSuccess) return 0;
+  uint32_t* buf = nullptr;
+  cudaStream_t st = nullptr;
+  uint32_t host = 0;
+  int ok = 0;
+  if (cudaMalloc(&buf, sizeof(uint32_t)) == cudaSuccess &&
+      cudaMemset(buf, 0, sizeof(uint32_t)) == cudaSuccess &&
+      cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess &&
+      wv((CUstream)st, (CUdeviceptr)buf, 0x5a5a1234u, 0) == CUDA_SUCCESS &&
+      cudaStreamSynchronize(st) == cudaSuccess &&
+      cudaMemcpy(&host, buf, sizeof(uint32_t), cudaMemcpyDeviceToHost) == cudaSuccess)
+    ok = host == 0x5a5a1234u;
+  if (st) cudaStreamDestroy(st);
+  if (buf) cudaFree(buf);
+  if (prev != device) cudaSetDevice(prev);
+  cudaGetLastError();
+  cached[device] = ok;
+  return ok;
+}
+
 }  // namespace ferryb
+
+extern "C" int ferryb_stream_mem_ops_supported(int device) {
+  return ferryb::stream_mem_ops_supported(device);
+}
 
 extern "C" const char* ferryb_last_error(void) { return ferryb::g_error; }
 

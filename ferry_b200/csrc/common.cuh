@@ -64,6 +64,12 @@ typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_
                                     CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 PFN_encodeTiled encode_tiled_fn();
 
+// cuStreamWriteValue32 (a flag store executed by the stream's front end, no SM
+// needed) and whether the device supports stream memory operations.
+typedef CUresult (*PFN_writeValue32)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+PFN_writeValue32 write_value32_fn();
+int stream_mem_ops_supported(int device);
+
 // 2D bf16 tensor map over a row-major [rows, cols] matrix (cols contiguous),
 // box = [box_cols, box_rows], 128-byte swizzle (box_cols * 2 must be 128).
 int make_map_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,

@@ -295,6 +295,361 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Persistent fused kernel: both phases of every group in one launch.
+//
+// Work items are claimed in order from an atomic counter:
+//   cached groups' phase-1 tiles, cached groups' phase-2 tiles, then for each
+//   fetched group (in fetch order) its phase-1 tiles and its phase-2 tiles.
+// A phase-2 tile of group g starts when g's phase-1 tiles have all been
+// written (dep[g] counts epilogue warps), and a fetched group's tiles start
+// when its readiness flag has been raised (cuStreamWriteValue32 on the H2D
+// engine's flag stream once the group's copy has landed).  A
+// producer only waits on an item's dependencies after it has issued every
+// load of the items it claimed before, and every dependency belongs to an
+// earlier-claimed item or to an already-enqueued copy, so the grid (<= one
+// CTA per SM, all resident) always makes progress; each wait is bounded.
+struct FusedParams {
+  const GemmGroup* groups;
+  int n_groups, n_hit;
+  int mt1, mt2, kb1, kb2;
+  int rows1, up_off, rows2, down_off;
+  int inter, hidden;
+  __nv_bfloat16* act;
+  __nv_bfloat16* out;
+  const __nv_bfloat16* route_w;
+  const uint32_t* ready;  // [fetched] readiness flags, fetch order
+  uint32_t ready_value;
+  int* queue;  // [1] claim counter, zero at launch
+  int* dep;    // [n_groups] phase-1 epilogue-warp completions, zero at launch
+  int* err;
+};
+
+struct FusedItem {
+  int phase, group, tile, fetched;  // fetched: fetch index or -1
+};
+
+__device__ __forceinline__ FusedItem decode_item(const FusedParams& p, int item) {
+  FusedItem it;
+  const int per = p.mt1 + p.mt2;
+  const int h1 = p.n_hit * p.mt1, h2 = p.n_hit * per;
+  if (item < h1) {
+    it.phase = 1; it.group = item / p.mt1; it.tile = item % p.mt1; it.fetched = -1;
+  } else if (item < h2) {
+    const int i = item - h1;
+    it.phase = 2; it.group = i / p.mt2; it.tile = i % p.mt2; it.fetched = -1;
+  } else {
+    const int i = item - h2;
+    const int j = i / per, r = i % per;
+    it.group = p.n_hit + j;
+    it.fetched = j;
+    if (r < p.mt1) { it.phase = 1; it.tile = r; }
+    else { it.phase = 2; it.tile = r - p.mt1; }
+  }
+  return it;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_acquire_s32_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded spin until *flag >= value (readiness) / *cnt >= target (deps).
+__device__ bool spin_ready(const uint32_t* flag, uint32_t value, volatile int* abort_flag, int* err) {
+  if (ld_acquire_u32(flag) >= value) return true;
+  const uint64_t t0 = global_ns();
+  while (ld_acquire_u32(flag) < value) {
+    __nanosleep(128);
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitNs) { *abort_flag = 1; atomicCAS(err, 0, DEV_WAIT_TIMEOUT); return false; }
+  }
+  return true;
+}
+__device__ bool spin_count(const int* cnt, int target, volatile int* abort_flag, int* err) {
+  if (ld_acquire_s32_gpu(cnt) >= target) return true;
+  const uint64_t t0 = global_ns();
+  while (ld_acquire_s32_gpu(cnt) < target) {
+    __nanosleep(64);
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitNs) { *abort_flag = 1; atomicCAS(err, 0, DEV_WAIT_TIMEOUT); return false; }
+  }
+  return true;
+}
+
+constexpr int kSched = 4;           // claimed-item ring depth
+constexpr int kFusedStages = 4;
+constexpr uint32_t kFusedStageBytes = 2 * kTileBytesA + kTileBytesB;  // 48 KB
+constexpr uint32_t kFusedSmem = kFusedStages * kFusedStageBytes + 1024 + 512;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    swiglu_fused_kernel(const __grid_constant__ CUtensorMap w1, const __grid_constant__ CUtensorMap w2,
+                        const __grid_constant__ BMaps bx, const __grid_constant__ BMaps ba,
+                        const FusedParams p) {
+  constexpr int S = kFusedStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kFusedStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;     // [2]
+  uint64_t* tempty = tfull + 2;    // [2]
+  uint64_t* drain = tempty + 2;    // [1]
+  uint64_t* sfull = drain + 1;     // [kSched]
+  uint64_t* sempty = sfull + kSched;  // [kSched]
+  int* sched = reinterpret_cast<int*>(sempty + kSched);  // [kSched]
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(sched + kSched);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_items = p.n_groups * (p.mt1 + p.mt2);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
+    mbar_init(drain, 1);
+    for (int q = 0; q < kSched; ++q) { mbar_init(&sfull[q], 1); mbar_init(&sempty[q], 5); }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&w1);
+    tma_prefetch_desc(&w2);
+    for (int i = 0; i < 4; ++i) { tma_prefetch_desc(&bx.m[i]); tma_prefetch_desc(&ba.m[i]); }
+  }
+  if (warp == 1) { tmem_alloc(tmem_base_smem, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_smem;
+
+  if (warp == 0) {
+    // ---------------- scheduler + TMA producer ----------------
+    if (elect_one()) {
+      int stage = 0, q = 0;
+      uint32_t phase = 0, qphase = 0;
+      uint32_t pending = 0, pend_parity = 0;
+      bool ok = true;
+      for (;;) {
+        if (!wait_bounded(&sempty[q], qphase ^ 1, abort_flag, p.err)) { ok = false; break; }
+        int item = atomicAdd(p.queue, 1);
+        if (item >= n_items || *abort_flag) item = -1;
+        sched[q] = item;
+        mbar_arrive(&sfull[q]);
+        if (++q == kSched) { q = 0; qphase ^= 1; }
+        if (item < 0) break;
+        const FusedItem it = decode_item(p, item);
+        const GemmGroup g = p.groups[it.group];
+        // dependencies: copy readiness, then (phase 2) the group's phase-1 tiles
+        if (it.fetched >= 0 && !spin_ready(p.ready + it.fetched, p.ready_value, abort_flag, p.err)) {
+          ok = false; break;
+        }
+        if (it.phase == 2 && !spin_count(p.dep + it.group, 4 * p.mt1, abort_flag, p.err)) {
+          ok = false; break;
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        const int kb_n = it.phase == 1 ? p.kb1 : p.kb2;
+        const CUtensorMap* wm = it.phase == 1 ? &w1 : &w2;
+        const BMaps* bm = it.phase == 1 ? &bx : &ba;
+        const int row_a = it.phase == 1 ? g.slot * p.rows1 + it.tile * kBlockM
+                                        : g.slot * p.rows2 + p.down_off + it.tile * kBlockM;
+        const uint32_t a_bytes = (it.phase == 1 ? 2 : 1) * kTileBytesA;
+        const int chunks = (g.count + kMaxN - 1) / kMaxN;
+        for (int c = 0; c < chunks && ok; ++c) {
+          const int n_valid = min(kMaxN, g.count - c * kMaxN);
+          const int bi = box_index(n_valid);
+          const uint32_t b_bytes = (16u << bi) * kBlockK * 2;
+          const int row_b = g.start + c * kMaxN;
+          for (int kb = 0; kb < kb_n; ++kb) {
+            if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err)) { ok = false; break; }
+            uint8_t* st = smem + stage * kFusedStageBytes;
+            mbar_expect_tx(&full[stage], a_bytes + b_bytes);
+            tma_load_2d(st, wm, &full[stage], kb * kBlockK, row_a);
+            if (it.phase == 1) tma_load_2d(st + kTileBytesA, wm, &full[stage], kb * kBlockK, row_a + p.up_off);
+            tma_load_2d(st + 2 * kTileBytesA, &bm->m[bi], &full[stage], kb * kBlockK, row_b);
+            pending |= 1u << stage;
+            pend_parity = (pend_parity & ~(1u << stage)) | (phase << stage);
+            if (++stage == S) { stage = 0; phase ^= 1; }
+          }
+        }
+        if (!ok) break;
+      }
+      if (!ok) {
+        // consumers poll the abort flag in their bounded waits and stop
+        *abort_flag = 1;
+        const uint64_t t0 = global_ns();
+        for (int s2 = 0; s2 < S; ++s2)
+          if (pending & (1u << s2))
+            while (!mbar_try_wait(&full[s2], (pend_parity >> s2) & 1) && global_ns() - t0 < kWaitNs) {}
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (elect_one()) {
+      int stage = 0, acc = 0, q = 0;
+      uint32_t phase = 0, acc_phase = 0, qphase = 0;
+      bool ok = true;
+      for (;;) {
+        if (!wait_bounded(&sfull[q], qphase, abort_flag, p.err)) break;
+        const int item = sched[q];
+        mbar_arrive(&sempty[q]);
+        if (++q == kSched) { q = 0; qphase ^= 1; }
+        if (item < 0) break;
+        const FusedItem it = decode_item(p, item);
+        const GemmGroup g = p.groups[it.group];
+        const int kb_n = it.phase == 1 ? p.kb1 : p.kb2;
+        const int chunks = (g.count + kMaxN - 1) / kMaxN;
+        for (int c = 0; c < chunks && ok; ++c) {
+          const int n_valid = min(kMaxN, g.count - c * kMaxN);
+          const uint32_t n_mma = 16u << box_index(n_valid);
+          const uint32_t idesc = idesc_bf16_f32(kBlockM, n_mma);
+          if (!wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d0 = tmem_base + acc * 256;
+          const uint32_t d1 = d0 + 128;
+          for (int kb = 0; kb < kb_n; ++kb) {
+            if (!wait_bounded(&full[stage], phase, abort_flag, p.err)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t st = smem_u32(smem + stage * kFusedStageBytes);
+            const uint32_t sb = st + 2 * kTileBytesA;
+#pragma unroll
+            for (int k = 0; k < kBlockK / 16; ++k) {
+              const uint64_t bdesc = smem_desc_sw128(sb + k * 32);
+              const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+              umma_bf16(d0, smem_desc_sw128(st + k * 32), bdesc, idesc, accum);
+              if (it.phase == 1) umma_bf16(d1, smem_desc_sw128(st + kTileBytesA + k * 32), bdesc, idesc, accum);
+            }
+            umma_commit(&empty[stage]);
+            if (++stage == S) { stage = 0; phase ^= 1; }
+          }
+          if (!ok) break;
+          umma_commit(&tfull[acc]);
+          if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        }
+        if (!ok) break;
+      }
+      umma_commit(drain);
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain, 0) && global_ns() - t0 < kWaitNs) {}
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int qd = warp & 3;
+    int acc = 0, q = 0;
+    uint32_t acc_phase = 0, qphase = 0;
+    bool ok = true;
+    for (;;) {
+      if (!wait_bounded(&sfull[q], qphase, abort_flag, p.err)) break;
+      const int item = sched[q];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[q]);
+      if (++q == kSched) { q = 0; qphase ^= 1; }
+      if (item < 0) break;
+      const FusedItem it = decode_item(p, item);
+      const GemmGroup g = p.groups[it.group];
+      const int chunks = (g.count + kMaxN - 1) / kMaxN;
+      const int feature = it.tile * kBlockM + qd * 32 + lane;
+      const int out_cols = it.phase == 1 ? p.inter : p.hidden;
+      for (int c = 0; c < chunks; ++c) {
+        const int n_valid = min(kMaxN, g.count - c * kMaxN);
+        if (!wait_bounded(&tfull[acc], acc_phase, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d0 = tmem_base + (static_cast<uint32_t>(qd * 32) << 16) + acc * 256;
+        for (int c0 = 0; c0 < n_valid; c0 += 16) {
+          float v0[16];
+          tmem_ld16(d0 + c0, v0);
+          if (it.phase == 1) {
+            float v1[16];
+            tmem_ld16(d0 + 128 + c0, v1);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if (c0 + j < n_valid) {
+                const float gt = bf16_round(v0[j]);
+                const float up = bf16_round(v1[j]);
+                const float a = (gt / (1.0f + expf(-gt))) * up;
+                const size_t row = static_cast<size_t>(g.start + c * kMaxN + c0 + j);
+                p.act[row * out_cols + feature] = __float2bfloat16_rn(a);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if (c0 + j < n_valid) {
+                const size_t row = static_cast<size_t>(g.start + c * kMaxN + c0 + j);
+                float y = bf16_round(v0[j]);
+                if (p.route_w) y = y * __bfloat162float(p.route_w[row]);
+                p.out[row * out_cols + feature] = __float2bfloat16_rn(y);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      if (!ok) break;
+      if (it.phase == 1) {
+        // publish this warp's activations to the group's phase-2 tiles
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(p.dep + it.group, 1);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups, int n_hit,
+                        const uint32_t* ready, uint32_t ready_value, int* queue_dep,
+                        const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
+                        int* err, cudaStream_t stream) {
+  if (n_groups == 0) return FERRYB_OK;
+  int device = 0;
+  FB_CUDA(cudaGetDevice(&device));
+  FusedParams p{};
+  p.groups = groups;
+  p.n_groups = n_groups;
+  p.n_hit = n_hit;
+  p.mt1 = static_cast<int>(m.inter / kBlockM);
+  p.mt2 = static_cast<int>(m.hidden / kBlockM);
+  p.kb1 = static_cast<int>(m.hidden / kBlockK);
+  p.kb2 = static_cast<int>(m.inter / kBlockK);
+  p.rows1 = static_cast<int>(3 * m.inter);
+  p.up_off = static_cast<int>(m.inter);
+  p.rows2 = static_cast<int>(3 * m.hidden);
+  p.down_off = static_cast<int>(2 * m.hidden);
+  p.inter = static_cast<int>(m.inter);
+  p.hidden = static_cast<int>(m.hidden);
+  p.act = act;
+  p.out = out;
+  p.route_w = route_w;
+  p.ready = ready;
+  p.ready_value = ready_value;
+  p.queue = queue_dep;
+  p.dep = queue_dep + 1;
+  p.err = err;
+  FB_CUDA(cudaMemsetAsync(queue_dep, 0, sizeof(int) * (1 + n_groups), stream));
+  const int items = n_groups * (p.mt1 + p.mt2);
+  const int grid = items < num_sms(device) ? items : num_sms(device);
+  FB_CUDA(cudaFuncSetAttribute(swiglu_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kFusedSmem));
+  swiglu_fused_kernel<<<grid, kThreads, kFusedSmem, stream>>>(m.w1, m.w2, m.bx, m.ba, p);
+  FB_LAUNCH_CHECK();
+  return FERRYB_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Gather of the routed rows into X (one row per route, grouped) and of their
 // routing weights: X[p] = input[rows[p]], W[p] = routing_weights[rows[p], cols[p]].
 __global__ void gather_routes_kernel(const __nv_bfloat16* __restrict__ input, int64_t n_input,

@@ -21,6 +21,7 @@ struct ferryb_h2d {
   const uint8_t* pool = nullptr;
   int64_t pool_rows = 0;
   std::vector<cudaStream_t> streams;
+  cudaStream_t flag_stream = nullptr;  // raises readiness flags after copies
   std::vector<cudaEvent_t> copy_done, used;
   std::vector<char> used_valid;
   int64_t copies = 0;
@@ -71,6 +72,10 @@ extern "C" int ferryb_h2d_create(void* cache, int64_t cache_slots, int64_t row_b
       delete h;
       return fail(FERRYB_ECUDA, "h2d_create: cudaStreamCreate failed");
     }
+  }
+  if (cudaStreamCreateWithFlags(&h->flag_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete h;
+    return fail(FERRYB_ECUDA, "h2d_create: cudaStreamCreate failed");
   }
   h->copy_done.resize(cache_slots);
   h->used.resize(cache_slots);
@@ -140,6 +145,7 @@ extern "C" int ferryb_h2d_mark_used(ferryb_h2d* h, const int64_t* slots, int64_t
 extern "C" int ferryb_h2d_synchronize(ferryb_h2d* h) {
   FB_CHECK_ARG(h, "h2d_synchronize: NULL engine");
   for (auto s : h->streams) FB_CUDA(cudaStreamSynchronize(s));
+  FB_CUDA(cudaStreamSynchronize(h->flag_stream));
   return FERRYB_OK;
 }
 
@@ -152,8 +158,42 @@ extern "C" int ferryb_h2d_destroy(ferryb_h2d* h) {
     cudaStreamSynchronize(s);
     cudaStreamDestroy(s);
   }
+  if (h->flag_stream) {
+    cudaStreamSynchronize(h->flag_stream);
+    cudaStreamDestroy(h->flag_stream);
+  }
   for (auto e : h->copy_done) cudaEventDestroy(e);
   for (auto e : h->used) cudaEventDestroy(e);
   delete h;
+  return FERRYB_OK;
+}
+
+// Copies with readiness flags for a kernel that waits on the device: fetch i
+// copies its whole row on a copy stream and records the slot's copy event; a
+// separate flag stream waits for that event and stores flags[i] = value with
+// cuStreamWriteValue32 (a stream memory operation with a memory barrier, run
+// by the stream's front end, so no SM is involved).  Keeping the flag stores
+// off the copy stream leaves the copies back to back.
+extern "C" int ferryb_h2d_fetch_flagged(ferryb_h2d* h, const int64_t* slots, const int64_t* keys,
+                                        int64_t n, uint32_t* flags, uint32_t value) {
+  FB_CHECK_ARG(h && (n == 0 || (slots && keys && flags)), "h2d_fetch_flagged: bad arguments");
+  PFN_writeValue32 wv = write_value32_fn();
+  if (!wv) return fail(FERRYB_ECUDA, "cuStreamWriteValue32 is unavailable");
+  DeviceGuard g(h->device);
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t slot = slots[i], key = keys[i];
+    FB_CHECK_ARG(slot >= 0 && slot < h->cache_slots, "h2d_fetch_flagged: slot out of range");
+    FB_CHECK_ARG(key >= 0, "h2d_fetch_flagged: negative key");
+    cudaStream_t s = h->streams[h->next_stream++ % h->streams.size()];
+    if (h->used_valid[slot]) FB_CUDA(cudaStreamWaitEvent(s, h->used[slot], 0));
+    FB_CUDA(cudaMemcpyAsync(h->cache + slot * h->row_bytes,
+                            h->pool + (key % h->pool_rows) * h->row_bytes, h->row_bytes,
+                            cudaMemcpyHostToDevice, s));
+    FB_CUDA(cudaEventRecord(h->copy_done[slot], s));
+    FB_CUDA(cudaStreamWaitEvent(h->flag_stream, h->copy_done[slot], 0));
+    if (wv((CUstream)h->flag_stream, (CUdeviceptr)(flags + i), value, 0) != CUDA_SUCCESS)
+      return fail(FERRYB_ECUDA, "cuStreamWriteValue32 failed");
+    ++h->copies;
+  }
   return FERRYB_OK;
 }

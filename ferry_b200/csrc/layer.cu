@@ -60,6 +60,8 @@ struct ferryb_layer {
   int64_t* selected;
   int* hist_local;
   unsigned* done;
+  uint32_t* ready;  // [experts] copy readiness flags (monotonic sequence numbers)
+  int* queue_dep;   // [1 + experts] GEMM work counter + phase-1 completions
   // host side
   ferryb_layout_summary* summary_host = nullptr;
   int32_t* errs_host = nullptr;  // pinned copy of the device error words
@@ -163,6 +165,8 @@ static int64_t workspace_bytes(const ferryb_layer_config& c, uint8_t* base, ferr
     auto hist_local = cv.take<int>(E);
     auto done = cv.take<unsigned>(1);
     auto peer_base = cv.take<uintptr_t>(R);
+    auto ready = cv.take<uint32_t>(2 * E);
+    auto queue_dep = cv.take<int>(1 + E);
     if (L) {
       L->dest = dest; L->fetches = fetches; L->n_fetches = n_fetches; L->counts = counts;
       L->errs = errs; L->layer_slot = layer_slot; L->send_idx = send_idx; L->send_ids = send_ids;
@@ -173,6 +177,8 @@ static int64_t workspace_bytes(const ferryb_layer_config& c, uint8_t* base, ferr
       L->expert_out = expert_out; L->route_w = route_w; L->weights = weights;
       L->selected = selected; L->hist_local = hist_local; L->done = done;
       L->peer_base_dev = peer_base;
+      L->ready = ready;
+      L->queue_dep = queue_dep;
     }
   });
 }
@@ -203,6 +209,13 @@ extern "C" int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_
                "layer_create: workspace too small");
   FB_CHECK_ARG((cfg->probability_score != 0) == (planner->ring_p != nullptr),
                "layer_create: probability score needs the planner's probability ring");
+  {
+    int device = 0;
+    FB_CUDA(cudaGetDevice(&device));
+    FB_CHECK_ARG(stream_mem_ops_supported(device),
+                 "layer_create: the device lacks stream memory operations (cuStreamWriteValue32), "
+                 "which the per-copy readiness flags need");
+  }
   auto* L = new ferryb_layer();
   L->cfg = *cfg;
   L->planner = *planner;
@@ -383,14 +396,17 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
       return fail(FERRYB_ETIMEOUT, "timed out waiting for the routing metadata of a peer rank");
     return fail(FERRYB_EDEVICE, "planner/layout device error %d/%d", plan_err, sum.err);
   }
-  // 5 fetches (copy engines)
+  // 5 fetches on the copy engine, each raising a readiness flag when it has
+  //   landed; the first goes out before the compute-stream launches
   std::vector<int64_t> fslots(sum.n_fetch_mine), fkeys(sum.n_fetch_mine);
   for (int i = 0; i < sum.n_fetch_mine; ++i) {
     fslots[i] = sum.fetch_slots[i];
     fkeys[i] = sum.fetch_keys[i];
   }
-  if (sum.n_fetch_mine) {
-    if ((s = ferryb_h2d_fetch(L->h2d, fslots.data(), fkeys.data(), sum.n_fetch_mine))) return s;
+  const uint32_t ready_value = (uint32_t)seq;
+  if (sum.n_fetch_mine > 0) {
+    if ((s = ferryb_h2d_fetch_flagged(L->h2d, fslots.data(), fkeys.data(), 1, L->ready, ready_value)))
+      return s;
   }
 
   // 6-7 dispatch + permute
@@ -401,18 +417,23 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   launches += 2 + (c.world > 1 ? 1 : 0);  // dispatch (+ signal) + permute
   if (timing) FB_CUDA(cudaEventRecord(L->tev[2], stream));
 
-  // 8 grouped SwiGLU: cached experts, then each fetched expert after its copy
-  if ((s = swiglu_grouped_maps(L->maps, L->groups, sum.n_hit, L->route_w, L->act,
-                               L->expert_out, L->errs + 2, stream)))
+  // 8 grouped SwiGLU (kernel 5), both phases per launch: the experts cached
+  //   before this layer (no waits), then the fetched experts, whose tiles
+  //   start as their readiness flags arrive
+  if ((s = swiglu_fused_launch(L->maps, L->groups, sum.n_hit, sum.n_hit, nullptr, 0, L->queue_dep,
+                               L->route_w, L->act, L->expert_out, L->errs + 2, stream)))
     return s;
-  if (sum.n_hit) launches += 2;
+  if (sum.n_hit) launches += 1;
   if (timing) FB_CUDA(cudaEventRecord(L->tev[3], stream));
-  for (int i = 0; i < sum.n_fetch_mine; ++i) {
-    if ((s = ferryb_h2d_wait_device(L->h2d, &fslots[i], 1, stream))) return s;
-    if ((s = swiglu_grouped_maps(L->maps, L->groups + sum.n_hit + i, 1, L->route_w, L->act,
-                                 L->expert_out, L->errs + 2, stream)))
+  if ((s = swiglu_fused_launch(L->maps, L->groups + sum.n_hit, sum.n_fetch_mine, 0, L->ready,
+                               ready_value, L->queue_dep, L->route_w, L->act, L->expert_out,
+                               L->errs + 2, stream)))
+    return s;
+  if (sum.n_fetch_mine) launches += 1;
+  if (sum.n_fetch_mine > 1) {
+    if ((s = ferryb_h2d_fetch_flagged(L->h2d, fslots.data() + 1, fkeys.data() + 1,
+                                      sum.n_fetch_mine - 1, L->ready + 1, ready_value)))
       return s;
-    launches += 2;
   }
   if (timing) FB_CUDA(cudaEventRecord(L->tev[4], stream));
 

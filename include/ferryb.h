@@ -53,6 +53,9 @@ typedef struct CUstream_st* ferryb_stream_t; /* == cudaStream_t */
 FERRYB_API const char* ferryb_last_error(void);
 FERRYB_API int ferryb_version(void);
 FERRYB_API int ferryb_device_sm_count(int device);
+/* 1 if the device supports stream memory operations (cuStreamWriteValue32),
+ * which the H2D engine uses to raise per-copy readiness flags. */
+FERRYB_API int ferryb_stream_mem_ops_supported(int device);
 
 /* ------------------------------------------------------------------------
  * Kernel 5: routed-expert SwiGLU grouped GEMM (tcgen05 / TMEM / TMA).
@@ -235,6 +238,12 @@ FERRYB_API int ferryb_h2d_create(void* cache, int64_t cache_slots, int64_t row_b
                                  ferryb_h2d** out);
 FERRYB_API int ferryb_h2d_fetch(ferryb_h2d* h2d, const int64_t* slots, const int64_t* keys,
                                 int64_t n);
+/* Fetch with device-side readiness flags (flags: device uint32, one per
+ * fetch): once fetch i's copy has landed, flags[i] = value is stored by the
+ * engine's flag stream (stream memory operation).  Needs
+ * ferryb_stream_mem_ops_supported. */
+FERRYB_API int ferryb_h2d_fetch_flagged(ferryb_h2d* h2d, const int64_t* slots, const int64_t* keys,
+                                        int64_t n, uint32_t* flags, uint32_t value);
 FERRYB_API int ferryb_h2d_wait_host(ferryb_h2d* h2d, const int64_t* slots, int64_t n);
 FERRYB_API int ferryb_h2d_wait_device(ferryb_h2d* h2d, const int64_t* slots, int64_t n,
                                       ferryb_stream_t stream);
