@@ -71,6 +71,9 @@ SIGNATURES = {
     'ferryb_execute_experts_workspace': (_i64, [_i64, _i64, _i64, _i64]),
     'ferryb_execute_experts': (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp,
                                       _i64, _i64, _vp, _vp, _i64, _vp]),
+    'ferryb_execute_experts_noalloc_limit': (_i64, []),
+    'ferryb_execute_experts_noalloc': (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp,
+                                              _vp, _i64, _i64, _vp, _vp]),
     'ferryb_plan_layer': (_i32, [ctypes.POINTER(Planner), _i64, _i32c, _vp, _i32c, _i32c, _vp, _vp,
                                  _vp, _i32c, _vp, _vp, _vp, _vp, _vp, _vp]),
     'ferryb_greedy_quota_rows': (_i32, [_i32c, _vp, _vp, _i32c, _vp, _i32c, _i32c, _vp, _vp, _vp]),

@@ -30,6 +30,7 @@
 // full/empty mbarriers; TMEM holds two accumulator buffers so the epilogue of
 // one tile overlaps the MMAs of the next.  The grid is persistent (<= #SMs).
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -846,5 +847,106 @@ extern "C" int ferryb_execute_experts(const void* cache, int64_t cache_slots, co
   FB_CUDA(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, stream));
   FB_CUDA(cudaStreamSynchronize(stream));
   if (h_err) return fail(FERRYB_EDEVICE, "execute_experts: device error %d", h_err);
+  return FERRYB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// execute_experts without any allocation: the scratch (gathered rows,
+// activations, route weights, group table, error word) lives in a fixed
+// array inside this library instead of a caller-provided workspace.  For
+// callers that cannot allocate device memory at all -- for example a host
+// application that has already handed the whole GPU to its own memory pool,
+// or a plugin reached through a C binding (cgo, JNI) with no device
+// allocator of its own.
+namespace ferryb {
+
+// 4 MiB per GPU, held for the life of the process by every process that loads
+// the library (the cost of offering this entry point).
+constexpr int64_t kNoAllocScratchBytes = int64_t(4) << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// In host code `g_noalloc_scratch` only names the symbol; its device address
+// is looked up once per device, with that device current.
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[64] = {};
+
+static int noalloc_scratch(void** out) {
+  int device = 0;
+  FB_CUDA(cudaGetDevice(&device));
+  FB_CHECK_ARG(device >= 0 && device < 64, "execute_experts_noalloc: device index %d", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    FB_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_addr[device] = p;
+  }
+  *out = g_noalloc_addr[device];
+  return FERRYB_OK;
+}
+
+}  // namespace ferryb
+
+extern "C" int64_t ferryb_execute_experts_noalloc_limit(void) { return ferryb::kNoAllocScratchBytes; }
+
+extern "C" int ferryb_execute_experts_noalloc(const void* cache, int64_t cache_slots,
+                                              const void* input, int64_t n_input,
+                                              const void* routing_weights, int64_t topk,
+                                              const int64_t* slots, const int64_t* group_sizes,
+                                              int64_t n_groups, const int64_t* rows,
+                                              const int64_t* cols, int64_t hidden,
+                                              int64_t intermediate, void* out,
+                                              cudaStream_t stream) {
+  constexpr int64_t kMaxGroups = 1024;
+  FB_CHECK_ARG(n_groups >= 0 && n_groups <= kMaxGroups && hidden > 0 && intermediate > 0,
+               "execute_experts_noalloc: bad sizes (at most %lld groups)", (long long)kMaxGroups);
+  FB_CHECK_ARG(n_groups == 0 || (slots && group_sizes), "slots/group_sizes required");
+  GemmGroup host_groups[kMaxGroups];  // on the stack: no heap allocation either
+  int64_t total = 0;
+  for (int64_t i = 0; i < n_groups; ++i) {
+    FB_CHECK_ARG(slots[i] >= 0 && slots[i] < cache_slots, "slot %lld out of range [0, %lld)",
+                 (long long)slots[i], (long long)cache_slots);
+    FB_CHECK_ARG(group_sizes[i] >= 0, "negative group size");
+    host_groups[i] = GemmGroup{static_cast<int32_t>(slots[i]), static_cast<int32_t>(total),
+                               static_cast<int32_t>(group_sizes[i]), static_cast<int32_t>(i)};
+    total += group_sizes[i];
+  }
+  if (total == 0) return FERRYB_OK;
+  FB_CHECK_ARG(cache && input && routing_weights && rows && cols && out, "null pointer");
+  const ExecWs ws = exec_ws(total, n_groups, hidden, intermediate);
+  if (ws.total > kNoAllocScratchBytes)
+    return fail(FERRYB_EINVAL,
+                "execute_experts_noalloc: %lld routes of hidden %lld / intermediate %lld need "
+                "%lld bytes of scratch, above the fixed %lld; use ferryb_execute_experts with a "
+                "workspace",
+                (long long)total, (long long)hidden, (long long)intermediate, (long long)ws.total,
+                (long long)kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  int s = noalloc_scratch(&scratch);
+  if (s) return s;
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  auto* x = reinterpret_cast<__nv_bfloat16*>(base + ws.x);
+  auto* act = reinterpret_cast<__nv_bfloat16*>(base + ws.act);
+  auto* w = reinterpret_cast<__nv_bfloat16*>(base + ws.w);
+  auto* groups = reinterpret_cast<GemmGroup*>(base + ws.groups);
+  int* err = reinterpret_cast<int*>(base + ws.err);
+  // the array keeps the previous call's contents: the error word starts at zero
+  FB_CUDA(cudaMemsetAsync(err, 0, sizeof(int), stream));
+  FB_CUDA(cudaMemcpyAsync(groups, host_groups, n_groups * sizeof(GemmGroup),
+                          cudaMemcpyHostToDevice, stream));
+  const int64_t work = total * (hidden / 8);
+  int blocks = static_cast<int>((work + 255) / 256);
+  if (blocks > 4096) blocks = 4096;
+  gather_routes_kernel<<<blocks, 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(input), n_input,
+      static_cast<const __nv_bfloat16*>(routing_weights), topk, rows, cols, total, hidden, x, w,
+      err);
+  FB_LAUNCH_CHECK();
+  s = swiglu_grouped(cache, cache_slots, groups, static_cast<int>(n_groups), total, x, w, act,
+                     static_cast<__nv_bfloat16*>(out), hidden, intermediate, err, stream);
+  if (s) return s;
+  int h_err = 0;
+  FB_CUDA(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  FB_CUDA(cudaStreamSynchronize(stream));
+  if (h_err) return fail(FERRYB_EDEVICE, "execute_experts_noalloc: device error %d", h_err);
   return FERRYB_OK;
 }

@@ -86,6 +86,28 @@ FERRYB_API int ferryb_execute_experts(const void* cache, int64_t cache_slots, co
                            int64_t workspace_bytes, ferryb_stream_t stream);
 
 
+/* The same computation as ferryb_execute_experts for callers that cannot
+ * allocate device memory (a host that has already given the whole GPU to its
+ * own memory pool, or a plugin reached through a C binding with no device
+ * allocator).  No counterpart in the reference.  Its scratch is a fixed
+ * 4 MiB array inside this library (ferryb_execute_experts_noalloc_limit()
+ * bytes), which every process that loads the library holds on each GPU it
+ * uses until exit; calls whose rows, activations and tables need more
+ * return FERRYB_EINVAL.  Nothing is allocated: no cudaMalloc/cudaFree.
+ * All calls share that array: calls that overlap on the GPU (other streams
+ * or threads) race.  The first call on a device looks the array up
+ * (cudaGetSymbolAddress) and should come before any stream capture.
+ * Synchronises `stream` before returning, like ferryb_execute_experts. */
+FERRYB_API int64_t ferryb_execute_experts_noalloc_limit(void);
+FERRYB_API int ferryb_execute_experts_noalloc(const void* cache, int64_t cache_slots,
+                                              const void* input, int64_t n_input,
+                                              const void* routing_weights, int64_t topk,
+                                              const int64_t* slots, const int64_t* group_sizes,
+                                              int64_t n_groups, const int64_t* rows,
+                                              const int64_t* cols, int64_t hidden,
+                                              int64_t intermediate, void* out,
+                                              ferryb_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Kernel 2: placement planner (one CTA, bit-exact with the reference).
  * Replaces Controller.plan -> plan_layer (ferry/policy.py:130-194, :208-228)
