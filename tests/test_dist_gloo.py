@@ -1,0 +1,143 @@
+"""Multi-process CPU tests of the N > 1 path over gloo (no GPU).
+
+a DeepSeek-V2-Lite-shaped MoE layer (hidden 2048, 64
+experts top-6, intermediate 1408) run by 4 gloo ranks with 16 tokens each for
+8 consecutive steps, through the reference's distributed flow restated in
+oracle/dist_layer.py; every rank's output must match what the single-process
+emulation (oracle/layer.py) computes for that rank within the BF16 tolerance
+(CPU GEMM rounding depends on the thread count), and every rank must reach
+identical cache decisions.  A world-size-2 run checks the same at a smaller
+shape, plus the symmetric-buffer handle exchange of ferry_b200.symm.
+"""
+import os
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import expert_ops as ops
+from oracle import planner as op
+from oracle.layer import OracleRuntime
+from tests.tolerance import assert_bf16_close
+
+
+class _Spec:
+    def __init__(self, layers, experts, topk, hidden, inter):
+        self.layers, self.experts, self.topk = layers, experts, topk
+        self.hidden, self.intermediate = hidden, inter
+        self.expert_elements = 3 * hidden * inter
+
+
+def _setup(spec, seed, world):
+    g = torch.Generator().manual_seed(seed)
+    pool = (torch.randn(spec.layers * spec.experts, spec.expert_elements, generator=g) * 0.02).to(torch.bfloat16)
+    gates = [(torch.randn(spec.experts, spec.hidden, generator=g) * 0.02).to(torch.bfloat16)
+             for _ in range(spec.layers)]
+    from ferry_b200.workload import zipf_bias
+    biases = [zipf_bias(spec.experts, 1.1, g) for _ in range(spec.layers)]
+    return pool, gates, biases
+
+
+def _inputs(spec, step, rank, T, gates, biases):
+    g = torch.Generator().manual_seed(1000 * step + rank)
+    x = torch.randn(T, spec.hidden, generator=g).to(torch.bfloat16)
+    layer = step % spec.layers
+    sel, w, _ = ops.route_deepseek(x, gates[layer].float(), spec.topk, 1.0, biases[layer])
+    return layer, x, sel, w
+
+
+def _worker(rank, world, port, shape, caps, steps, T, out_dir):
+    import torch.distributed as dist
+    from oracle.dist_layer import DistOracleRuntime
+    torch.set_num_threads(2)
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    spec = _Spec(*shape)
+    pool, gates, biases = _setup(spec, 0, world)
+    masks = np.asarray([1 << r for r in range(world)], np.int64)
+    lut = op.build_lut(spec.experts, world, masks, np.ones(world))
+    rt = DistOracleRuntime(spec, pool, caps, 'ferry', masks, np.ones(world), lut)
+    outs = []
+    for step in range(steps):
+        layer, x, sel, w = _inputs(spec, step, rank, T, gates, biases)
+        y, _ = rt.execute(layer, x, sel, w)
+        outs.append(y)
+    torch.save({'outs': outs, 'slots': rt.ctl.slots, 'owner': rt.ctl.owner},
+               os.path.join(out_dir, f'rank{rank}.pt'))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _run(world, shape, caps, steps, T, port):
+    spec = _Spec(*shape)
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_worker, args=(world, port, shape, caps, steps, T, tmp), nprocs=world)
+        res = [torch.load(os.path.join(tmp, f'rank{r}.pt'), weights_only=False) for r in range(world)]
+    pool, gates, biases = _setup(spec, 0, world)
+    masks = np.asarray([1 << r for r in range(world)], np.int64)
+    lut = op.build_lut(spec.experts, world, masks, np.ones(world))
+    orc = OracleRuntime(spec, pool, caps, 'ferry', masks, np.ones(world), lut)
+    for step in range(steps):
+        per = [_inputs(spec, step, r, T, gates, biases) for r in range(world)]
+        want, _, _ = orc.execute(per[0][0], [p[1] for p in per], [p[2] for p in per], [p[3] for p in per])
+        for r in range(world):  # CPU GEMMs differ in rounding with the thread count
+            assert_bf16_close(res[r]['outs'][step], want[r], f'step {step} rank {r}')
+    for r in range(world):
+        np.testing.assert_array_equal(res[r]['slots'], orc.ctl.slots)
+        np.testing.assert_array_equal(res[r]['owner'], orc.ctl.owner)
+
+
+def test_config0_world4_gloo():
+    """DSV2-Lite layer, 4 gloo ranks x 16 tokens, 8 steps,
+    global 30 % cache of a 2-layer slice (38 slots -> 10/10/9/9)."""
+    _run(4, (2, 64, 6, 2048, 1408), [10, 10, 9, 9], 8, 16, 29651)
+
+
+def test_world2_gloo_small():
+    _run(2, (2, 16, 4, 128, 64), [6, 5], 6, 8, 29652)
+
+
+def _symm_worker(rank, world, port, out_dir):
+    """The IPC-handle exchange of ferry_b200.symm over gloo, with the CUDA
+    calls replaced by stand-ins (no GPU here)."""
+    import ctypes
+    import torch.distributed as dist
+    from ferry_b200 import symm
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    opened = []
+
+    def fake_call(name, *args):
+        if name == 'ferryb_symm_alloc':
+            args[1]._obj.value = 0x1000 * (rank + 1)
+            if args[2] is not None:
+                for i in range(64):
+                    args[2][i] = (rank * 7 + i) & 0xff
+        elif name == 'ferryb_symm_open':
+            handle = bytes(args[0])
+            args[1]._obj.value = 0x100000 + handle[0]
+            opened.append(handle[0])
+        return 0
+
+    symm.call = fake_call
+    buf = symm.SymmetricBuffer(4096, rank, world)
+    bases = list(buf.bases)
+    buf._opened = []
+    buf.local = None
+    torch.save({'bases': bases, 'opened': opened}, os.path.join(out_dir, f's{rank}.pt'))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_symmetric_handle_exchange_world2():
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_symm_worker, args=(2, 29653, tmp), nprocs=2)
+        res = [torch.load(os.path.join(tmp, f's{r}.pt')) for r in range(2)]
+    # rank r keeps its own address and maps the peer's handle (first byte = peer * 7)
+    assert res[0]['bases'][0] == 0x1000 and res[1]['bases'][1] == 0x2000
+    assert res[0]['opened'] == [7] and res[1]['opened'] == [0]
+    assert res[0]['bases'][1] == 0x100000 + 7 and res[1]['bases'][0] == 0x100000

@@ -1,0 +1,98 @@
+"""The multi-GPU path (P2P all-gather, dispatch and combine over NVSwitch,
+replicated device planner) on 2 GPUs: one process per GPU runs
+OffloadRuntime.execute; the oracle emulates the same ranks in one process.
+Cache decisions bit-exact on every rank, outputs within the BF16 tolerance.
+Needs 2 GPUs (gpurun --gpus 2); skipped otherwise."""
+import os
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import expert_ops as ref_ops
+from oracle.layer import OracleRuntime
+from tests.tolerance import assert_bf16_close
+
+pytestmark = pytest.mark.gpu
+
+CASES = {
+    'small': ((3, 32, 4, 256, 128), 12, [16, 14], 9),
+    'qwen3': ((2, 128, 8, 2048, 768), 64, [110, 100], 6),
+}
+
+
+def _spec(shape):
+    from ferry_b200.model import ModelSpec
+    layers, E, K, H, I = shape
+    return ModelSpec('qwen3_moe', tuple(range(layers)), E, K, H, I)
+
+
+def _world_inputs(spec, step, rank, T):
+    from ferry_b200.workload import zipf_bias
+    g = torch.Generator().manual_seed(7)
+    gates = [(torch.randn(spec.experts, spec.hidden, generator=g) * 0.02).to(torch.bfloat16)
+             for _ in range(spec.layers)]
+    biases = [zipf_bias(spec.experts, 1.1, g) for _ in range(spec.layers)]
+    gx = torch.Generator().manual_seed(100 * step + rank)
+    x = torch.randn(T, spec.hidden, generator=gx).to(torch.bfloat16)
+    layer = step % spec.layers
+    sel, w, _ = ref_ops.route_qwen3(x, gates[layer], spec.topk, True, biases[layer])
+    return layer, x, sel, w
+
+
+def _worker(rank, world, port, case, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from ferry_b200.quota import Topology
+    from ferry_b200.runtime import OffloadRuntime
+    from ferry_b200.workload import cpu_pool
+    torch.cuda.set_device(rank)
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    shape, T, caps, steps = CASES[case]
+    spec = _spec(shape)
+    pool = cpu_pool(spec, spec.layers, 0).pin_memory()
+    rt = OffloadRuntime(spec, pool, caps, 'ferry', Topology.uniform(world, spec.experts))
+    outs = []
+    for step in range(steps):
+        layer, x, sel, w = _world_inputs(spec, step, rank, T)
+        got = rt.execute(layer, x.cuda(), sel.cuda(), w.cuda(), None)
+        outs.append(got.cpu())
+    torch.cuda.synchronize()
+    torch.save({'outs': outs, 'slots': rt.controller.slots, 'owner': rt.controller.owner,
+                'fetches': rt.fetches_per_rank, 'dispatch_bytes': rt.dispatch_bytes},
+               os.path.join(out_dir, f'rank{rank}.pt'))
+    dist.barrier()
+    rt.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize('case', list(CASES))
+def test_two_gpu_execute_matches_oracle(case):
+    if torch.cuda.device_count() < 2:
+        pytest.skip('needs 2 GPUs')
+    world = 2
+    shape, T, caps, steps = CASES[case]
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_worker, args=(world, 29700 + len(case), case, tmp), nprocs=world)
+        res = [torch.load(os.path.join(tmp, f'rank{r}.pt'), weights_only=False) for r in range(world)]
+    spec = _spec(shape)
+    from ferry_b200.workload import cpu_pool
+    from oracle import planner as op
+    pool = cpu_pool(spec, spec.layers, 0)
+    masks = np.asarray([1 << r for r in range(world)], np.int64)
+    lut = op.build_lut(spec.experts, world, masks, np.ones(world))
+    orc = OracleRuntime(spec, pool, caps, 'ferry', masks, np.ones(world), lut)
+    for step in range(steps):
+        per = [_world_inputs(spec, step, r, T) for r in range(world)]
+        want, _, _ = orc.execute(per[0][0], [p[1] for p in per], [p[2] for p in per], [p[3] for p in per])
+        for r in range(world):
+            assert_bf16_close(res[r]['outs'][step], want[r], f'{case} step {step} rank {r}')
+    for r in range(world):
+        np.testing.assert_array_equal(res[r]['slots'], orc.ctl.slots)
+        np.testing.assert_array_equal(res[r]['owner'], orc.ctl.owner)
+        np.testing.assert_array_equal(res[r]['fetches'], orc.fetches_per_rank)
+    assert res[0]['dispatch_bytes'] > 0
