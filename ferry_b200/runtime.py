@@ -105,7 +105,8 @@ class OffloadRuntime:
         return ex
 
     def reset(self):
-        """Empty expert cache and routing history (start of every measured run)."""
+        """Empty expert cache and routing history (start of every measured run,
+        ferry/runtime.py:51-62)."""
         if self.h2d is not None:
             self.h2d.synchronize()
         torch.cuda.synchronize(self.device)
@@ -120,7 +121,6 @@ class OffloadRuntime:
         self.fetches_per_rank = np.zeros(self.world, np.int64)
         self.decode_fetches_per_rank = np.zeros(self.world, np.int64)
         self.serial_wait_ns = 0
-        self._last_fetch = {}
 
     def execute(self, layer, hidden, selected, weights, probs_tail):
         """ferry/runtime.py:64-89: routing given by the MoE hook."""
@@ -150,116 +150,13 @@ class OffloadRuntime:
         return out
 
     def _after(self, ex, before):
+        """Counters of ferry/runtime.py:58-62, :70-72, :80-81 (fetches of every
+        rank come from the replicated plan's summary)."""
         st = ex.stats()
         self.serial_wait_ns += int((st.host_wait_us - before) * 1000)
         summ = _lib.LayoutSummary()
         call('ferryb_layer_last_summary', ex.h, ctypes.byref(summ))
         counts = np.asarray(summ.fetch_counts[:self.world], np.int64)
-        self.fetches_per_rank += counts
-        if self.event >= self.spec.layers:
-            self.decode_fetches_per_rank += counts
-        self.event += 1
-
-    def stats(self):
-        st = _lib.LayerStats()
-        call('ferryb_layer_get_stats', self.h, ctypes.byref(st))
-        return st
-
-    def close(self):
-        if self.h:
-            _lib.lib().ferryb_layer_destroy(self.h)
-            self.h = None
-        self.symm.close()
-
-
-class OffloadRuntime:
-    def __init__(self, spec, pool, capacities, policy, topology, history_window=128,
-                 balance_tol_bps=200, salt=1, eviction_score='frequency', *, n_copy_streams=1,
-                 norm_topk_prob=True, routed_scaling_factor=1.0, timing=False, group=None,
-                 device=None):
-        self.spec = spec
-        self.pool = pool
-        self.group = group
-        self.rank, self.world = _rank_world(group)
-        self.device = torch.device('cuda', torch.cuda.current_device()) if device is None else torch.device(device)
-        self.capacities = list(capacities)
-        self.cap = self.capacities[self.rank]
-        self.window = history_window
-        self.eviction_score = eviction_score
-        self.norm_topk_prob = norm_topk_prob
-        self.routed_scaling_factor = routed_scaling_factor
-        self.timing = timing
-        self.n_copy_streams = n_copy_streams
-        self.cache = torch.empty((self.cap, spec.expert_elements), dtype=torch.bfloat16, device=self.device)
-        self.controller = Controller(spec, capacities, policy, topology, balance_tol_bps, salt,
-                                     device=self.device, window=history_window,
-                                     score=eviction_score, topk=spec.topk)
-        self.h2d = None
-        self._executors = {}
-        self.reset()
-
-    def _executor(self, tokens):
-        ex = self._executors.get(tokens)
-        if ex is None:
-            ex = self._executors[tokens] = _Executor(self, tokens)
-        return ex
-
-    def reset(self):
-        """Empty expert cache and routing history (start of every measured run)."""
-        if self.h2d is not None:
-            self.h2d.synchronize()
-        torch.cuda.synchronize(self.device)
-        for ex in self._executors.values():
-            ex.close()
-        self._executors = {}
-        self.controller.reset()
-        if self.h2d is not None:
-            self.h2d.close()
-        self.h2d = H2DEngine(self.cache, self.pool, self.n_copy_streams)
-        self.event = 0
-        self.fetches_per_rank = np.zeros(self.world, np.int64)
-        self.decode_fetches_per_rank = np.zeros(self.world, np.int64)
-        self.serial_wait_ns = 0
-        self._last_fetch = {}
-
-    def execute(self, layer, hidden, selected, weights, probs_tail):
-        """ferry/runtime.py:64-89: routing given by the MoE hook."""
-        tokens = hidden.shape[0]
-        ex = self._executor(tokens)
-        out = torch.empty_like(hidden)
-        h = hidden.contiguous()
-        sel = selected.contiguous().long()
-        w = weights.contiguous().to(torch.bfloat16)
-        pt = probs_tail.float().contiguous() if (probs_tail is not None and
-                                                 self.eviction_score == 'probability') else None
-        before = ex.stats().host_wait_us
-        call('ferryb_layer_execute', ex.h, self.event, int(layer), ptr(h), ptr(sel), ptr(w), ptr(pt),
-             0 if pt is None else pt.shape[0], ptr(out), stream_ptr(self.device))
-        self._after(ex, before)
-        return out
-
-    def forward(self, layer, hidden, gate_weight, gate_bias=None, selected_out=None, weights_out=None):
-        """execute() with the MoE hook's router fused into kernel 1."""
-        tokens = hidden.shape[0]
-        ex = self._executor(tokens)
-        out = torch.empty_like(hidden)
-        before = ex.stats().host_wait_us
-        call('ferryb_layer_forward', ex.h, self.event, int(layer), ptr(hidden), ptr(gate_weight),
-             ptr(gate_bias), ptr(out), ptr(selected_out), ptr(weights_out), stream_ptr(self.device))
-        self._after(ex, before)
-        return out
-
-    def _after(self, ex, before):
-        st = ex.stats()
-        self.serial_wait_ns += int((st.host_wait_us - before) * 1000)
-        counts = np.zeros(self.world, np.int64)
-        # the executor's summary holds every rank's fetch count for this layer
-        summ = _lib.LayoutSummary.from_address(ctypes.addressof(ctypes.c_char.from_buffer(
-            (ctypes.c_char * 1).from_address(0))) if False else 0) if False else None
-        del summ
-        fetched = st.fetches - self._last_fetch.get(id(ex), 0)
-        self._last_fetch[id(ex)] = st.fetches
-        counts[self.rank] = fetched
         self.fetches_per_rank += counts
         if self.event >= self.spec.layers:
             self.decode_fetches_per_rank += counts
