@@ -60,6 +60,9 @@ def parse():
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--cpu-seconds', type=float, default=12.0)
+    p.add_argument('--sync-fetch', action='store_true',
+                   help='issue each layer\'s copies before its fetched-expert GEMM and wait on '
+                        'them from the stream (for profilers that serialise GPU work)')
     return p.parse_args()
 
 
@@ -149,7 +152,7 @@ def measured_peaks():
 
 def ncu_traffic():
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
-    path = ROOT / 'profiles' / 'gemm_traffic.json'
+    path = ROOT / 'profiles' / 'swiglu_fused_kernel_traffic.json'
     if path.exists():
         try:
             return json.loads(path.read_text())
@@ -211,7 +214,7 @@ def run_ours(a, rank, world, local):
     setup_s = time.time() - t0
     topo = Topology.uniform(world, spec.experts)
     rt = OffloadRuntime(spec, wl.pool, caps, a.policy, topo, n_copy_streams=a.copy_streams,
-                        timing=True)
+                        timing=True, sync_fetch=a.sync_fetch)
     b_host = host_link_gbs(rt.cache, wl.pool)
     stream = wl.hidden_stream(T, seed=1, world=world, rank=rank)
     n_steps = a.warmup + a.steps
@@ -279,8 +282,9 @@ def run_ours(a, rank, world, local):
                 'achieved': round(achieved, 1), 'peak': hbm_gbs, 'unit': 'GB/s',
                 'frac': round(achieved / hbm_gbs, 4), 'peak_source': peak_kind,
                 'algorithmic_bytes_per_layer': st.hit_weight_bytes / layers_timed,
-                'traffic': traffic.get('dram_bytes_per_expert') if traffic else None,
-                'traffic_note': traffic.get('note') if traffic else 'no ncu capture committed'}
+                'traffic': (round(traffic['dram_bytes_per_hit_expert'] * st.hit_experts / max(1, st.layers))
+                            if traffic and st.hit_experts else None),
+                'traffic_note': (traffic.get('note') if traffic else 'no ncu capture committed')}
     # per-layer roofline: slowest of host-link fetch, NVLink exchange, tensor FLOPs
     expert_bytes = spec.expert_bytes
     fetch_bytes = st.fetches * expert_bytes

@@ -51,7 +51,8 @@ class LayerConfig(ctypes.Structure):
     """ferryb_layer_config (include/ferryb.h)."""
     _fields_ = [(n, _i32c) for n in ('world', 'rank', 'tokens_per_rank', 'topk', 'experts', 'hidden',
                                       'intermediate', 'router_mode', 'norm_topk')] + [
-        ('scaling', ctypes.c_float), ('probability_score', _i32c), ('timing', _i32c)]
+        ('scaling', ctypes.c_float), ('probability_score', _i32c), ('timing', _i32c),
+        ('sync_fetch', _i32c)]
 
 
 class LayerStats(ctypes.Structure):
@@ -59,7 +60,7 @@ class LayerStats(ctypes.Structure):
     _fields_ = [(n, _i64) for n in ('layers', 'fetches', 'routes', 'recv_rows', 'dispatch_bytes',
                                      'combine_bytes', 'launches', 'hit_experts', 'hit_weight_bytes',
                                      'timed_layers')] + [
-        ('host_wait_us', _dbl), ('phase_us', _dbl * 5)]
+        ('host_wait_us', _dbl), ('phase_us', _dbl * 5), ('host_us', _dbl * 6)]
 
 
 # name -> (restype, argtypes); every symbol declared in include/ferryb.h.

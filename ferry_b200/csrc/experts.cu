@@ -321,6 +321,7 @@ struct FusedParams {
   const uint32_t* ready;  // [fetched] readiness flags, fetch order
   uint32_t ready_value;
   int* queue;  // [1] claim counter, zero at launch
+  int* done;   // [1] CTAs finished; the last one zeroes queue/dep/done for the next launch
   int* dep;    // [n_groups] phase-1 epilogue-warp completions, zero at launch
   int* err;
 };
@@ -609,6 +610,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
+  // the last CTA to finish leaves the counters zeroed for the next launch on
+  // this stream (every CTA is past its last claim and dependency read)
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.done, 1) == (int)gridDim.x - 1) {
+      for (int g = 0; g < p.n_groups; ++g) p.dep[g] = 0;
+      *p.queue = 0;
+      __threadfence();
+      *p.done = 0;
+    }
+  }
 }
 
 int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups, int n_hit,
@@ -638,13 +650,17 @@ int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups
   p.ready = ready;
   p.ready_value = ready_value;
   p.queue = queue_dep;
-  p.dep = queue_dep + 1;
+  p.done = queue_dep + 1;
+  p.dep = queue_dep + 2;
   p.err = err;
-  FB_CUDA(cudaMemsetAsync(queue_dep, 0, sizeof(int) * (1 + n_groups), stream));
   const int items = n_groups * (p.mt1 + p.mt2);
   const int grid = items < num_sms(device) ? items : num_sms(device);
-  FB_CUDA(cudaFuncSetAttribute(swiglu_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)kFusedSmem));
+  static bool attr_set[64] = {};
+  if (device < 64 && !attr_set[device]) {
+    FB_CUDA(cudaFuncSetAttribute(swiglu_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kFusedSmem));
+    attr_set[device] = true;
+  }
   swiglu_fused_kernel<<<grid, kThreads, kFusedSmem, stream>>>(m.w1, m.w2, m.bx, m.ba, p);
   FB_LAUNCH_CHECK();
   return FERRYB_OK;

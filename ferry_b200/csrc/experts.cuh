@@ -24,7 +24,8 @@ int swiglu_grouped_maps(const GemmMaps& m, const GemmGroup* groups, int n_groups
 // Both phases of every group in one persistent launch; groups [n_hit,
 // n_groups) are fetched experts whose tiles wait for ready[j] >= ready_value
 // (raised when fetch j has landed).  queue_dep: device
-// scratch of 1 + n_groups ints (zeroed by the launcher).
+// scratch of 2 + n_groups ints, zero before the first launch; every launch
+// leaves it zeroed again (its last CTA resets it).
 int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups, int n_hit,
                         const uint32_t* ready, uint32_t ready_value, int* queue_dep,
                         const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,

@@ -61,7 +61,7 @@ struct ferryb_layer {
   int* hist_local;
   unsigned* done;
   uint32_t* ready;  // [experts] copy readiness flags (monotonic sequence numbers)
-  int* queue_dep;   // [1 + experts] GEMM work counter + phase-1 completions
+  int* queue_dep;   // [2 + experts] GEMM work counter, done counter, phase-1 completions
   // host side
   ferryb_layout_summary* summary_host = nullptr;
   int32_t* errs_host = nullptr;  // pinned copy of the device error words
@@ -166,7 +166,7 @@ static int64_t workspace_bytes(const ferryb_layer_config& c, uint8_t* base, ferr
     auto done = cv.take<unsigned>(1);
     auto peer_base = cv.take<uintptr_t>(R);
     auto ready = cv.take<uint32_t>(2 * E);
-    auto queue_dep = cv.take<int>(1 + E);
+    auto queue_dep = cv.take<int>(2 + E);
     if (L) {
       L->dest = dest; L->fetches = fetches; L->n_fetches = n_fetches; L->counts = counts;
       L->errs = errs; L->layer_slot = layer_slot; L->send_idx = send_idx; L->send_ids = send_ids;
@@ -296,6 +296,13 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   const bool timing = c.timing != 0;
   uint8_t* half = L->symm + parity * L->sl.half;
   int64_t launches = 0;
+  using clk = std::chrono::steady_clock;
+  auto h_prev = clk::now();
+  auto host_mark = [&](int stage) {
+    const auto now = clk::now();
+    L->stats.host_us[stage] += std::chrono::duration<double, std::micro>(now - h_prev).count();
+    h_prev = now;
+  };
   if (timing) {
     if (L->tev_used + 6 > L->tev_pool.size()) {
       for (int i = 0; i < 6 * 64; ++i) {
@@ -379,10 +386,13 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   FB_CUDA(cudaMemcpyAsync(L->errs_host, L->errs, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost,
                           stream));
   FB_CUDA(cudaEventRecord(L->summary_ev, stream));
-  const auto t0 = std::chrono::steady_clock::now();
+  host_mark(0);
   FB_CUDA(cudaEventSynchronize(L->summary_ev));
-  L->stats.host_wait_us +=
-      std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
+  {
+    const auto now = clk::now();
+    L->stats.host_wait_us += std::chrono::duration<double, std::micro>(now - h_prev).count();
+    h_prev = now;
+  }
   const ferryb_layout_summary sum = *L->summary_host;
   // error words: [0] planner, [1] layout, [2] GEMM, [3] transport (earlier layers)
   const int plan_err = L->errs_host[0];
@@ -408,6 +418,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     if ((s = ferryb_h2d_fetch_flagged(L->h2d, fslots.data(), fkeys.data(), 1, L->ready, ready_value)))
       return s;
   }
+  host_mark(1);
 
   // 6-7 dispatch + permute
   const FusedArgs fa = fused_args(L, parity, static_cast<const __nv_bfloat16*>(hidden),
@@ -416,6 +427,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   if ((s = fused_permute(fa, seq, sum.n_routes, stream))) return s;
   launches += 2 + (c.world > 1 ? 1 : 0);  // dispatch (+ signal) + permute
   if (timing) FB_CUDA(cudaEventRecord(L->tev[2], stream));
+  host_mark(2);
 
   // 8 grouped SwiGLU (kernel 5), both phases per launch: the experts cached
   //   before this layer (no waits), then the fetched experts, whose tiles
@@ -425,17 +437,31 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     return s;
   if (sum.n_hit) launches += 1;
   if (timing) FB_CUDA(cudaEventRecord(L->tev[3], stream));
+  host_mark(3);
+  if (c.sync_fetch) {
+    // profiler-safe order: every copy is issued (and its flag raised) before
+    // the fetched-expert GEMM, which the compute stream makes wait for them
+    if (sum.n_fetch_mine > 1) {
+      if ((s = ferryb_h2d_fetch_flagged(L->h2d, fslots.data() + 1, fkeys.data() + 1,
+                                        sum.n_fetch_mine - 1, L->ready + 1, ready_value)))
+        return s;
+    }
+    if (sum.n_fetch_mine > 0) {
+      if ((s = ferryb_h2d_wait_device(L->h2d, fslots.data(), sum.n_fetch_mine, stream))) return s;
+    }
+  }
   if ((s = swiglu_fused_launch(L->maps, L->groups + sum.n_hit, sum.n_fetch_mine, 0, L->ready,
                                ready_value, L->queue_dep, L->route_w, L->act, L->expert_out,
                                L->errs + 2, stream)))
     return s;
   if (sum.n_fetch_mine) launches += 1;
-  if (sum.n_fetch_mine > 1) {
+  if (!c.sync_fetch && sum.n_fetch_mine > 1) {
     if ((s = ferryb_h2d_fetch_flagged(L->h2d, fslots.data() + 1, fkeys.data() + 1,
                                       sum.n_fetch_mine - 1, L->ready + 1, ready_value)))
       return s;
   }
   if (timing) FB_CUDA(cudaEventRecord(L->tev[4], stream));
+  host_mark(4);
 
   // 9 combine
   if ((s = fused_combine(fa, seq, sum.n_recv, stream))) return s;
@@ -465,6 +491,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   }
   L->stats.dispatch_bytes += sent_remote * (2 * (int64_t)c.hidden + 3 * c.topk);
   L->stats.combine_bytes += recv_remote * 2 * (int64_t)c.hidden;
+  host_mark(5);
   return FERRYB_OK;
 }
 

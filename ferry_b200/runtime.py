@@ -46,6 +46,7 @@ class _Executor:
         cfg.scaling = float(rt.routed_scaling_factor)
         cfg.probability_score = int(rt.eviction_score == 'probability')
         cfg.timing = int(rt.timing)
+        cfg.sync_fetch = int(rt.sync_fetch)
         self.cfg = cfg
         lib = _lib.lib()
         ws_bytes = lib.ferryb_layer_workspace_bytes(ctypes.byref(cfg))
@@ -76,8 +77,9 @@ class OffloadRuntime:
     def __init__(self, spec, pool, capacities, policy, topology, history_window=128,
                  balance_tol_bps=200, salt=1, eviction_score='frequency', *, n_copy_streams=1,
                  norm_topk_prob=True, routed_scaling_factor=1.0, timing=False, group=None,
-                 device=None):
+                 device=None, sync_fetch=False):
         self.spec = spec
+        self.sync_fetch = sync_fetch
         self.pool = pool
         self.group = group
         self.rank, self.world = _rank_world(group)
@@ -161,6 +163,12 @@ class OffloadRuntime:
         if self.event >= self.spec.layers:
             self.decode_fetches_per_rank += counts
         self.event += 1
+
+    def last_summary(self, tokens):
+        """The plan summary of the last layer run with `tokens` tokens."""
+        summ = _lib.LayoutSummary()
+        call('ferryb_layer_last_summary', self._executors[tokens].h, ctypes.byref(summ))
+        return summ
 
     def stats(self):
         """Per-executor counters (layers, fetches, routes, bytes, phase times)."""

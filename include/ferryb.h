@@ -332,7 +332,12 @@ typedef struct ferryb_layer_config {
   int32_t norm_topk;         /* Qwen3 norm_topk_prob */
   float scaling;             /* DeepSeek-V2 routed_scaling_factor */
   int32_t probability_score; /* eviction score 'probability' (ferry/metadata.py:59-60) */
-  int32_t timing;            /* record per-phase CUDA-event times (synchronises each layer) */
+  int32_t timing;            /* record per-phase CUDA-event times (collected by
+                                ferryb_layer_collect_timing) */
+  int32_t sync_fetch;        /* 1: issue all of a layer's copies first and make the compute
+                                stream wait for them before the fetched-expert GEMM (for
+                                profilers that serialise GPU work, e.g. ncu); 0: the GEMM
+                                waits on the device for each copy's readiness flag */
 } ferryb_layer_config;
 
 typedef struct ferryb_layer_stats {
@@ -346,6 +351,12 @@ typedef struct ferryb_layer_stats {
                                 ferryb_layer_collect_timing): route+plan+layout,
                                 summary+dispatch+permute, cached-expert GEMM,
                                 fetched-expert GEMMs (incl. copy waits), combine */
+  double host_us[6];         /* host time spent issuing each stage (steady
+                                clock, every call): router+planner+layout,
+                                first fetch after the summary arrives,
+                                dispatch+permute, cached-expert GEMM,
+                                fetched-expert GEMM + remaining fetches,
+                                combine + counters */
 } ferryb_layer_stats;
 
 typedef struct ferryb_layer ferryb_layer;
