@@ -319,6 +319,11 @@ def run_ours(a, rank, world, local):
         'roofline': roofline, 'layer_roofline': layer_roofline, 'layer_split_us': split,
         'gpu_launches': int(st.launches), 'h2d_expert_copies': int(fetch_copies),
         'host_wait_us_per_layer': round(st.host_wait_us / max(1, st.layers), 1),
+        'host_issue_us_per_layer': {name: round(st.host_us[i] / max(1, st.layers), 1) for i, name in enumerate(
+            ['route_plan_layout', 'first_fetch', 'dispatch_permute', 'gemm_cached', 'gemm_fetched_fetches',
+             'combine'])},
+        'copy_lane_us_per_layer': {name: round(st.copy_us[i] / layers_timed, 1) for i, name in enumerate(
+            ['layout_end_to_first_copy', 'copies', 'last_copy_to_combine_end'])},
         'setup_s': round(setup_s, 1), 'e2e': e2e, 'clocks': clocks,
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

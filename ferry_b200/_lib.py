@@ -60,7 +60,8 @@ class LayerStats(ctypes.Structure):
     _fields_ = [(n, _i64) for n in ('layers', 'fetches', 'routes', 'recv_rows', 'dispatch_bytes',
                                      'combine_bytes', 'launches', 'hit_experts', 'hit_weight_bytes',
                                      'timed_layers')] + [
-        ('host_wait_us', _dbl), ('phase_us', _dbl * 5), ('host_us', _dbl * 6)]
+        ('host_wait_us', _dbl), ('phase_us', _dbl * 5), ('host_us', _dbl * 6),
+        ('copy_us', _dbl * 3)]
 
 
 # name -> (restype, argtypes); every symbol declared in include/ferryb.h.

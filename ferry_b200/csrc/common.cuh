@@ -69,6 +69,9 @@ PFN_encodeTiled encode_tiled_fn();
 typedef CUresult (*PFN_writeValue32)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
 PFN_writeValue32 write_value32_fn();
 int stream_mem_ops_supported(int device);
+// h2d.cu: record an event on the copy lane (0: before the next fetch, 1:
+// after the last fetch issued)
+int h2d_record_event(ferryb_h2d* h, cudaEvent_t ev, int which);
 
 // 2D bf16 tensor map over a row-major [rows, cols] matrix (cols contiguous),
 // box = [box_cols, box_rows], 128-byte swizzle (box_cols * 2 must be 128).

@@ -45,6 +45,17 @@ struct DeviceGuard {
 };
 }  // namespace
 
+namespace ferryb {
+// Records `ev` on the copy stream the next fetch will use (which = 0) or on
+// the stream of the last fetch issued (which = 1): timing of the copy lane.
+int h2d_record_event(ferryb_h2d* h, cudaEvent_t ev, int which) {
+  const size_t ns = h->streams.size();
+  const int64_t i = which == 0 ? h->next_stream : h->next_stream - 1;
+  FB_CUDA(cudaEventRecord(ev, h->streams[(size_t)((i % (int64_t)ns + ns) % ns)]));
+  return FERRYB_OK;
+}
+}  // namespace ferryb
+
 extern "C" int ferryb_h2d_create(void* cache, int64_t cache_slots, int64_t row_bytes,
                                  const void* pool, int64_t pool_rows, int32_t n_streams,
                                  ferryb_h2d** out) {

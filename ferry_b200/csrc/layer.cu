@@ -66,9 +66,11 @@ struct ferryb_layer {
   ferryb_layout_summary* summary_host = nullptr;
   int32_t* errs_host = nullptr;  // pinned copy of the device error words
   cudaEvent_t summary_ev = nullptr;
-  // timing mode: 6 events per layer, recorded without host syncs and
-  // collected by ferryb_layer_collect_timing
+  // timing mode: 8 events per layer (6 on the compute stream, 2 on the copy
+  // lane), recorded without host syncs and collected by
+  // ferryb_layer_collect_timing
   std::vector<cudaEvent_t> tev_pool;
+  std::vector<char> tev_fetched;  // per timed layer: copy-lane events recorded
   size_t tev_used = 0;
   cudaEvent_t* tev = nullptr;
   GemmMaps maps{};
@@ -304,15 +306,16 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     h_prev = now;
   };
   if (timing) {
-    if (L->tev_used + 6 > L->tev_pool.size()) {
-      for (int i = 0; i < 6 * 64; ++i) {
+    if (L->tev_used + 8 > L->tev_pool.size()) {
+      for (int i = 0; i < 8 * 64; ++i) {
         cudaEvent_t e;
         FB_CUDA(cudaEventCreate(&e));
         L->tev_pool.push_back(e);
       }
     }
     L->tev = L->tev_pool.data() + L->tev_used;
-    L->tev_used += 6;
+    L->tev_used += 8;
+    L->tev_fetched.push_back(0);
     FB_CUDA(cudaEventRecord(L->tev[0], stream));
   }
 
@@ -415,6 +418,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   }
   const uint32_t ready_value = (uint32_t)seq;
   if (sum.n_fetch_mine > 0) {
+    if (timing && (s = h2d_record_event(L->h2d, L->tev[6], 0))) return s;
     if ((s = ferryb_h2d_fetch_flagged(L->h2d, fslots.data(), fkeys.data(), 1, L->ready, ready_value)))
       return s;
   }
@@ -460,6 +464,10 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
                                       sum.n_fetch_mine - 1, L->ready + 1, ready_value)))
       return s;
   }
+  if (timing && sum.n_fetch_mine > 0) {
+    if ((s = h2d_record_event(L->h2d, L->tev[7], 1))) return s;
+    L->tev_fetched.back() = 1;
+  }
   if (timing) FB_CUDA(cudaEventRecord(L->tev[4], stream));
   host_mark(4);
 
@@ -497,7 +505,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
 
 extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
   FB_CHECK_ARG(L, "layer_collect_timing: null argument");
-  for (size_t b = 0; b + 6 <= L->tev_used; b += 6) {
+  for (size_t b = 0; b + 8 <= L->tev_used; b += 8) {
     cudaEvent_t* e = L->tev_pool.data() + b;
     FB_CUDA(cudaEventSynchronize(e[5]));
     for (int i = 0; i < 5; ++i) {
@@ -505,8 +513,18 @@ extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
       FB_CUDA(cudaEventElapsedTime(&ms, e[i], e[i + 1]));
       L->stats.phase_us[i] += ms * 1000.0;
     }
+    if (L->tev_fetched[b / 8]) {
+      const int pairs[3][2] = {{1, 6}, {6, 7}, {7, 5}};
+      for (int i = 0; i < 3; ++i) {
+        float ms = 0.0f;
+        FB_CUDA(cudaEventSynchronize(e[pairs[i][1]]));
+        FB_CUDA(cudaEventElapsedTime(&ms, e[pairs[i][0]], e[pairs[i][1]]));
+        L->stats.copy_us[i] += ms * 1000.0;
+      }
+    }
     L->stats.timed_layers += 1;
   }
+  L->tev_fetched.clear();
   L->tev_used = 0;
   return FERRYB_OK;
 }

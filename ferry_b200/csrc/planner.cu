@@ -262,71 +262,157 @@ __device__ bool greedy_quota_warp(const PlanConfig& c, int m, const int* capacit
 // load_balanced_assignment (ferry/policy.py:49-106) on one warp; lane r
 // owns rank r.  Loads are token counts (< 2^31), so 32-bit arithmetic is
 // exact; the peak load only grows at the chosen rank, so it is kept
-// incrementally.  Reductions run over the next power of two >= R lanes.
+// incrementally.  The per-miss choice -- the lexicographic maximum of
+// (d_{r,e}, -P_r, -N_r) over eligible ranks, lowest rank on ties -- is three
+// warp reductions (redux.sync) and a ballot; the next miss's inputs are
+// loaded while the current one is decided.  With one rank every miss goes to
+// rank 0 while its quota lasts.
 __device__ void assignment_warp(const PlanConfig& c, PlanSmem& sm, const int* demand /*[E*R]*/,
                                 const int* owner_layer /*[E]*/) {
   const int lane = threadIdx.x & 31;
   const int R = c.world, E = c.experts, m = sm.m;
-  int span = 1;
-  while (span < R) span <<= 1;
+  if (R == 1) {
+    const int q = (int)sm.quota[0];
+    for (int oi = lane; oi < m; oi += 32) sm.assignment[sm.order[oi]] = oi < q ? 0 : -1;
+    __syncwarp();
+    return;
+  }
   // N_r: tokens routed to experts already cached on r (owner_layer in smem).
-  int load = 0, remaining = 0;
+  int load = 0;
   for (int e0 = 0; e0 < E; e0 += 32) {
     const int e = e0 + lane;
     const int o = e < E ? owner_layer[e] : -1;
     const int d = e < E ? sm.demand_total[e] : 0;
     for (int r = 0; r < R; ++r) {
-      int v = (o == r) ? d : 0;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      const int v = __reduce_add_sync(0xffffffffu, o == r ? d : 0);
       if (lane == r) load += v;
     }
   }
-  if (lane < R) remaining = (int)sm.quota[lane];
-  int peak = lane < R ? load : 0;
-  for (int off = span >> 1; off > 0; off >>= 1) peak = max(peak, __shfl_xor_sync(0xffffffffu, peak, off));
+  int remaining = lane < R ? (int)sm.quota[lane] : 0;
+  int peak = __reduce_max_sync(0xffffffffu, lane < R ? load : 0);
   const int kBig = 0x7fffffff;
+  int nx_i = 0, nx_total = 0, nx_a = 0;
+  if (m > 0) {
+    nx_i = sm.order[0];
+    nx_total = (int)sm.totals[nx_i];
+    nx_a = lane < R ? demand[sm.misses[nx_i] * R + lane] : 0;
+  }
   for (int oi = 0; oi < m; ++oi) {
-    const int i = sm.order[oi];
-    const int e = sm.misses[i];
-    const int total = (int)sm.totals[i];
+    const int i = nx_i, total = nx_total, a = nx_a;
+    if (oi + 1 < m) {  // next miss's inputs, off the dependency chain
+      nx_i = sm.order[oi + 1];
+      nx_total = (int)sm.totals[nx_i];
+      nx_a = lane < R ? demand[sm.misses[nx_i] * R + lane] : 0;
+    }
     const bool has = lane < R && remaining > 0;
     const int projected = has ? max(peak, load + total) : kBig;
-    int lowest = projected;
-    for (int off = span >> 1; off > 0; off >>= 1) lowest = min(lowest, __shfl_xor_sync(0xffffffffu, lowest, off));
+    const int lowest = __reduce_min_sync(0xffffffffu, projected);
     int slack = 0;
     if (c.bps > 0) {
-      const int64_t prod = (int64_t)lowest * c.bps;  // lowest >= 0 here
-      const int64_t q = prod / 10000;
+      const int64_t q = (int64_t)lowest * c.bps / 10000;  // lowest >= 0 here
       slack = q > 1 ? (int)q : 1;
     }
     const bool eligible = has && (int64_t)projected <= (int64_t)lowest + slack;
-    const int a = (lane < R) ? demand[e * R + lane] : 0;
-    // lexicographic max of (a, -projected, -load), lowest lane on ties
-    int best = eligible ? lane : -1, ba = a, bp = projected, bl = load;
-    for (int off = span >> 1; off > 0; off >>= 1) {
-      const int ob = __shfl_xor_sync(0xffffffffu, best, off);
-      const int oa = __shfl_xor_sync(0xffffffffu, ba, off);
-      const int op = __shfl_xor_sync(0xffffffffu, bp, off);
-      const int ol = __shfl_xor_sync(0xffffffffu, bl, off);
-      bool take;
-      if (ob < 0) take = false;
-      else if (best < 0) take = true;
-      else if (oa != ba) take = oa > ba;
-      else if (op != bp) take = op < bp;
-      else if (ol != bl) take = ol < bl;
-      else take = ob < best;
-      if (take) { best = ob; ba = oa; bp = op; bl = ol; }
-    }
-    best = __shfl_sync(0xffffffffu, best, 0);
+    const int amax = __reduce_max_sync(0xffffffffu, eligible ? a : -1);
+    const bool c1 = eligible && a == amax;
+    const int pmin = __reduce_min_sync(0xffffffffu, c1 ? projected : kBig);
+    const bool c2 = c1 && projected == pmin;
+    const int lmin = __reduce_min_sync(0xffffffffu, c2 ? load : kBig);
+    const unsigned win = __ballot_sync(0xffffffffu, c2 && load == lmin);
+    const int best = win ? __ffs(win) - 1 : -1;
     if (lane == 0) sm.assignment[i] = best;
     if (best >= 0) {
       if (lane == best) { remaining -= 1; load += total; }
-      const int nb = __shfl_sync(0xffffffffu, load, best);
-      peak = max(peak, nb);
+      peak = max(peak, __shfl_sync(0xffffffffu, load, best));
     }
   }
   __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// Ascending bitonic sort of n (power of two >= 64) records (k0, k1, sl) in
+// shared memory by (k0, k1).  Compare-exchanges of stride >= 64 run in shared
+// memory, one pair per thread and a block barrier per stage; every stride
+// <= 32 stays inside one 64-record block, which a warp sorts in registers
+// (lane holds records base+lane and base+lane+32: stride 32 within the lane,
+// strides 16..1 by shuffles).  Equal keys never swap, so no record is lost
+// or duplicated.
+struct Rec {
+  uint64_t k0, k1;
+  uint32_t sl;
+};
+
+__device__ __forceinline__ bool rec_lt(const Rec& a, const Rec& b) {
+  return a.k0 < b.k0 || (a.k0 == b.k0 && a.k1 < b.k1);
+}
+
+__device__ __forceinline__ Rec shfl_rec(const Rec& r, int mask) {
+  Rec o;
+  o.k0 = __shfl_xor_sync(0xffffffffu, r.k0, mask);
+  o.k1 = __shfl_xor_sync(0xffffffffu, r.k1, mask);
+  o.sl = __shfl_xor_sync(0xffffffffu, r.sl, mask);
+  return o;
+}
+
+// stages (size, stride) for stride = first..1 on the two records of a lane;
+// idx_a = index of record a (b = idx_a + 32)
+__device__ __forceinline__ void warp_stages(Rec& a, Rec& b, int idx_a, int size, int first,
+                                            int lane) {
+  for (int stride = first; stride > 0; stride >>= 1) {
+    const bool up_a = (idx_a & size) == 0;
+    const bool up_b = ((idx_a + 32) & size) == 0;
+    if (stride == 32) {
+      // a and b are partners (size >= 64 here, so up_a == up_b)
+      const bool swap = up_a ? rec_lt(b, a) : rec_lt(a, b);
+      if (swap) { const Rec t = a; a = b; b = t; }
+    } else {
+      const bool lower = (lane & stride) == 0;
+      const Rec oa = shfl_rec(a, stride), ob = shfl_rec(b, stride);
+      // the lower record of an ascending pair keeps the minimum
+      const bool want_min_a = lower == up_a, want_min_b = lower == up_b;
+      if (want_min_a ? rec_lt(oa, a) : rec_lt(a, oa)) a = oa;
+      if (want_min_b ? rec_lt(ob, b) : rec_lt(b, ob)) b = ob;
+    }
+  }
+}
+
+__device__ void sort_records(uint64_t* k0, uint64_t* k1, uint32_t* sl, int n) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_warps = blockDim.x >> 5;
+  // sizes 2..64 entirely inside each 64-record block
+  for (int blk = warp; blk < n / 64; blk += n_warps) {
+    const int ia = blk * 64 + lane, ib = ia + 32;
+    Rec a{k0[ia], k1[ia], sl[ia]}, b{k0[ib], k1[ib], sl[ib]};
+    for (int size = 2; size <= 64; size <<= 1) warp_stages(a, b, ia, size, size >> 1, lane);
+    k0[ia] = a.k0; k1[ia] = a.k1; sl[ia] = a.sl;
+    k0[ib] = b.k0; k1[ib] = b.k1; sl[ib] = b.sl;
+  }
+  __syncthreads();
+  for (int size = 128; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride >= 64; stride >>= 1) {
+      for (int i = tid; i < n / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const uint64_t a0 = k0[lo], b0 = k0[hi], a1 = k1[lo], b1 = k1[hi];
+        const bool b_less = b0 < a0 || (b0 == a0 && b1 < a1);
+        const bool a_less = a0 < b0 || (a0 == b0 && a1 < b1);
+        if (up ? b_less : a_less) {
+          k0[lo] = b0; k0[hi] = a0; k1[lo] = b1; k1[hi] = a1;
+          const uint32_t t = sl[lo]; sl[lo] = sl[hi]; sl[hi] = t;
+        }
+      }
+      __syncthreads();
+    }
+    for (int blk = warp; blk < n / 64; blk += n_warps) {
+      const int ia = blk * 64 + lane, ib = ia + 32;
+      Rec a{k0[ia], k1[ia], sl[ia]}, b{k0[ib], k1[ib], sl[ib]};
+      warp_stages(a, b, ia, size, 32, lane);
+      k0[ia] = a.k0; k1[ia] = a.k1; sl[ia] = a.sl;
+      k0[ib] = b.k0; k1[ib] = b.k1; sl[ib] = b.sl;
+    }
+    __syncthreads();
+  }
 }
 
 __global__ void __launch_bounds__(kPlanThreads, 1)
@@ -508,47 +594,25 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     }
     __syncthreads();
     PLAN_TS(4);
-    // bitonic sort, ascending.  With one compare-exchange per thread, the
-    // pairs of a stage with stride <= 32 lie inside one warp's 64-element
-    // block, so those stages need only __syncwarp.
-    const bool one_pass = n / 2 <= (int)blockDim.x;
-    for (int size = 2; size <= n; size <<= 1) {
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int i = tid; i < n / 2; i += blockDim.x) {
-          const int lo = 2 * i - (i & (stride - 1));
-          const int hi = lo + stride;
-          const bool up = (lo & size) == 0;
-          const uint64_t a0 = k0[lo], b0 = k0[hi], a1 = k1[lo], b1 = k1[hi];
-          const bool b_less = b0 < a0 || (b0 == a0 && b1 < a1);
-          if (b_less == up) {
-            k0[lo] = b0; k0[hi] = a0; k1[lo] = b1; k1[hi] = a1;
-            const uint32_t t = sl[lo]; sl[lo] = sl[hi]; sl[hi] = t;
-          }
-        }
-        // block-wide barrier when this stage or the next pairs elements of
-        // different warps (stride > 32); between two warp-local stages a
-        // warp barrier suffices
-        const int next_stride = stride > 1 ? stride >> 1 : size;
-        if (stride > 32 || next_stride > 32 || !one_pass) __syncthreads();
-        else __syncwarp();
-      }
-    }
-    __syncthreads();
+    sort_records(k0, k1, sl, n);
     PLAN_TS(5);
     // the j-th miss assigned to rank r takes the j-th record of r's segment
     if (tid == 0) {
       int pos = 0;
-      for (int r = 0; r < R; ++r) { sm.seg_start[r] = pos; pos += c.capacities[r]; sm.n_assigned[r] = 0; }
-      for (int i = 0; i < m; ++i) {
-        const int r = sm.assignment[i];
-        sm.victim_pos[i] = sm.seg_start[r] + sm.n_assigned[r];
-        sm.n_assigned[r] += 1;
-      }
+      for (int r = 0; r < R; ++r) { sm.seg_start[r] = pos; pos += c.capacities[r]; }
+    }
+    __syncthreads();
+    for (int i = tid; i < m; i += blockDim.x) {
+      const int r = sm.assignment[i];
+      int before = 0;  // earlier misses assigned to the same rank
+      for (int j = 0; j < i; ++j) before += sm.assignment[j] == r;
+      sm.victim_pos[i] = r >= 0 && r < R ? sm.seg_start[r] + before : -1;
     }
     __syncthreads();
     for (int i = tid; i < m; i += blockDim.x) {
       const int r = sm.assignment[i];
       const int vp = sm.victim_pos[i];
+      if (vp < 0 || vp >= n) { set_err(out.err, DEV_NO_SLOT); continue; }
       const uint64_t rk0 = k0[vp];
       const uint32_t rslot = sl[vp];
       const uint64_t cls = (rk0 >> 48) & 0xff;
@@ -574,7 +638,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   if (tid < R) out.counts[tid] = 0;
   __syncthreads();
   if (tid == 0) *out.n_fetches = m;
-  for (int i = tid; i < m; i += blockDim.x) atomicAdd(&out.counts[sm.assignment[i]], 1);
+  for (int i = tid; i < m; i += blockDim.x) {
+    const int r = sm.assignment[i];
+    if (r >= 0 && r < R) atomicAdd(&out.counts[r], 1);
+  }
   for (int i = tid; i < n_tok * K; i += blockDim.x) {
     const int e = in.ids[i];
     out.dest[i] = e < E ? s.owner[base + e] : -1;
@@ -719,7 +786,7 @@ size_t plan_dyn_smem(int experts, int world, int total_slots, int n_domains, siz
                      size_t* greedy_off, int* sort_n) {
   size_t off = (size_t)experts * world * sizeof(int);
   off = (off + 15) & ~size_t(15);
-  int n = 1;
+  int n = 64;  // the sort works on whole 64-record warp blocks
   while (n < total_slots) n <<= 1;
   *sort_n = n;
   *sort_off = off;

@@ -357,6 +357,10 @@ typedef struct ferryb_layer_stats {
                                 dispatch+permute, cached-expert GEMM,
                                 fetched-expert GEMM + remaining fetches,
                                 combine + counters */
+  double copy_us[3];         /* timing mode, layers with fetches: layout end ->
+                                first copy start (the host round trip), first
+                                copy start -> last copy end, last copy end ->
+                                combine end (the compute tail) */
 } ferryb_layer_stats;
 
 typedef struct ferryb_layer ferryb_layer;
