@@ -52,7 +52,7 @@ class LayerConfig(ctypes.Structure):
     _fields_ = [(n, _i32c) for n in ('world', 'rank', 'tokens_per_rank', 'topk', 'experts', 'hidden',
                                       'intermediate', 'router_mode', 'norm_topk')] + [
         ('scaling', ctypes.c_float), ('probability_score', _i32c), ('timing', _i32c),
-        ('sync_fetch', _i32c)]
+        ('sync_fetch', _i32c), ('shared_intermediate', _i32c)]
 
 
 class LayerStats(ctypes.Structure):
@@ -105,6 +105,10 @@ SIGNATURES = {
     'ferryb_symm_open': (_i32, [_vp, ctypes.POINTER(_vp)]),
     'ferryb_symm_close': (_i32, [_vp]),
     'ferryb_symm_free': (_i32, [_vp]),
+    'ferryb_history_update': (_i32, [_vp, _vp, _vp, _i32c, _i32c, _i32c, _i32c, _vp, _i64, _vp]),
+    'ferryb_history_scores': (_i32, [_vp, _vp, _i32c, _i32c, _i32c, _i32c, _vp, _vp]),
+    'ferryb_symm_allgather': (_i32, [_vp, _i32c, _i32c, _i64, _vp, _i64, _i64, ctypes.c_uint64, _vp]),
+    'ferryb_symm_wait': (_i32, [_vp, _i64, _i32c, ctypes.c_uint64, _vp, _vp]),
     'ferryb_layer_workspace_bytes': (_i64, [ctypes.POINTER(LayerConfig)]),
     'ferryb_layer_symm_bytes': (_i64, [ctypes.POINTER(LayerConfig), _i32c]),
     'ferryb_layer_create': (_i32, [ctypes.POINTER(LayerConfig), ctypes.POINTER(Planner), _vp, _i64,
@@ -113,6 +117,7 @@ SIGNATURES = {
     'ferryb_layer_execute': (_i32, [_vp, _i64, _i32c, _vp, _vp, _vp, _vp, _i32c, _vp, _vp]),
     'ferryb_layer_get_stats': (_i32, [_vp, ctypes.POINTER(LayerStats)]),
     'ferryb_layer_reset_stats': (_i32, [_vp]),
+    'ferryb_layer_set_shared': (_i32, [_vp, _i32c, _vp]),
     'ferryb_layer_last_summary': (_i32, [_vp, ctypes.POINTER(LayoutSummary)]),
     'ferryb_layer_collect_timing': (_i32, [_vp]),
     'ferryb_debug_plan_timestamps': (_i32, [_vp]),

@@ -17,6 +17,12 @@ struct GemmMaps {
 
 int make_gemm_maps(GemmMaps* m, const void* cache, int64_t cache_slots, const void* x,
                    const void* act, int64_t rows_cap, int64_t hidden, int64_t inter);
+// Two-launch grouped SwiGLU with maps encoded for this call (cache = expert
+// rows [slots, 3*H*I]); x [total_routes, H], route_w [total_routes].
+int swiglu_grouped(const void* cache, int64_t cache_slots, const GemmGroup* groups, int n_groups,
+                   int64_t total_routes, const __nv_bfloat16* x, const __nv_bfloat16* route_w,
+                   __nv_bfloat16* act, __nv_bfloat16* out, int64_t hidden, int64_t inter,
+                   int* err, cudaStream_t stream);
 int swiglu_grouped_maps(const GemmMaps& m, const GemmGroup* groups, int n_groups,
                         const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
                         int* err, cudaStream_t stream);

@@ -62,6 +62,10 @@ struct ferryb_layer {
   unsigned* done;
   uint32_t* ready;  // [experts] copy readiness flags (monotonic sequence numbers)
   int* queue_dep;   // [2 + experts] GEMM work counter, done counter, phase-1 completions
+  // shared experts (shared_intermediate > 0)
+  std::vector<const void*> shared_w;  // per MoE layer, borrowed
+  __nv_bfloat16 *shared_act = nullptr, *shared_out = nullptr, *shared_ones = nullptr;
+  GemmGroup* shared_group = nullptr;
   // host side
   ferryb_layout_summary* summary_host = nullptr;
   int32_t* errs_host = nullptr;  // pinned copy of the device error words
@@ -132,6 +136,8 @@ static int check_config(const ferryb_layer_config* c) {
   FB_CHECK_ARG(c->hidden % 256 == 0 && c->intermediate % 128 == 0,
                "layer: hidden must be a multiple of 256 and intermediate of 128");
   FB_CHECK_ARG(c->router_mode >= 0 && c->router_mode <= 1, "layer: router_mode must be 0 or 1");
+  FB_CHECK_ARG(c->shared_intermediate >= 0 && c->shared_intermediate % 128 == 0,
+               "layer: shared_intermediate must be a non-negative multiple of 128");
   return FERRYB_OK;
 }
 
@@ -169,6 +175,11 @@ static int64_t workspace_bytes(const ferryb_layer_config& c, uint8_t* base, ferr
     auto peer_base = cv.take<uintptr_t>(R);
     auto ready = cv.take<uint32_t>(2 * E);
     auto queue_dep = cv.take<int>(2 + E);
+    const int64_t Is = c.shared_intermediate;
+    auto shared_act = cv.take<__nv_bfloat16>(Is > 0 ? T * Is : 0);
+    auto shared_out = cv.take<__nv_bfloat16>(Is > 0 ? T * H : 0);
+    auto shared_ones = cv.take<__nv_bfloat16>(Is > 0 ? T : 0);
+    auto shared_group = cv.take<GemmGroup>(Is > 0 ? 1 : 0);
     if (L) {
       L->dest = dest; L->fetches = fetches; L->n_fetches = n_fetches; L->counts = counts;
       L->errs = errs; L->layer_slot = layer_slot; L->send_idx = send_idx; L->send_ids = send_ids;
@@ -181,6 +192,10 @@ static int64_t workspace_bytes(const ferryb_layer_config& c, uint8_t* base, ferr
       L->peer_base_dev = peer_base;
       L->ready = ready;
       L->queue_dep = queue_dep;
+      if (Is > 0) {
+        L->shared_act = shared_act; L->shared_out = shared_out; L->shared_ones = shared_ones;
+        L->shared_group = shared_group;
+      }
     }
   });
 }
@@ -244,6 +259,15 @@ extern "C" int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_
   FB_CUDA(cudaMemset(workspace, 0, (size_t)workspace_size));
   FB_CUDA(cudaMemcpy(L->peer_base_dev, peer_bases, sizeof(uint64_t) * cfg->world,
                      cudaMemcpyHostToDevice));
+  L->shared_w.assign((size_t)planner->layers, nullptr);
+  if (cfg->shared_intermediate > 0) {
+    // one group over every local token, routing weight 1 (exact in bf16)
+    std::vector<__nv_bfloat16> ones((size_t)cfg->tokens_per_rank, __float2bfloat16(1.0f));
+    FB_CUDA(cudaMemcpy(L->shared_ones, ones.data(), ones.size() * sizeof(__nv_bfloat16),
+                       cudaMemcpyHostToDevice));
+    const GemmGroup g{0, 0, cfg->tokens_per_rank, 0};
+    FB_CUDA(cudaMemcpy(L->shared_group, &g, sizeof(g), cudaMemcpyHostToDevice));
+  }
   FB_CUDA(cudaHostAlloc(&L->summary_host, sizeof(ferryb_layout_summary), cudaHostAllocDefault));
   FB_CUDA(cudaHostAlloc(&L->errs_host, 8 * sizeof(int32_t), cudaHostAllocDefault));
   FB_CUDA(cudaEventCreateWithFlags(&L->summary_ev, cudaEventDisableTiming));
@@ -296,6 +320,11 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   const int parity = (int)(event & 1);
   const uint64_t seq = (uint64_t)event + 1;
   const bool timing = c.timing != 0;
+  // the shared expert belongs to the whole MoE block (forward), not to the
+  // reference's execute, whose caller adds it
+  const void* shared = (c.shared_intermediate > 0 && !given_selected) ? L->shared_w[layer] : nullptr;
+  FB_CHECK_ARG(!shared || reinterpret_cast<uintptr_t>(hidden) % 16 == 0,
+               "layer_forward: hidden must be 16-byte aligned with shared experts");
   uint8_t* half = L->symm + parity * L->sl.half;
   int64_t launches = 0;
   using clk = std::chrono::steady_clock;
@@ -425,8 +454,9 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   host_mark(1);
 
   // 6-7 dispatch + permute
-  const FusedArgs fa = fused_args(L, parity, static_cast<const __nv_bfloat16*>(hidden),
-                                  static_cast<__nv_bfloat16*>(out));
+  FusedArgs fa = fused_args(L, parity, static_cast<const __nv_bfloat16*>(hidden),
+                            static_cast<__nv_bfloat16*>(out));
+  if (shared) fa.addend = L->shared_out;
   if ((s = fused_dispatch(fa, seq, stream))) return s;
   if ((s = fused_permute(fa, seq, sum.n_routes, stream))) return s;
   launches += 2 + (c.world > 1 ? 1 : 0);  // dispatch (+ signal) + permute
@@ -440,6 +470,14 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
                                L->route_w, L->act, L->expert_out, L->errs + 2, stream)))
     return s;
   if (sum.n_hit) launches += 1;
+  if (shared) {  // dense shared expert on every local token, in the copies' shadow
+    if ((s = swiglu_grouped(shared, 1, L->shared_group, 1, c.tokens_per_rank,
+                            static_cast<const __nv_bfloat16*>(hidden), L->shared_ones,
+                            L->shared_act, L->shared_out, c.hidden, c.shared_intermediate,
+                            L->errs + 2, stream)))
+      return s;
+    launches += 2;
+  }
   if (timing) FB_CUDA(cudaEventRecord(L->tev[3], stream));
   host_mark(3);
   if (c.sync_fetch) {
@@ -547,6 +585,18 @@ extern "C" int ferryb_layer_execute(ferryb_layer* L, int64_t event, int32_t laye
                "layer_execute: probability score needs probs_tail rows");
   return layer_forward(L, event, layer, hidden, nullptr, nullptr, selected, weights, probs_tail,
                        n_probs_tail, out, nullptr, nullptr, stream);
+}
+
+extern "C" int ferryb_layer_set_shared(ferryb_layer* L, int32_t moe_layer, const void* weights) {
+  FB_CHECK_ARG(L, "layer_set_shared: null layer");
+  FB_CHECK_ARG(L->cfg.shared_intermediate > 0, "layer_set_shared: the layer was created without "
+               "shared experts (shared_intermediate = 0)");
+  FB_CHECK_ARG(moe_layer >= 0 && moe_layer < (int32_t)L->shared_w.size(),
+               "layer_set_shared: layer %d out of range", moe_layer);
+  FB_CHECK_ARG(reinterpret_cast<uintptr_t>(weights) % 16 == 0,
+               "layer_set_shared: weights must be 16-byte aligned");
+  L->shared_w[moe_layer] = weights;
+  return FERRYB_OK;
 }
 
 extern "C" int ferryb_layer_get_stats(const ferryb_layer* L, ferryb_layer_stats* out) {

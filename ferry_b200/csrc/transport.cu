@@ -27,7 +27,19 @@ __device__ __forceinline__ bool wait_flags(const uint64_t* flags, int n, uint64_
 }
 
 // ---------------------------------------------------------------------------
-// Compat: pack_dispatch.  One CTA per packet.
+// Compat: pack_dispatch / unpack_dispatch.  One CTA per packet.  A packet is
+// [hidden bf16 x H | weights bf16 x K | ids u8 x K] with no padding
+// (2H + 3K bytes, ferry/csrc/expert_ops.cpp:50-73), so packet rows are only
+// as aligned as that stride: the hidden bytes move in pieces of V bytes, V the
+// largest power of two <= 8 dividing the stride and the packet base (chosen
+// on the host), and the bf16 weights move bytewise.
+template <class V>
+__device__ __forceinline__ void copy_pieces(uint8_t* dst, const uint8_t* src, int64_t bytes) {
+  for (int64_t v = threadIdx.x; v < bytes / (int64_t)sizeof(V); v += blockDim.x)
+    reinterpret_cast<V*>(dst)[v] = reinterpret_cast<const V*>(src)[v];
+}
+
+template <class V>
 __global__ void pack_dispatch_kernel(const __nv_bfloat16* __restrict__ hidden, int64_t tokens,
                                      int64_t H, const int64_t* __restrict__ selected,
                                      const __nv_bfloat16* __restrict__ weights, int64_t K_sel,
@@ -42,10 +54,7 @@ __global__ void pack_dispatch_kernel(const __nv_bfloat16* __restrict__ hidden, i
     if (threadIdx.x == 0) atomicCAS(err, 0, DEV_BAD_INPUT);
     return;
   }
-  // hidden bytes: 8-byte pieces (the packet stride is a multiple of 8 when H is)
-  const uint2* src = reinterpret_cast<const uint2*>(hidden + t * H);
-  uint2* dst = reinterpret_cast<uint2*>(row);
-  for (int64_t v = threadIdx.x; v < H / 4; v += blockDim.x) dst[v] = src[v];
+  copy_pieces<V>(row, reinterpret_cast<const uint8_t*>(hidden + t * H), 2 * H);
   if (threadIdx.x < K) {
     const int j = threadIdx.x;
     const int64_t e = send_ids[i * K + j];
@@ -58,20 +67,34 @@ __global__ void pack_dispatch_kernel(const __nv_bfloat16* __restrict__ hidden, i
         if (selected[t * K_sel + jj] == e) acc += __bfloat162float(weights[t * K_sel + jj]);
       w = __float2bfloat16_rn(acc);
     }
-    reinterpret_cast<__nv_bfloat16*>(row + 2 * H)[j] = w;
+    const uint16_t bits = __bfloat16_as_ushort(w);
+    row[2 * H + 2 * j] = static_cast<uint8_t>(bits & 0xff);
+    row[2 * H + 2 * j + 1] = static_cast<uint8_t>(bits >> 8);
     row[2 * H + 2 * K + j] = static_cast<uint8_t>(e);
   }
 }
 
+template <class V>
 __global__ void unpack_dispatch_kernel(const uint8_t* __restrict__ raw, int64_t m, int64_t H,
                                        int64_t K, __nv_bfloat16* __restrict__ x,
                                        __nv_bfloat16* __restrict__ w) {
   const int64_t i = blockIdx.x;
   const uint8_t* row = raw + i * (2 * H + 3 * K);
-  const uint2* src = reinterpret_cast<const uint2*>(row);
-  uint2* dst = reinterpret_cast<uint2*>(x + i * H);
-  for (int64_t v = threadIdx.x; v < H / 4; v += blockDim.x) dst[v] = src[v];
-  if (threadIdx.x < K) w[i * K + threadIdx.x] = reinterpret_cast<const __nv_bfloat16*>(row + 2 * H)[threadIdx.x];
+  copy_pieces<V>(reinterpret_cast<uint8_t*>(x + i * H), row, 2 * H);
+  if (threadIdx.x < K) {
+    const int j = threadIdx.x;
+    const uint16_t bits = static_cast<uint16_t>(row[2 * H + 2 * j]) |
+                          static_cast<uint16_t>(row[2 * H + 2 * j + 1]) << 8;
+    w[i * K + j] = __ushort_as_bfloat16(bits);
+  }
+}
+
+// largest power of two <= 8 dividing the packet stride and both bases (hidden
+// rows are 2H bytes apart, a multiple of 8)
+static int packet_align(int64_t stride, const void* packets, const void* rows) {
+  const uint64_t v = static_cast<uint64_t>(stride) | reinterpret_cast<uintptr_t>(packets) |
+                     reinterpret_cast<uintptr_t>(rows) | 8u;
+  return static_cast<int>(v & (~v + 1));
 }
 
 // ---------------------------------------------------------------------------
@@ -290,6 +313,14 @@ __global__ void fused_permute_kernel(const FusedArgs a, uint64_t seq) {
   }
 }
 
+// o = bf16(float(o) + float(b)) lane-wise (a torch bf16 add)
+__device__ __forceinline__ void add_bf16x8(uint4& o, const uint4 b) {
+  __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
+  const __nv_bfloat16* be = reinterpret_cast<const __nv_bfloat16*>(&b);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) oe[q] = __float2bfloat16_rn(__bfloat162float(oe[q]) + __bfloat162float(be[q]));
+}
+
 // combine (owner side): per receive row, bf16(sum over its routes in ascending
 // expert order of float(out[route])), stored to the source rank's return
 // buffer -- or, with one rank, straight into the layer output.
@@ -301,8 +332,10 @@ __global__ void fused_combine_kernel(const FusedArgs a) {
   const int g = a.recv_token[row];
   const int src = g / a.tokens_per_rank, t = g % a.tokens_per_rank;
   __nv_bfloat16* dst;
+  const __nv_bfloat16* add = nullptr;
   if (a.world == 1) {
     dst = a.out + (size_t)t * H;
+    if (a.addend) add = a.addend + (size_t)t * H;
   } else {
     uint8_t* base = reinterpret_cast<uint8_t*>(a.peer_base[src]) + a.parity * a.buf_stride;
     dst = reinterpret_cast<__nv_bfloat16*>(base + a.off_ret) +
@@ -329,6 +362,7 @@ __global__ void fused_combine_kernel(const FusedArgs a) {
     __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
 #pragma unroll
     for (int q = 0; q < 8; ++q) oe[q] = __float2bfloat16_rn(acc[q]);
+    if (add) add_bf16x8(o, *reinterpret_cast<const uint4*>(add + c));
     *reinterpret_cast<uint4*>(dst + c) = o;
   }
 }
@@ -360,6 +394,7 @@ __global__ void fused_final_kernel(const FusedArgs a, uint64_t seq) {
     __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
 #pragma unroll
     for (int q = 0; q < 8; ++q) oe[q] = __float2bfloat16_rn(acc[q]);
+    if (a.addend) add_bf16x8(o, *reinterpret_cast<const uint4*>(a.addend + (size_t)t * H + c));
     *reinterpret_cast<uint4*>(a.out + (size_t)t * H + c) = o;
   }
 }
@@ -406,10 +441,16 @@ extern "C" int ferryb_pack_dispatch(const void* hidden, int64_t tokens, int64_t 
   if (n_packets == 0) return FERRYB_OK;
   FB_CHECK_ARG(hidden && selected && weights && send_idx && send_ids && payload && err,
                "pack_dispatch: null pointer");
-  pack_dispatch_kernel<<<(unsigned)n_packets, 256, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(hidden), tokens, hidden_dim, selected,
-      static_cast<const __nv_bfloat16*>(weights), topk, send_idx, send_ids, topk, experts,
-      static_cast<uint8_t*>(payload), err);
+  const auto* hid = static_cast<const __nv_bfloat16*>(hidden);
+  const auto* wts = static_cast<const __nv_bfloat16*>(weights);
+  auto* out = static_cast<uint8_t*>(payload);
+  const unsigned grid = (unsigned)n_packets;
+  switch (packet_align(2 * hidden_dim + 3 * topk, payload, hidden)) {
+    case 8: pack_dispatch_kernel<uint2><<<grid, 256, 0, stream>>>(hid, tokens, hidden_dim, selected, wts, topk, send_idx, send_ids, topk, experts, out, err); break;
+    case 4: pack_dispatch_kernel<uint32_t><<<grid, 256, 0, stream>>>(hid, tokens, hidden_dim, selected, wts, topk, send_idx, send_ids, topk, experts, out, err); break;
+    case 2: pack_dispatch_kernel<uint16_t><<<grid, 256, 0, stream>>>(hid, tokens, hidden_dim, selected, wts, topk, send_idx, send_ids, topk, experts, out, err); break;
+    default: pack_dispatch_kernel<uint8_t><<<grid, 256, 0, stream>>>(hid, tokens, hidden_dim, selected, wts, topk, send_idx, send_ids, topk, experts, out, err); break;
+  }
   FB_LAUNCH_CHECK();
   return FERRYB_OK;
 }
@@ -418,10 +459,16 @@ extern "C" int ferryb_unpack_dispatch(const void* raw, int64_t m, int64_t hidden
                                       void* x, void* w, cudaStream_t stream) {
   FB_CHECK_ARG(hidden_dim % 4 == 0 && topk >= 1 && topk <= 256 && m >= 0, "unpack: bad sizes");
   if (m == 0) return FERRYB_OK;
-  unpack_dispatch_kernel<<<(unsigned)m, 256, 0, stream>>>(static_cast<const uint8_t*>(raw), m,
-                                                          hidden_dim, topk,
-                                                          static_cast<__nv_bfloat16*>(x),
-                                                          static_cast<__nv_bfloat16*>(w));
+  const auto* src = static_cast<const uint8_t*>(raw);
+  auto* xo = static_cast<__nv_bfloat16*>(x);
+  auto* wo = static_cast<__nv_bfloat16*>(w);
+  const unsigned grid = (unsigned)m;
+  switch (packet_align(2 * hidden_dim + 3 * topk, raw, x)) {
+    case 8: unpack_dispatch_kernel<uint2><<<grid, 256, 0, stream>>>(src, m, hidden_dim, topk, xo, wo); break;
+    case 4: unpack_dispatch_kernel<uint32_t><<<grid, 256, 0, stream>>>(src, m, hidden_dim, topk, xo, wo); break;
+    case 2: unpack_dispatch_kernel<uint16_t><<<grid, 256, 0, stream>>>(src, m, hidden_dim, topk, xo, wo); break;
+    default: unpack_dispatch_kernel<uint8_t><<<grid, 256, 0, stream>>>(src, m, hidden_dim, topk, xo, wo); break;
+  }
   FB_LAUNCH_CHECK();
   return FERRYB_OK;
 }

@@ -40,6 +40,7 @@ struct FusedArgs {
   __nv_bfloat16* route_w;     // [routes]
   const __nv_bfloat16* expert_out;  // [routes, H]
   __nv_bfloat16* out;         // [T, H]
+  const __nv_bfloat16* addend;  // [T, H] or null: out = bf16(bf16(routed) + addend)
   int* err;
 };
 

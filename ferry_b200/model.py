@@ -9,6 +9,8 @@ import json
 from dataclasses import dataclass
 from pathlib import Path
 
+import torch
+
 
 @dataclass(frozen=True)
 class ModelSpec:
@@ -18,6 +20,7 @@ class ModelSpec:
     topk: int
     hidden: int
     intermediate: int      # routed-expert intermediate size
+    shared_intermediate: int = 0  # DeepSeek-V2 shared experts as one MLP (n_shared * moe_intermediate)
 
     @property
     def layers(self):
@@ -56,8 +59,15 @@ def spec_from_config(c):
             raise NotImplementedError('only greedy top-k routing is supported for DeepSeek-V2')
     else:
         raise NotImplementedError(f'unsupported model_type {kind}')
+    shared = (c.get('n_shared_experts') or 0) * c['moe_intermediate_size'] if kind == 'deepseek_v2' else 0
     return ModelSpec(kind, layers, experts, c['num_experts_per_tok'], c['hidden_size'],
-                     c['moe_intermediate_size'])
+                     c['moe_intermediate_size'], shared)
+
+
+def pack_expert(gate_w, up_w, down_w):
+    """One expert (or shared-expert MLP) as a cache/pool row: [gate I x H | up
+    I x H | down H x I] of the nn.Linear weights (ferry/model.py:88)."""
+    return torch.cat([gate_w.reshape(-1), up_w.reshape(-1), down_w.reshape(-1)]).to(torch.bfloat16)
 
 
 def read_spec(model_path):

@@ -47,6 +47,7 @@ class _Executor:
         cfg.probability_score = int(rt.eviction_score == 'probability')
         cfg.timing = int(rt.timing)
         cfg.sync_fetch = int(rt.sync_fetch)
+        cfg.shared_intermediate = rt.shared_intermediate
         self.cfg = cfg
         lib = _lib.lib()
         ws_bytes = lib.ferryb_layer_workspace_bytes(ctypes.byref(cfg))
@@ -60,6 +61,9 @@ class _Executor:
              ptr(rt.cache), rt.cache.shape[0], rt.h2d.handle, ctypes.c_void_p(self.symm.local),
              self.symm.bases_c, ptr(self.workspace), ws_bytes, ctypes.byref(h))
         self.h = h
+        for layer, w in enumerate(rt.shared_experts or ()):
+            if w is not None:
+                call('ferryb_layer_set_shared', h, layer, ptr(w))
 
     def stats(self):
         st = _lib.LayerStats()
@@ -77,9 +81,23 @@ class OffloadRuntime:
     def __init__(self, spec, pool, capacities, policy, topology, history_window=128,
                  balance_tol_bps=200, salt=1, eviction_score='frequency', *, n_copy_streams=1,
                  norm_topk_prob=True, routed_scaling_factor=1.0, timing=False, group=None,
-                 device=None, sync_fetch=False):
+                 device=None, sync_fetch=False, shared_experts=None):
+        """shared_experts: per MoE layer, the DeepSeek-V2 shared-expert MLP as one
+        bf16 device row (ferry_b200.model.pack_expert) or None; forward() adds
+        it to the routed output, execute() leaves it to the caller as the
+        reference does."""
         self.spec = spec
         self.sync_fetch = sync_fetch
+        self.shared_experts = list(shared_experts) if shared_experts is not None else None
+        self.shared_intermediate = 0
+        if self.shared_experts:
+            sizes = {w.numel() for w in self.shared_experts if w is not None}
+            if len(sizes) != 1 or next(iter(sizes)) % (3 * spec.hidden):
+                raise ValueError('shared experts must be equal-size [3 * hidden * I] rows')
+            self.shared_intermediate = next(iter(sizes)) // (3 * spec.hidden)
+            for w in self.shared_experts:
+                if w is not None and (w.dtype != torch.bfloat16 or not w.is_cuda or not w.is_contiguous()):
+                    raise ValueError('shared experts must be contiguous bf16 CUDA tensors')
         self.pool = pool
         self.group = group
         self.rank, self.world = _rank_world(group)

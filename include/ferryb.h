@@ -316,6 +316,34 @@ FERRYB_API int ferryb_symm_close(void* peer_ptr);
 FERRYB_API int ferryb_symm_free(void* ptr);
 
 /* ------------------------------------------------------------------------
+ * Routing metadata for callers composing their own layer flow (the fused
+ * executor does this inside kernels 1-2).
+ *
+ * GateHistory.update / .scores (ferry/metadata.py:15-38) on device state:
+ * rows [layers, window, experts] float64, count/head [layers] int64, all
+ * zero initially.  update: probs [n_rows, experts] float64 (device). */
+FERRYB_API int ferryb_history_update(double* rows, int64_t* count, int64_t* head, int32_t layers,
+                                     int32_t window, int32_t experts, int32_t layer,
+                                     const double* probs, int64_t n_rows, ferryb_stream_t stream);
+/* out [experts] float32 = float32(sum of the layer's ring rows / max(1, count)) */
+FERRYB_API int ferryb_history_scores(const double* rows, const int64_t* count, int32_t layers,
+                                     int32_t window, int32_t experts, int32_t layer, float* out,
+                                     ferryb_stream_t stream);
+/* RouteGather.collect's all-gather (ferry/metadata.py:67-76) over symmetric
+ * buffers: copies `bytes` of src (device) into every rank's buffer at
+ * offset + rank * bytes, then stores `seq` into every rank's flag word
+ * flag_offset + 8 * rank (system-scope release).  peer_bases: DEVICE array
+ * [world] of the buffers' addresses as mapped in this process. */
+FERRYB_API int ferryb_symm_allgather(const uint64_t* peer_bases, int32_t world, int32_t rank,
+                                     int64_t offset, const void* src, int64_t bytes,
+                                     int64_t flag_offset, uint64_t seq, ferryb_stream_t stream);
+/* Waits (on the GPU, at most 2 s) until all `world` flag words at
+ * local_base + flag_offset reach seq; on time-out sets *err (device int32) to
+ * a non-zero code instead. */
+FERRYB_API int ferryb_symm_wait(const void* local_base, int64_t flag_offset, int32_t world,
+                                uint64_t seq, int32_t* err, ferryb_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * The fused per-layer executor.  Replaces OffloadRuntime.execute
  * (ferry/runtime.py:64-89) together with the MoE hook's router
  * (ferry/model.py:137-148).  One call runs, on this rank: router + all-gather
@@ -338,6 +366,10 @@ typedef struct ferryb_layer_config {
                                 stream wait for them before the fetched-expert GEMM (for
                                 profilers that serialise GPU work, e.g. ncu); 0: the GEMM
                                 waits on the device for each copy's readiness flag */
+  int32_t shared_intermediate; /* > 0: dense shared-expert SwiGLU of this intermediate size
+                                added to every token's output (DeepSeek-V2 shared experts,
+                                transformers DeepseekV2MLP outside ferry/model.py:151-158);
+                                weights per MoE layer via ferryb_layer_set_shared */
 } ferryb_layer_config;
 
 typedef struct ferryb_layer_stats {
@@ -393,6 +425,15 @@ FERRYB_API int ferryb_layer_collect_timing(ferryb_layer* layer);
 /* The plan summary of the last layer run (fetch list, per-rank counts). */
 FERRYB_API int ferryb_layer_last_summary(const ferryb_layer* layer, ferryb_layout_summary* out);
 FERRYB_API int ferryb_layer_reset_stats(ferryb_layer* layer);
+/* Shared-expert weights of one MoE layer: device bf16 [3 * hidden *
+ * shared_intermediate] laid out [gate I x H | up I x H | down H x I] (row-
+ * major nn.Linear weights), or NULL to clear.  Borrowed: the caller keeps
+ * them alive while the layer runs.  ferryb_layer_forward (the whole MoE
+ * block) runs them on every local token while the layer's expert copies
+ * stream and adds bf16(routed) + bf16(shared) into the output (a torch bf16
+ * add); ferryb_layer_execute (the reference's execute, whose caller adds the
+ * shared expert itself) does not. */
+FERRYB_API int ferryb_layer_set_shared(ferryb_layer* layer, int32_t moe_layer, const void* weights);
 FERRYB_API int ferryb_layer_destroy(ferryb_layer* layer);
 
 #ifdef __cplusplus

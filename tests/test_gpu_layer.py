@@ -116,3 +116,44 @@ def test_reset_and_counters():
     want, _, _ = orc.execute(0, [x], [sel], [w])
     assert_bf16_close(got.cpu(), want[0], 'after reset')
     rt.close()
+
+
+def test_forward_deepseek_shared_experts():
+    """DeepSeek-V2-Lite MoE block through forward(): the greedy softmax router in
+    kernel 1, routed experts, and the two shared experts (one 2816-wide MLP) run
+    in the copies' shadow and added as transformers does (bf16 add); execute()
+    leaves the shared expert out, as the reference's execute does."""
+    from ferry_b200.model import ModelSpec, pack_expert
+    from ferry_b200.quota import Topology
+    from ferry_b200.runtime import OffloadRuntime
+    from ferry_b200.workload import cpu_pool
+    E, K, H, I, Is, T, cap, layers = 64, 6, 2048, 1408, 2816, 16, 60, 2
+    spec = ModelSpec('deepseek_v2', tuple(range(layers)), E, K, H, I, Is)
+    pool = cpu_pool(spec, layers, 11).pin_memory()
+    g = torch.Generator().manual_seed(12)
+    gates = [(torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16) for _ in range(layers)]
+    shared = [[(torch.randn(*shp, generator=g) * 0.02).to(torch.bfloat16)
+               for shp in ((Is, H), (Is, H), (H, Is))] for _ in range(layers)]
+    rows = [pack_expert(*s).to(DEV) for s in shared]
+    topo = Topology.uniform(1, E)
+    rt = OffloadRuntime(spec, pool, [cap], 'ferry', topo, norm_topk_prob=False, shared_experts=rows)
+    orc = OracleRuntime(spec, pool, [cap], 'ferry', topo.masks, topo.seconds, topo.lut)
+    for step in range(4):
+        layer = step % layers
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        sel_out = torch.empty((T, K), dtype=torch.int64, device=DEV)
+        w_out = torch.empty((T, K), dtype=torch.bfloat16, device=DEV)
+        got = rt.forward(layer, x.to(DEV), gates[layer].to(DEV), None, sel_out, w_out)
+        torch.cuda.synchronize()
+        routed, _, _ = orc.execute(layer, [x], [sel_out.cpu()], [w_out.cpu()])
+        want = (routed[0].float() + ref_ops.shared_expert(x, *shared[layer]).float()).to(torch.bfloat16)
+        assert_bf16_close(got.cpu(), want, f'forward+shared step {step}')
+        np.testing.assert_array_equal(rt.controller.slots, orc.ctl.slots)
+    # execute(): routed experts only
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    sel, w, _ = ref_ops.route_deepseek(x, gates[0].float(), K, 1.0, None)
+    got = rt.execute(0, x.to(DEV), sel.to(DEV), w.to(DEV), None)
+    torch.cuda.synchronize()
+    want, _, _ = orc.execute(0, [x], [sel], [w])
+    assert_bf16_close(got.cpu(), want[0], 'execute without shared')
+    rt.close()

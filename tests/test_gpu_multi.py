@@ -96,3 +96,54 @@ def test_two_gpu_execute_matches_oracle(case):
         np.testing.assert_array_equal(res[r]['owner'], orc.ctl.owner)
         np.testing.assert_array_equal(res[r]['fetches'], orc.fetches_per_rank)
     assert res[0]['dispatch_bytes'] > 0
+
+
+def _gather_worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from ferry_b200.metadata import RouteGather
+    torch.cuda.set_device(rank)
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    res = {}
+    for score in ('frequency', 'probability'):
+        rg = RouteGather(8, 128, 128, score)
+        for step, tokens in enumerate((64, 64, 5, 64)):  # parity halves alternate; sizes change
+            g = torch.Generator().manual_seed(1000 * step + rank)
+            sel = torch.stack([torch.randperm(128, generator=g)[:8] for _ in range(tokens)])
+            probs = torch.softmax(torch.randn(tokens, 128, generator=g), -1)
+            res[(score, step)] = rg.collect(sel.cuda(), probs.cuda())
+        rg.close()
+    torch.save(res, os.path.join(out_dir, f'g{rank}.pt'))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_gpu_route_gather_p2p():
+    """RouteGather.collect over P2P stores into the peers' symmetric buffers:
+    every rank receives the reference's gathered view (ids rank-major,
+    origins, history rows of each rank's last tail tokens)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip('needs 2 GPUs')
+    from oracle import metadata as om
+    world = 2
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_gather_worker, args=(world, 29710, tmp), nprocs=world)
+        res = [torch.load(os.path.join(tmp, f'g{r}.pt'), weights_only=False) for r in range(world)]
+    for score in ('frequency', 'probability'):
+        for step, tokens in enumerate((64, 64, 5, 64)):
+            sels, probs = [], []
+            for r in range(world):
+                g = torch.Generator().manual_seed(1000 * step + r)
+                sels.append(torch.stack([torch.randperm(128, generator=g)[:8] for _ in range(tokens)]).numpy())
+                probs.append(torch.softmax(torch.randn(tokens, 128, generator=g), -1).numpy())
+            ids, origins = om.gather_ids(sels)
+            tail = om.history_tail(tokens, 128, world)
+            rows = (om.frequency_rows(ids, world, tokens, 128, 128) if score == 'frequency'
+                    else om.probability_rows([p[-tail:] for p in probs]))
+            for r in range(world):
+                got_ids, got_origins, got_rows = res[r][(score, step)]
+                np.testing.assert_array_equal(got_ids, ids)
+                np.testing.assert_array_equal(got_origins, origins)
+                np.testing.assert_array_equal(got_rows, rows)

@@ -1,0 +1,63 @@
+"""Host-side pieces with no GPU: model geometry (ferry/model.py:24-70 rules),
+the expert row layout, and the synthetic workload's router bias."""
+import math
+
+import pytest
+import torch
+
+from ferry_b200.model import DEEPSEEK_V2_LITE, QWEN3_30B_A3B, pack_expert, spec_from_config
+from ferry_b200.workload import zipf_bias
+
+
+def test_qwen3_spec():
+    s = spec_from_config(QWEN3_30B_A3B)
+    assert s.layers == 48 and s.moe_layers == tuple(range(48))
+    assert (s.experts, s.topk, s.hidden, s.intermediate) == (128, 8, 2048, 768)
+    assert s.shared_intermediate == 0
+    assert s.expert_bytes == 9_437_184
+    # global 30 % budget split with the remainder on the lower ranks
+    assert s.cache_slots(0.3, 1) == [1843]
+    assert s.cache_slots(0.3, 4) == [461, 461, 461, 460]
+    assert sum(s.cache_slots(0.3, 8)) == 1843
+
+
+def test_deepseek_spec():
+    s = spec_from_config(DEEPSEEK_V2_LITE)
+    assert s.layers == 26 and s.moe_layers[0] == 1  # first_k_dense_replace = 1
+    assert (s.experts, s.topk, s.intermediate) == (64, 6, 1408)
+    assert s.shared_intermediate == 2 * 1408
+    assert s.expert_bytes == 17_301_504
+    assert s.cache_slots(0.3, 4) == [125, 125, 125, 124]  # floor(0.3 * 26 * 64) = 499
+
+
+def test_spec_rejects_non_greedy_deepseek():
+    c = dict(DEEPSEEK_V2_LITE, topk_method='group_limited_greedy')
+    with pytest.raises(NotImplementedError):
+        spec_from_config(c)
+
+
+def test_qwen3_sparse_step_and_dense_layers():
+    c = dict(QWEN3_30B_A3B, num_hidden_layers=8, decoder_sparse_step=2, mlp_only_layers=[3])
+    assert spec_from_config(c).moe_layers == (1, 5, 7)
+
+
+def test_pack_expert_layout():
+    H, I = 8, 4
+    g = torch.arange(I * H, dtype=torch.float32).reshape(I, H)
+    u = g + 64  # small integers: exact in bf16
+    d = torch.arange(H * I, dtype=torch.float32).reshape(H, I) + 128
+    row = pack_expert(g, u, d)
+    assert row.dtype == torch.bfloat16 and row.numel() == 3 * H * I
+    assert torch.equal(row[:I * H].float(), g.reshape(-1))
+    assert torch.equal(row[I * H:2 * I * H].float(), u.reshape(-1))
+    assert torch.equal(row[2 * I * H:].float(), d.reshape(-1))
+
+
+def test_zipf_bias_is_log_of_normalised_zipf():
+    g = torch.Generator().manual_seed(0)
+    b = zipf_bias(64, 1.1, g)
+    p = torch.exp(b.double())
+    assert math.isclose(float(p.sum()), 1.0, rel_tol=1e-6)
+    ranks = torch.argsort(torch.argsort(-p)) + 1  # 1 = most popular
+    want = ranks.double() ** -1.1
+    assert torch.allclose(p, want / want.sum(), rtol=1e-5)
