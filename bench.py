@@ -285,6 +285,16 @@ def run_ours(a, rank, world, local):
                 'traffic': (round(traffic['dram_bytes_per_hit_expert'] * st.hit_experts / max(1, st.layers))
                             if traffic and st.hit_experts else None),
                 'traffic_note': (traffic.get('note') if traffic else 'no ncu capture committed')}
+    if st.hit_gemm_kernel_launches:
+        # the same launches on the device clock (earliest CTA start to latest CTA
+        # end): CUDA events on the compute stream also absorb the command-fetch
+        # delay the host link's saturating expert copies impose on every
+        # compute-stream command
+        clk_us = st.hit_gemm_kernel_us / st.hit_gemm_kernel_launches
+        clk = st.hit_weight_bytes / st.hit_gemm_kernel_launches / (clk_us * 1e-6) / 1e9
+        roofline['device_clock'] = {'achieved': round(clk, 1), 'frac': round(clk / hbm_gbs, 4),
+                                    'launch_us': round(clk_us, 1),
+                                    'event_launch_us': round(gemm_us / layers_timed, 1)}
     # per-layer roofline: slowest of host-link fetch, NVLink exchange, tensor FLOPs
     expert_bytes = spec.expert_bytes
     fetch_bytes = st.fetches * expert_bytes

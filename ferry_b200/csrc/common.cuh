@@ -141,7 +141,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2D TMA tile load (no multicast) into shared memory, completing on `bar`.
+// 2D TMA tile load into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t x, int32_t y) {
   asm volatile(

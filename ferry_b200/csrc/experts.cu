@@ -324,6 +324,7 @@ struct FusedParams {
   int* done;   // [1] CTAs finished; the last one zeroes queue/dep/done for the next launch
   int* dep;    // [n_groups] phase-1 epilogue-warp completions, zero at launch
   int* err;
+  unsigned long long* ts;  // null, or [2]: earliest CTA start / latest CTA end (globaltimer ns)
 };
 
 struct FusedItem {
@@ -424,6 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 4; ++i) { tma_prefetch_desc(&bx.m[i]); tma_prefetch_desc(&ba.m[i]); }
   }
   if (warp == 1) { tmem_alloc(tmem_base_smem, 512); tmem_relinquish(); }
+  if (p.ts && threadIdx.x == 0) atomicMin(&p.ts[0], (unsigned long long)globaltimer_ns());
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -613,6 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the last CTA to finish leaves the counters zeroed for the next launch on
   // this stream (every CTA is past its last claim and dependency read)
   if (threadIdx.x == 0) {
+    if (p.ts) atomicMax(&p.ts[1], (unsigned long long)globaltimer_ns());
     __threadfence();
     if (atomicAdd(p.done, 1) == (int)gridDim.x - 1) {
       for (int g = 0; g < p.n_groups; ++g) p.dep[g] = 0;
@@ -626,11 +629,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups, int n_hit,
                         const uint32_t* ready, uint32_t ready_value, int* queue_dep,
                         const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
-                        int* err, cudaStream_t stream) {
+                        int* err, cudaStream_t stream, unsigned long long* ts) {
   if (n_groups == 0) return FERRYB_OK;
   int device = 0;
   FB_CUDA(cudaGetDevice(&device));
   FusedParams p{};
+  p.ts = ts;
   p.groups = groups;
   p.n_groups = n_groups;
   p.n_hit = n_hit;

@@ -31,10 +31,12 @@ int swiglu_grouped_maps(const GemmMaps& m, const GemmGroup* groups, int n_groups
 // n_groups) are fetched experts whose tiles wait for ready[j] >= ready_value
 // (raised when fetch j has landed).  queue_dep: device
 // scratch of 2 + n_groups ints, zero before the first launch; every launch
-// leaves it zeroed again (its last CTA resets it).
+// leaves it zeroed again (its last CTA resets it).  ts: null, or device [2]
+// that the launch lowers to its earliest CTA start and raises to its latest CTA
+// end (globaltimer ns; start ~0 and end 0 beforehand).
 int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups, int n_hit,
                         const uint32_t* ready, uint32_t ready_value, int* queue_dep,
                         const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
-                        int* err, cudaStream_t stream);
+                        int* err, cudaStream_t stream, unsigned long long* ts = nullptr);
 
 }  // namespace ferryb

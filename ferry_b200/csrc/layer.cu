@@ -75,6 +75,11 @@ struct ferryb_layer {
   // ferryb_layer_collect_timing
   std::vector<cudaEvent_t> tev_pool;
   std::vector<char> tev_fetched;  // per timed layer: copy-lane events recorded
+  // device-clock span of each timed layer's cached-expert GEMM: starts[kTs]
+  // (initially ~0), ends[kTs] (initially 0), in the workspace
+  static constexpr int kTs = 512;
+  unsigned long long* gemm_ts = nullptr;
+  std::vector<char> ts_used;
   size_t tev_used = 0;
   cudaEvent_t* tev = nullptr;
   GemmMaps maps{};
@@ -175,6 +180,7 @@ static int64_t workspace_bytes(const ferryb_layer_config& c, uint8_t* base, ferr
     auto peer_base = cv.take<uintptr_t>(R);
     auto ready = cv.take<uint32_t>(2 * E);
     auto queue_dep = cv.take<int>(2 + E);
+    auto gemm_ts = cv.take<unsigned long long>(2 * ferryb_layer::kTs);
     const int64_t Is = c.shared_intermediate;
     auto shared_act = cv.take<__nv_bfloat16>(Is > 0 ? T * Is : 0);
     auto shared_out = cv.take<__nv_bfloat16>(Is > 0 ? T * H : 0);
@@ -192,6 +198,7 @@ static int64_t workspace_bytes(const ferryb_layer_config& c, uint8_t* base, ferr
       L->peer_base_dev = peer_base;
       L->ready = ready;
       L->queue_dep = queue_dep;
+      L->gemm_ts = gemm_ts;
       if (Is > 0) {
         L->shared_act = shared_act; L->shared_out = shared_out; L->shared_ones = shared_ones;
         L->shared_group = shared_group;
@@ -259,6 +266,12 @@ extern "C" int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_
   FB_CUDA(cudaMemset(workspace, 0, (size_t)workspace_size));
   FB_CUDA(cudaMemcpy(L->peer_base_dev, peer_bases, sizeof(uint64_t) * cfg->world,
                      cudaMemcpyHostToDevice));
+  {
+    std::vector<unsigned long long> ts(2 * ferryb_layer::kTs);
+    for (size_t i = 0; i < (size_t)ferryb_layer::kTs; ++i) { ts[2 * i] = ~0ull; ts[2 * i + 1] = 0; }
+    FB_CUDA(cudaMemcpy(L->gemm_ts, ts.data(), ts.size() * sizeof(unsigned long long),
+                       cudaMemcpyHostToDevice));
+  }
   L->shared_w.assign((size_t)planner->layers, nullptr);
   if (cfg->shared_intermediate > 0) {
     // one group over every local token, routing weight 1 (exact in bf16)
@@ -345,6 +358,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     L->tev = L->tev_pool.data() + L->tev_used;
     L->tev_used += 8;
     L->tev_fetched.push_back(0);
+    L->ts_used.push_back(0);
     FB_CUDA(cudaEventRecord(L->tev[0], stream));
   }
 
@@ -466,8 +480,14 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   // 8 grouped SwiGLU (kernel 5), both phases per launch: the experts cached
   //   before this layer (no waits), then the fetched experts, whose tiles
   //   start as their readiness flags arrive
+  unsigned long long* ts = nullptr;
+  if (timing && sum.n_hit > 0 && L->ts_used.size() <= (size_t)ferryb_layer::kTs) {
+    const size_t slot = L->ts_used.size() - 1;
+    ts = L->gemm_ts + 2 * slot;
+    L->ts_used.back() = 1;
+  }
   if ((s = swiglu_fused_launch(L->maps, L->groups, sum.n_hit, sum.n_hit, nullptr, 0, L->queue_dep,
-                               L->route_w, L->act, L->expert_out, L->errs + 2, stream)))
+                               L->route_w, L->act, L->expert_out, L->errs + 2, stream, ts)))
     return s;
   if (sum.n_hit) launches += 1;
   if (shared) {  // dense shared expert on every local token, in the copies' shadow
@@ -563,6 +583,20 @@ extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
     L->stats.timed_layers += 1;
   }
   L->tev_fetched.clear();
+  if (!L->ts_used.empty()) {
+    std::vector<unsigned long long> ts(2 * ferryb_layer::kTs);
+    FB_CUDA(cudaMemcpy(ts.data(), L->gemm_ts, ts.size() * sizeof(unsigned long long),
+                       cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < L->ts_used.size() && i < (size_t)ferryb_layer::kTs; ++i) {
+      if (!L->ts_used[i] || ts[2 * i + 1] < ts[2 * i]) continue;
+      L->stats.hit_gemm_kernel_us += (double)(ts[2 * i + 1] - ts[2 * i]) / 1000.0;
+      L->stats.hit_gemm_kernel_launches += 1;
+    }
+    for (size_t i = 0; i < (size_t)ferryb_layer::kTs; ++i) { ts[2 * i] = ~0ull; ts[2 * i + 1] = 0; }
+    FB_CUDA(cudaMemcpy(L->gemm_ts, ts.data(), ts.size() * sizeof(unsigned long long),
+                       cudaMemcpyHostToDevice));
+    L->ts_used.clear();
+  }
   L->tev_used = 0;
   return FERRYB_OK;
 }

@@ -4,7 +4,7 @@
 // it with a CUDA IPC handle; the handles are exchanged on the host (by the
 // caller, e.g. torch.distributed) and every rank opens its peers' buffers.
 // Kernels then read and write peers' memory directly over NVLink/NVSwitch.
-// Only plain loads and stores are used on peer memory (no TMA, no multicast).
+// Only plain loads and stores are used on peer memory (no TMA).
 #include <cstring>
 
 #include "common.cuh"

@@ -393,6 +393,9 @@ typedef struct ferryb_layer_stats {
                                 first copy start (the host round trip), first
                                 copy start -> last copy end, last copy end ->
                                 combine end (the compute tail) */
+  double hit_gemm_kernel_us; /* timing mode: cached-expert GEMM launches timed on the device
+                                clock (earliest CTA start to latest CTA end), summed */
+  int64_t hit_gemm_kernel_launches;
 } ferryb_layer_stats;
 
 typedef struct ferryb_layer ferryb_layer;
