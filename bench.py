@@ -60,6 +60,12 @@ def parse():
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--cpu-seconds', type=float, default=12.0)
+    p.add_argument('--ep-sweep', default='',
+                   help='comma-separated tokens per rank: time the EP dispatch + combine of one Qwen3 '
+                        'MoE layer with every expert cached (no fetches) instead of the decode bench')
+    p.add_argument('--per-rank-pool', action='store_true',
+                   help='one pinned expert pool per rank (the reference\'s layout) instead of one '
+                        'shared pool per node')
     p.add_argument('--sync-fetch', action='store_true',
                    help='issue each layer\'s copies before its fetched-expert GEMM and wait on '
                         'them from the stream (for profilers that serialise GPU work)')
@@ -208,9 +214,10 @@ def run_ours(a, rank, world, local):
     spec = qwen3_spec(a.layers)
     T, L = a.tokens, spec.layers
     caps = spec.cache_slots(a.cache_ratio, world)
-    pool_layers = auto_pool_layers(spec, world, a.pool_layers)
+    shared = world > 1 and not a.per_rank_pool
+    pool_layers = auto_pool_layers(spec, 1 if shared else world, a.pool_layers)
     t0 = time.time()
-    wl = SyntheticMoE(spec, seed=0, device=dev, pool_layers=pool_layers)
+    wl = SyntheticMoE(spec, seed=0, device=dev, pool_layers=pool_layers, shared=shared)
     setup_s = time.time() - t0
     topo = Topology.uniform(world, spec.experts)
     rt = OffloadRuntime(spec, wl.pool, caps, a.policy, topo, n_copy_streams=a.copy_streams,
@@ -324,7 +331,9 @@ def run_ours(a, rank, world, local):
                                '30% global expert cache, all experts in pinned host memory',
                    'model': 'Qwen3-30B-A3B MoE layers', 'moe_layers': L, 'global_batch': world * T,
                    'tokens_per_gpu': T, 'seq_len': 1, 'parallelism': f'dp{world}-ep{world}',
-                   'cache_slots_per_rank': caps, 'pool_layers': pool_layers, 'policy': a.policy,
+                   'cache_slots_per_rank': caps, 'pool_layers': pool_layers,
+                   'pool': 'one shared pinned pool per node' if shared else 'pinned pool per rank',
+                   'policy': a.policy,
                    'l2': 'no flush: each layer step reads > 126 MB of expert weights (> L2)'},
         'roofline': roofline, 'layer_roofline': layer_roofline, 'layer_split_us': split,
         'gpu_launches': int(st.launches), 'h2d_expert_copies': int(fetch_copies),
@@ -343,6 +352,58 @@ def run_ours(a, rank, world, local):
 
 
 # ---------------------------------------------------------------------------
+def run_ep_sweep(a, rank, world, local):
+    """BASELINE config 4's EP sweep: one Qwen3 MoE layer (top-8 of 128, Zipf
+    1.1 router bias), T tokens per rank, the 128 experts spread over the ranks'
+    caches (128 slots in all) so that, once warm, no step fetches: the step is
+    router + planner + layout + P2P dispatch + grouped GEMM + P2P combine.
+    Reports per T the dispatch (+ permute) and combine times (CUDA events on
+    the compute stream, max over ranks) and the NVLink bytes they move."""
+    from ferry_b200._lib import call
+    from ferry_b200.quota import Topology
+    from ferry_b200.runtime import OffloadRuntime
+    from ferry_b200.workload import SyntheticMoE
+    dev = torch.device('cuda', local)
+    spec = qwen3_spec(1)
+    caps = spec.cache_slots(1.0, world)
+    wl = SyntheticMoE(spec, seed=0, device=dev, shared=world > 1)
+    rt = OffloadRuntime(spec, wl.pool, caps, 'ferry', Topology.uniform(world, spec.experts), timing=True)
+    rows = []
+    for T in [int(t) for t in a.ep_sweep.split(',') if t]:
+        gen = torch.Generator(device=dev).manual_seed(100 + rank)
+        xs = [torch.randn(T, spec.hidden, generator=gen, device=dev).to(torch.bfloat16) for _ in range(4)]
+        for i in range(a.warmup):
+            rt.forward(0, xs[i % 4], wl.gate[0], wl.bias[0])
+        torch.cuda.synchronize()
+        ex = rt._executor(T)
+        call('ferryb_layer_collect_timing', ex.h)
+        call('ferryb_layer_reset_stats', ex.h)
+        barrier(world)
+        for i in range(a.steps):
+            rt.forward(0, xs[i % 4], wl.gate[0], wl.bias[0])
+        torch.cuda.synchronize()
+        call('ferryb_layer_collect_timing', ex.h)
+        st = ex.stats()
+        n = max(1, st.timed_layers)
+        disp = max_over_ranks(st.dispatch_permute_us / n, world)
+        comb = max_over_ranks(st.phase_us[4] / n, world)
+        layer = max_over_ranks(sum(st.phase_us[i] for i in range(5)) / n, world)
+        nvl = torch.tensor([float(st.dispatch_bytes + st.combine_bytes) / n], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(nvl)
+        fetches = max_over_ranks(float(st.fetches), world)
+        rows.append({'tokens_per_rank': T, 'dispatch_permute_us': round(disp, 1), 'combine_us': round(comb, 1),
+                     'layer_us': round(layer, 1), 'nvlink_bytes_all_ranks': int(nvl.item()),
+                     'nvlink_gbs_per_rank': round(float(nvl.item()) / world / ((disp + comb) * 1e-6) / 1e9, 1),
+                     'fetches_in_timed_steps': int(fetches)})
+    rt.close()
+    return {'metric': 'EP dispatch + combine of one Qwen3 MoE layer (P2P over NVSwitch)', 'n_gpus': world,
+            'steps': a.steps, 'warmup': a.warmup, 'dtype': 'bf16', 'data': 'synthetic',
+            'config': {'workload': 'config 4 EP sweep: H=2048, top-8 of 128, Zipf(1.1), all experts cached',
+                       'cache_slots_per_rank': caps},
+            'nvlink_peer_gbs_reference': 770.0, 'ep_sweep': rows}
+
+
 def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None):
     """Run the reference's CPU path (oracle port) over consecutive layers for
     about `seconds`; returns (layers_done, elapsed)."""
@@ -438,7 +499,7 @@ def main():
         return 0
     rank, world, local = init_dist(a.gpus)
     try:
-        result = run_ours(a, rank, world, local)
+        result = run_ep_sweep(a, rank, world, local) if a.ep_sweep else run_ours(a, rank, world, local)
         if rank == 0:
             print(json.dumps(result), flush=True)
     finally:

@@ -70,7 +70,7 @@ struct ferryb_layer {
   ferryb_layout_summary* summary_host = nullptr;
   int32_t* errs_host = nullptr;  // pinned copy of the device error words
   cudaEvent_t summary_ev = nullptr;
-  // timing mode: 8 events per layer (6 on the compute stream, 2 on the copy
+  // timing mode: 9 events per layer (7 on the compute stream, 2 on the copy
   // lane), recorded without host syncs and collected by
   // ferryb_layer_collect_timing
   std::vector<cudaEvent_t> tev_pool;
@@ -348,15 +348,15 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     h_prev = now;
   };
   if (timing) {
-    if (L->tev_used + 8 > L->tev_pool.size()) {
-      for (int i = 0; i < 8 * 64; ++i) {
+    if (L->tev_used + 9 > L->tev_pool.size()) {
+      for (int i = 0; i < 9 * 64; ++i) {
         cudaEvent_t e;
         FB_CUDA(cudaEventCreate(&e));
         L->tev_pool.push_back(e);
       }
     }
     L->tev = L->tev_pool.data() + L->tev_used;
-    L->tev_used += 8;
+    L->tev_used += 9;
     L->tev_fetched.push_back(0);
     L->ts_used.push_back(0);
     FB_CUDA(cudaEventRecord(L->tev[0], stream));
@@ -471,6 +471,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   FusedArgs fa = fused_args(L, parity, static_cast<const __nv_bfloat16*>(hidden),
                             static_cast<__nv_bfloat16*>(out));
   if (shared) fa.addend = L->shared_out;
+  if (timing) FB_CUDA(cudaEventRecord(L->tev[8], stream));
   if ((s = fused_dispatch(fa, seq, stream))) return s;
   if ((s = fused_permute(fa, seq, sum.n_routes, stream))) return s;
   launches += 2 + (c.world > 1 ? 1 : 0);  // dispatch (+ signal) + permute
@@ -563,7 +564,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
 
 extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
   FB_CHECK_ARG(L, "layer_collect_timing: null argument");
-  for (size_t b = 0; b + 8 <= L->tev_used; b += 8) {
+  for (size_t b = 0; b + 9 <= L->tev_used; b += 9) {
     cudaEvent_t* e = L->tev_pool.data() + b;
     FB_CUDA(cudaEventSynchronize(e[5]));
     for (int i = 0; i < 5; ++i) {
@@ -571,7 +572,12 @@ extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
       FB_CUDA(cudaEventElapsedTime(&ms, e[i], e[i + 1]));
       L->stats.phase_us[i] += ms * 1000.0;
     }
-    if (L->tev_fetched[b / 8]) {
+    {
+      float ms = 0.0f;
+      FB_CUDA(cudaEventElapsedTime(&ms, e[8], e[2]));
+      L->stats.dispatch_permute_us += ms * 1000.0;
+    }
+    if (L->tev_fetched[b / 9]) {
       const int pairs[3][2] = {{1, 6}, {6, 7}, {7, 5}};
       for (int i = 0; i < 3; ++i) {
         float ms = 0.0f;

@@ -31,7 +31,9 @@ def zipf_bias(experts, s, generator):
 
 class SyntheticMoE:
     def __init__(self, spec, *, seed=0, zipf_s=1.1, rho=0.5, device='cuda', pool_layers=None,
-                 build_pool=True):
+                 build_pool=True, shared=False, group=None):
+        """shared: one pool per node in shared pinned memory (ferry_b200.pool),
+        filled by the group's first rank, instead of one pinned pool per rank."""
         self.spec, self.rho, self.device = spec, rho, torch.device(device)
         E, H, L = spec.experts, spec.hidden, spec.layers
         g = torch.Generator().manual_seed(seed)
@@ -39,12 +41,23 @@ class SyntheticMoE:
                      for _ in range(L)]
         self.bias = [zipf_bias(E, zipf_s, g).to(self.device) for _ in range(L)]
         self.pool_layers = L if pool_layers is None else max(1, min(L, pool_layers))
-        self.pool = self._make_pool(seed + 1) if build_pool else None
+        self.shared_pool = None
+        self.pool = None
+        if build_pool:
+            rows = self.pool_layers * spec.experts
+            if shared:
+                from .pool import SharedPinnedPool
+                self.shared_pool = SharedPinnedPool(rows, spec.expert_elements,
+                                                    fill=lambda t: self._fill(t, seed + 1), group=group)
+                self.pool = self.shared_pool.tensor
+            else:
+                self.pool = torch.empty((rows, spec.expert_elements), dtype=torch.bfloat16, pin_memory=True)
+                self._fill(self.pool, seed + 1)
 
-    def _make_pool(self, seed):
+    def _fill(self, pool, seed):
+        """N(0, 0.02) bf16 rows drawn on the GPU from a seeded generator."""
         spec = self.spec
-        rows = self.pool_layers * spec.experts
-        pool = torch.empty((rows, spec.expert_elements), dtype=torch.bfloat16, pin_memory=True)
+        rows = pool.shape[0]
         gen = torch.Generator(device=self.device).manual_seed(seed)
         chunk = max(1, (1 << 30) // (spec.expert_elements * 2))
         for r0 in range(0, rows, chunk):

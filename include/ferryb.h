@@ -396,6 +396,9 @@ typedef struct ferryb_layer_stats {
   double hit_gemm_kernel_us; /* timing mode: cached-expert GEMM launches timed on the device
                                 clock (earliest CTA start to latest CTA end), summed */
   int64_t hit_gemm_kernel_launches;
+  double dispatch_permute_us; /* timing mode: dispatch (+ peer signal) and permute, from
+                                 after the host wait to the permute's end (waits for the
+                                 peers' packets included) */
 } ferryb_layer_stats;
 
 typedef struct ferryb_layer ferryb_layer;

@@ -141,3 +141,38 @@ def test_symmetric_handle_exchange_world2():
     assert res[0]['bases'][0] == 0x1000 and res[1]['bases'][1] == 0x2000
     assert res[0]['opened'] == [7] and res[1]['opened'] == [0]
     assert res[0]['bases'][1] == 0x100000 + 7 and res[1]['bases'][0] == 0x100000
+
+
+def _pool_worker(rank, world, port, out_dir):
+    """SharedPinnedPool over gloo with cudaHostRegister replaced (no GPU here):
+    every rank maps the same pages the first rank filled."""
+    import torch.distributed as dist
+    from ferry_b200 import pool as pool_mod
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    pool_mod.SharedPinnedPool._register = lambda self: None
+
+    def fill(t):
+        t.copy_(torch.arange(t.numel(), dtype=torch.float32).reshape(t.shape).to(torch.bfloat16))
+
+    sp = pool_mod.SharedPinnedPool(6, 40, fill=fill)
+    first = sp.tensor.clone()
+    dist.barrier()
+    if rank == world - 1:
+        sp.tensor[5, 39] = 7.0  # a write by one rank is seen by all
+    dist.barrier()
+    torch.save({'first': first, 'after': sp.tensor.clone()}, os.path.join(out_dir, f'p{rank}.pt'))
+    dist.barrier()
+    sp.close()
+    dist.destroy_process_group()
+
+
+def test_shared_pinned_pool_world3():
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_pool_worker, args=(3, 29654, tmp), nprocs=3)
+        res = [torch.load(os.path.join(tmp, f'p{r}.pt')) for r in range(3)]
+    want = torch.arange(240, dtype=torch.float32).reshape(6, 40).to(torch.bfloat16)
+    for r in range(3):
+        assert torch.equal(res[r]['first'], want)
+        assert float(res[r]['after'][5, 39]) == 7.0

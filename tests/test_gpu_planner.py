@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import planner as op
 from tests.goldens import PLAN_CASES, PlanCase, load
 
 pytestmark = pytest.mark.gpu
@@ -123,3 +124,22 @@ def test_demand_and_admission_capacity():
     np.testing.assert_array_equal(
         _admission_capacity(s['slots'], c.caps, s5['layer'], active, c.experts),
         op.admission_capacity(s['slots'], c.caps, s5['layer'], active, c.experts))
+
+
+@pytest.mark.parametrize('world,tokens,experts,topk', [(1, 2500, 16, 4), (4, 700, 128, 8), (8, 300, 64, 6)])
+def test_layout_multi_chunk_random(world, tokens, experts, topk):
+    """The layout kernel past one 1,024-token chunk (prefill-sized layers),
+    random destinations (including tokens with no route to some ranks),
+    bit-exact against the oracle's build_layout for every rank."""
+    from ferry_b200.layout import build_layout
+    rng = np.random.default_rng(world * 1000 + tokens)
+    n = world * tokens
+    sel = np.stack([rng.choice(experts, topk, replace=False) for _ in range(n)]).astype(np.int64)
+    owner = rng.integers(0, world, experts)
+    dest = owner[sel]
+    for r in range(world):
+        got = build_layout(sel, dest, tokens, r, experts)
+        want = op.build_layout(sel, dest, tokens, r, experts)
+        for g, w, name in zip(got, want, ['send_idx', 'send_ids', 'send_counts', 'recv_counts',
+                                          'starts', 'rows', 'cols']):
+            np.testing.assert_array_equal(g, w, err_msg=f'{name} rank {r}')
