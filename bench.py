@@ -63,6 +63,14 @@ def parse():
     p.add_argument('--ep-sweep', default='',
                    help='comma-separated tokens per rank: time the EP dispatch + combine of one Qwen3 '
                         'MoE layer with every expert cached (no fetches) instead of the decode bench')
+    p.add_argument('--full-model', choices=['qwen3', 'deepseek'],
+                   help='BASELINE configs 2-4: the whole model (transformers 5.5, random weights) with '
+                        'its MoE blocks on this runtime; reports TTFT, TPOT and decode tokens/s')
+    p.add_argument('--batch', type=int, default=64, help='--full-model: sequences per GPU')
+    p.add_argument('--prompt-len', type=int, default=1024, help='--full-model: input tokens')
+    p.add_argument('--new-tokens', type=int, default=64, help='--full-model: greedy output tokens')
+    p.add_argument('--topology', help='profiled topology JSON (ferry_b200.build_quota_lut) for N > 1; '
+                                      'default: uniform domains')
     p.add_argument('--per-rank-pool', action='store_true',
                    help='one pinned expert pool per rank (the reference\'s layout) instead of one '
                         'shared pool per node')
@@ -219,9 +227,16 @@ def run_ours(a, rank, world, local):
     t0 = time.time()
     wl = SyntheticMoE(spec, seed=0, device=dev, pool_layers=pool_layers, shared=shared)
     setup_s = time.time() - t0
-    topo = Topology.uniform(world, spec.experts)
+    topo = Topology(a.topology, world, spec.experts) if a.topology else Topology.uniform(world, spec.experts)
     rt = OffloadRuntime(spec, wl.pool, caps, a.policy, topo, n_copy_streams=a.copy_streams,
                         timing=True, sync_fetch=a.sync_fetch)
+    # this rank's link alone (ranks take turns), then with every rank copying at once
+    b_alone = 0.0
+    for r in range(world):
+        barrier(world)
+        if r == rank:
+            b_alone = host_link_gbs(rt.cache, wl.pool)
+    barrier(world)
     b_host = host_link_gbs(rt.cache, wl.pool)
     stream = wl.hidden_stream(T, seed=1, world=world, rank=rank)
     n_steps = a.warmup + a.steps
@@ -315,6 +330,10 @@ def run_ours(a, rank, world, local):
     layer_roofline = {'bound': ['host_link', 'nvlink', 'tensor'][int(np.argmax([t_host, t_nvl, t_flops]))],
                       'frac': round(t_roof / t_meas, 4) if t_meas > 0 else None,
                       'host_link_gbs_measured': round(b_host, 2),
+                      'host_link_gbs_alone': round(b_alone, 2),
+                      'host_link_note': 'measured with every rank copying at once (shared PCIe '
+                                        'switches / host memory); alone = this rank only',
+                      'topology': a.topology or 'uniform',
                       'fetch_gbs_achieved': round(fetch_bytes / t_meas / 1e9, 2),
                       'fetches_per_layer': st.fetches / max(1, st.layers),
                       'nvlink_bytes_per_layer': nvl_bytes / max(1, st.layers),
@@ -387,14 +406,16 @@ def run_ep_sweep(a, rank, world, local):
         n = max(1, st.timed_layers)
         disp = max_over_ranks(st.dispatch_permute_us / n, world)
         comb = max_over_ranks(st.phase_us[4] / n, world)
+        comb_store = max_over_ranks(st.combine_store_us / n, world)
         layer = max_over_ranks(sum(st.phase_us[i] for i in range(5)) / n, world)
         nvl = torch.tensor([float(st.dispatch_bytes + st.combine_bytes) / n], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(nvl)
         fetches = max_over_ranks(float(st.fetches), world)
-        rows.append({'tokens_per_rank': T, 'dispatch_permute_us': round(disp, 1), 'combine_us': round(comb, 1),
+        rows.append({'tokens_per_rank': T, 'dispatch_permute_us': round(disp, 1),
+                     'combine_store_us': round(comb_store, 1), 'combine_incl_peer_wait_us': round(comb, 1),
                      'layer_us': round(layer, 1), 'nvlink_bytes_all_ranks': int(nvl.item()),
-                     'nvlink_gbs_per_rank': round(float(nvl.item()) / world / ((disp + comb) * 1e-6) / 1e9, 1),
+                     'nvlink_gbs_per_rank': round(float(nvl.item()) / world / ((disp + comb_store) * 1e-6) / 1e9, 1),
                      'fetches_in_timed_steps': int(fetches)})
     rt.close()
     return {'metric': 'EP dispatch + combine of one Qwen3 MoE layer (P2P over NVSwitch)', 'n_gpus': world,
@@ -402,6 +423,33 @@ def run_ep_sweep(a, rank, world, local):
             'config': {'workload': 'config 4 EP sweep: H=2048, top-8 of 128, Zipf(1.1), all experts cached',
                        'cache_slots_per_rank': caps},
             'nvlink_peer_gbs_reference': 770.0, 'ep_sweep': rows}
+
+
+def run_full_model(a, rank, world, local):
+    """BASELINE configs 2-4 through ferry_b200.harness: seeded random prompts
+    (uniform token ids), one warm-up generation, then one timed generation."""
+    from ferry_b200.harness import run
+    from ferry_b200.model import DEEPSEEK_V2_LITE, QWEN3_30B_A3B
+    cfg = QWEN3_30B_A3B if a.full_model == 'qwen3' else DEEPSEEK_V2_LITE
+    dev = torch.device('cuda', local)
+    layers = a.layers if a.layers != 48 else None
+    model, rt, tokens, m = run(cfg, batch=a.batch, prompt_len=a.prompt_len, new_tokens=a.new_tokens,
+                               cache_ratio=a.cache_ratio, layers=layers, warmup=1, rank=rank, world=world,
+                               device=dev, policy=a.policy, topology=a.topology)
+    rt.close()
+    name = 'Qwen3-30B-A3B' if a.full_model == 'qwen3' else 'DeepSeek-V2-Lite'
+    return {'metric': f'decode tokens/s, full {name} (box, max over ranks)',
+            'value': m['decode_tokens_per_s'], 'unit': 'tokens/s', 'n_gpus': world, 'steps': a.new_tokens,
+            'warmup': 1, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
+            'data': 'synthetic: random-init weights, seeded uniform token ids',
+            'config': {'workload': f'config {"3/4" if a.full_model == "qwen3" else "2"}: full {name}',
+                       'batch_per_gpu': a.batch, 'prompt_len': a.prompt_len, 'new_tokens': a.new_tokens,
+                       'cache_ratio': a.cache_ratio, 'layers': layers or cfg['num_hidden_layers'],
+                       'policy': a.policy, 'topology': a.topology or 'uniform',
+                       'parallelism': f'dp{world}-ep{world}'},
+            'ttft_ms': round(m['ttft_ms'], 1), 'tpot_ms': round(m['tpot_ms'], 2),
+            'total_tokens_per_s': m['total_tokens_per_s'],
+            'fetches_per_rank': m['fetches_per_rank'], 'decode_fetches_per_rank': m['decode_fetches_per_rank']}
 
 
 def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None):
@@ -499,7 +547,12 @@ def main():
         return 0
     rank, world, local = init_dist(a.gpus)
     try:
-        result = run_ep_sweep(a, rank, world, local) if a.ep_sweep else run_ours(a, rank, world, local)
+        if a.ep_sweep:
+            result = run_ep_sweep(a, rank, world, local)
+        elif a.full_model:
+            result = run_full_model(a, rank, world, local)
+        else:
+            result = run_ours(a, rank, world, local)
         if rank == 0:
             print(json.dumps(result), flush=True)
     finally:

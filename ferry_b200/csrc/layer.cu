@@ -70,7 +70,7 @@ struct ferryb_layer {
   ferryb_layout_summary* summary_host = nullptr;
   int32_t* errs_host = nullptr;  // pinned copy of the device error words
   cudaEvent_t summary_ev = nullptr;
-  // timing mode: 9 events per layer (7 on the compute stream, 2 on the copy
+  // timing mode: 10 events per layer (8 on the compute stream, 2 on the copy
   // lane), recorded without host syncs and collected by
   // ferryb_layer_collect_timing
   std::vector<cudaEvent_t> tev_pool;
@@ -348,15 +348,15 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     h_prev = now;
   };
   if (timing) {
-    if (L->tev_used + 9 > L->tev_pool.size()) {
-      for (int i = 0; i < 9 * 64; ++i) {
+    if (L->tev_used + 10 > L->tev_pool.size()) {
+      for (int i = 0; i < 10 * 64; ++i) {
         cudaEvent_t e;
         FB_CUDA(cudaEventCreate(&e));
         L->tev_pool.push_back(e);
       }
     }
     L->tev = L->tev_pool.data() + L->tev_used;
-    L->tev_used += 9;
+    L->tev_used += 10;
     L->tev_fetched.push_back(0);
     L->ts_used.push_back(0);
     FB_CUDA(cudaEventRecord(L->tev[0], stream));
@@ -531,7 +531,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   host_mark(4);
 
   // 9 combine
-  if ((s = fused_combine(fa, seq, sum.n_recv, stream))) return s;
+  if ((s = fused_combine(fa, seq, sum.n_recv, stream, timing ? L->tev[9] : nullptr))) return s;
   launches += (sum.n_recv > 0 ? 1 : 0) + (c.world > 1 ? 2 : 0);  // combine (+ signal + final)
   if (timing) FB_CUDA(cudaEventRecord(L->tev[5], stream));
 
@@ -564,7 +564,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
 
 extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
   FB_CHECK_ARG(L, "layer_collect_timing: null argument");
-  for (size_t b = 0; b + 9 <= L->tev_used; b += 9) {
+  for (size_t b = 0; b + 10 <= L->tev_used; b += 10) {
     cudaEvent_t* e = L->tev_pool.data() + b;
     FB_CUDA(cudaEventSynchronize(e[5]));
     for (int i = 0; i < 5; ++i) {
@@ -577,7 +577,12 @@ extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
       FB_CUDA(cudaEventElapsedTime(&ms, e[8], e[2]));
       L->stats.dispatch_permute_us += ms * 1000.0;
     }
-    if (L->tev_fetched[b / 9]) {
+    {
+      float ms = 0.0f;
+      FB_CUDA(cudaEventElapsedTime(&ms, e[4], e[9]));
+      L->stats.combine_store_us += ms * 1000.0;
+    }
+    if (L->tev_fetched[b / 10]) {
       const int pairs[3][2] = {{1, 6}, {6, 7}, {7, 5}};
       for (int i = 0; i < 3; ++i) {
         float ms = 0.0f;

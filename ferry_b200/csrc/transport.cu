@@ -417,8 +417,10 @@ int fused_permute(const FusedArgs& a, uint64_t seq, int n_routes_hint, cudaStrea
 
 // With one rank every token has all its routes on this rank, so the combine
 // writes every output row.
-int fused_combine(const FusedArgs& a, uint64_t seq, int n_recv_hint, cudaStream_t stream) {
+int fused_combine(const FusedArgs& a, uint64_t seq, int n_recv_hint, cudaStream_t stream,
+                  cudaEvent_t after_stores) {
   if (n_recv_hint > 0) fused_combine_kernel<<<n_recv_hint, 256, 0, stream>>>(a);
+  if (after_stores) FB_CUDA(cudaEventRecord(after_stores, stream));
   if (a.world > 1) {
     signal_kernel<<<1, 32, 0, stream>>>(a, a.off_cflag, seq);
     if (a.tokens_per_rank > 0) fused_final_kernel<<<a.tokens_per_rank, 256, 0, stream>>>(a, seq);

@@ -47,7 +47,10 @@ struct FusedArgs {
 SymLayout sym_layout(int world, int tokens_per_rank, int topk, int hidden, int experts);
 int fused_dispatch(const FusedArgs& a, uint64_t seq, cudaStream_t stream);
 int fused_permute(const FusedArgs& a, uint64_t seq, int n_routes_hint, cudaStream_t stream);
-int fused_combine(const FusedArgs& a, uint64_t seq, int n_recv_hint, cudaStream_t stream);
+// after_stores (may be null): recorded once this rank's partials are stored,
+// before the wait for the peers' partials
+int fused_combine(const FusedArgs& a, uint64_t seq, int n_recv_hint, cudaStream_t stream,
+                  cudaEvent_t after_stores = nullptr);
 int ordered_segment_sum(const __nv_bfloat16* src, const int64_t* keys, int64_t n, int64_t n_keys,
                         int64_t H, __nv_bfloat16* dst, void* ws, int64_t ws_bytes,
                         cudaStream_t stream);

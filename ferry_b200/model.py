@@ -75,13 +75,19 @@ def read_spec(model_path):
 
 
 # BASELINE.json configs 1/3/4 (Qwen3-30B-A3B) and 0/2 (DeepSeek-V2-Lite).
+# (public model configs; the full-model harness builds them with random weights)
 QWEN3_30B_A3B = dict(model_type='qwen3_moe', num_hidden_layers=48, num_experts=128,
                      num_experts_per_tok=8, hidden_size=2048, moe_intermediate_size=768,
-                     norm_topk_prob=True, decoder_sparse_step=1, mlp_only_layers=[],
-                     num_attention_heads=32, num_key_value_heads=4, head_dim=128,
-                     vocab_size=151936)
+                     intermediate_size=6144, norm_topk_prob=True, decoder_sparse_step=1,
+                     mlp_only_layers=[], num_attention_heads=32, num_key_value_heads=4, head_dim=128,
+                     vocab_size=151936, max_position_embeddings=262144, rms_norm_eps=1e-6,
+                     rope_theta=10000000.0, hidden_act='silu', tie_word_embeddings=False)
 DEEPSEEK_V2_LITE = dict(model_type='deepseek_v2', num_hidden_layers=27, n_routed_experts=64,
                         num_experts_per_tok=6, hidden_size=2048, moe_intermediate_size=1408,
-                        first_k_dense_replace=1, moe_layer_freq=1, n_shared_experts=2,
-                        routed_scaling_factor=1.0, topk_method='greedy', norm_topk_prob=False,
-                        kv_lora_rank=512, num_attention_heads=16, vocab_size=102400)
+                        intermediate_size=10944, first_k_dense_replace=1, moe_layer_freq=1,
+                        n_shared_experts=2, routed_scaling_factor=1.0, topk_method='greedy',
+                        norm_topk_prob=False, n_group=1, topk_group=1, kv_lora_rank=512,
+                        q_lora_rank=None, qk_rope_head_dim=64, qk_nope_head_dim=128, v_head_dim=128,
+                        num_attention_heads=16, num_key_value_heads=16, vocab_size=102400,
+                        max_position_embeddings=163840, rms_norm_eps=1e-6, rope_theta=10000.0,
+                        hidden_act='silu', tie_word_embeddings=False)

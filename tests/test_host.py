@@ -61,3 +61,50 @@ def test_zipf_bias_is_log_of_normalised_zipf():
     ranks = torch.argsort(torch.argsort(-p)) + 1  # 1 = most popular
     want = ranks.double() ** -1.1
     assert torch.allclose(p, want / want.sum(), rtol=1e-5)
+
+
+def _profile(world):
+    import itertools
+    doms = []
+    for n in range(1, world + 1):
+        for s in itertools.combinations(range(world), n):
+            # pairs (0,1), (2,3) share a switch uplink of 50 GiB/s; 40 GiB/s per GPU alone
+            per = {g: 40.0 for g in s}
+            for pair in ((0, 1), (2, 3)):
+                if all(g in s for g in pair):
+                    for g in pair:
+                        per[g] = 25.0
+            doms.append(dict(gpus=list(s), mask=sum(1 << g for g in s), gib_per_s=sum(per.values()),
+                             per_gpu_gib_per_s=[per[g] for g in s]))
+    return dict(world=world, physical_gpus=list(range(world)), expert_bytes=9437184, copies=64, repeats=5,
+                domains=doms)
+
+
+def test_quota_lut_builder_and_topology_file(tmp_path):
+    """build_quota_lut over a synthetic 4-GPU profile (two GPU pairs sharing an
+    uplink), the LUT rows from the oracle's build_lut, read back through
+    Topology with the reference's checks."""
+    import json
+    import numpy as np
+    from ferry_b200.build_quota_lut import build, select_domains
+    from ferry_b200.model import QWEN3_30B_A3B, spec_from_config
+    from ferry_b200.quota import Topology
+    from oracle import planner as op
+    spec = spec_from_config(QWEN3_30B_A3B)
+    prof = _profile(4)
+    assert len(select_domains(prof)) == 15
+    doms = select_domains(prof, '0,1:2,3')
+    assert [d['mask'] for d in doms] == [1, 2, 4, 8, 3, 12]
+    topo = build(prof, spec, '0,1:2,3', lut_fn=lambda *a: op.build_lut(*a))
+    path = tmp_path / 'topo.json'
+    path.write_text(json.dumps(topo))
+    t = Topology(path, 4, spec.experts)
+    assert list(t.masks) == [1, 2, 4, 8, 3, 12]
+    np.testing.assert_allclose(t.seconds, [1 / 40.0] * 4 + [1 / 50.0] * 2)
+    assert t.lut.shape == (129, 4) and all(int(t.lut[m].sum()) == m for m in range(129))
+    # the pairs are symmetric, so quotas split evenly between them
+    assert abs(int(t.lut[64][:2].sum()) - int(t.lut[64][2:].sum())) <= 1
+    with pytest.raises(ValueError):
+        Topology(path, 8, spec.experts)
+    with pytest.raises(ValueError):
+        select_domains(dict(prof, domains=prof['domains'][:4]), '0,1:2,3')
