@@ -21,7 +21,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from ._lib import addr, call, ptr, stream_ptr
+from ._lib import call, ptr, stream_ptr
 from .expert_ops import H2DEngine
 from .policy import Controller
 from .symm import SymmetricBuffer

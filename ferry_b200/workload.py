@@ -16,7 +16,6 @@ the same).
 """
 import math
 
-import numpy as np
 import torch
 
 

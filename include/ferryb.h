@@ -399,6 +399,8 @@ typedef struct ferryb_layer_stats {
   double dispatch_permute_us; /* timing mode: dispatch (+ peer signal) and permute, from
                                  after the host wait to the permute's end (waits for the
                                  peers' packets included) */
+  double combine_store_us;    /* timing mode: the combine kernel alone (this rank's partials
+                                 reduced and stored to their source ranks) */
 } ferryb_layer_stats;
 
 typedef struct ferryb_layer ferryb_layer;

@@ -2,7 +2,7 @@
 replicated device planner) on 2 GPUs: one process per GPU runs
 OffloadRuntime.execute; the oracle emulates the same ranks in one process.
 Cache decisions bit-exact on every rank, outputs within the BF16 tolerance.
-Needs 2 GPUs (gpurun --gpus 2); skipped otherwise."""
+Needs 2 GPUs; skipped otherwise."""
 import os
 import tempfile
 
