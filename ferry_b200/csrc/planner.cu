@@ -100,6 +100,7 @@ struct PlanSmem {
   int64_t loads[kMaxWorld];
   int n_assigned[kMaxWorld];
   int seg_start[kMaxWorld + 1];
+  int blk_start[kMaxWorld + 1];  // first 64-record block of each rank (fast victim path)
   float gate[kMaxExperts];
   int owner_layer[kMaxExperts];
   int status;
@@ -415,6 +416,58 @@ __device__ void sort_records(uint64_t* k0, uint64_t* k1, uint32_t* sl, int n) {
   }
 }
 
+// Per rank, the 64 smallest records in ascending order, in the rank's first
+// block.  Rank r owns blocks [blk_start[r], blk_start[r + 1]) of 64 records
+// (padding records are ~0 and sort last).  Every block is sorted in registers
+// by one warp; then, level by level, one warp merges block pairs (left, left
+// + stride) of the same rank into the left block, keeping the lower half:
+// c[i] = min(A[i], B[63 - i]) is the lower 64 of A and B as a bitonic
+// sequence, which six shuffle stages sort.
+__device__ void select_lowest64(uint64_t* k0, uint64_t* k1, uint32_t* sl, const int* blk_start,
+                                int R) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n_warps = blockDim.x >> 5;
+  const int n_blocks = blk_start[R];
+  for (int blk = warp; blk < n_blocks; blk += n_warps) {
+    const int ia = blk * 64 + lane, ib = ia + 32;
+    Rec a{k0[ia], k1[ia], sl[ia]}, b{k0[ib], k1[ib], sl[ib]};
+    for (int size = 2; size <= 64; size <<= 1) warp_stages(a, b, lane, size, size >> 1, lane);
+    k0[ia] = a.k0; k1[ia] = a.k1; sl[ia] = a.sl;
+    k0[ib] = b.k0; k1[ib] = b.k1; sl[ib] = b.sl;
+  }
+  __syncthreads();
+  int max_nb = 0;
+  for (int r = 0; r < R; ++r) max_nb = max(max_nb, blk_start[r + 1] - blk_start[r]);
+  for (int stride = 1; stride < max_nb; stride <<= 1) {
+    // merges of this level, rank-major: rank r has ceil((nb_r - stride) / (2 stride))
+    int total = 0;
+    for (int r = 0; r < R; ++r) {
+      const int nb = blk_start[r + 1] - blk_start[r];
+      total += nb > stride ? (nb - stride + 2 * stride - 1) / (2 * stride) : 0;
+    }
+    for (int item = warp; item < total; item += n_warps) {
+      int r = 0, q = item;
+      for (; r < R; ++r) {
+        const int nb = blk_start[r + 1] - blk_start[r];
+        const int cnt = nb > stride ? (nb - stride + 2 * stride - 1) / (2 * stride) : 0;
+        if (q < cnt) break;
+        q -= cnt;
+      }
+      const int left = blk_start[r] + 2 * stride * q, right = left + stride;
+      const int ia = left * 64 + lane, ja = right * 64 + lane;
+      const Rec a0{k0[ia], k1[ia], sl[ia]}, a1{k0[ia + 32], k1[ia + 32], sl[ia + 32]};
+      const Rec b0{k0[ja], k1[ja], sl[ja]}, b1{k0[ja + 32], k1[ja + 32], sl[ja + 32]};
+      const Rec rb1 = shfl_rec(b1, 31), rb0 = shfl_rec(b0, 31);  // B[63 - i]
+      Rec c0 = rec_lt(rb1, a0) ? rb1 : a0;
+      Rec c1 = rec_lt(rb0, a1) ? rb0 : a1;
+      warp_stages(c0, c1, lane, 64, 32, lane);
+      k0[ia] = c0.k0; k1[ia] = c0.k1; sl[ia] = c0.sl;
+      k0[ia + 32] = c1.k0; k1[ia + 32] = c1.k1; sl[ia + 32] = c1.sl;
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void __launch_bounds__(kPlanThreads, 1)
     plan_kernel(const PlanConfig c, const PlanState s, const PlanInputs in, const PlanOutputs out) {
   extern __shared__ uint8_t dsm[];
@@ -562,62 +615,77 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     return;
   }
 
-  // -- Step 4: victims (one sort of every slot) and the commit -------------
+  // -- Step 4: victims (one ordering of every slot) and the commit ---------
+  // The j-th miss assigned to rank r takes the j-th smallest slot record of
+  // rank r.  When every rank needs at most 64 victims and the ranks' slots
+  // fit whole 64-record blocks, each rank keeps only its 64 smallest records
+  // (select_lowest64); otherwise all records are sorted (sort_records).
   if (m > 0) {
-    const int n = c.sort_n;  // power of two >= total_slots
-    // struct-of-arrays records in dynamic shared memory
+    const int n = c.sort_n;  // power of two >= total_slots, >= 64
     uint64_t* k0 = reinterpret_cast<uint64_t*>(recs);
     uint64_t* k1 = k0 + n;
     uint32_t* sl = reinterpret_cast<uint32_t*>(k1 + n);
-    for (int i = tid; i < n; i += blockDim.x) {
-      uint64_t a0 = ~0ull, a1 = ~0ull;
-      uint32_t ix = 0xffffffffu;
-      if (i < c.total_slots) {
-        const int r = c.slot_rank[i];
-        const int idx = c.slot_index[i];
-        const int key = s.slots[idx];
-        uint64_t cls, lo, hi;
-        if (key < 0) {
-          cls = 0; lo = 0; hi = (uint64_t)(idx - r * c.maxcap);
-        } else if (key / E == L && sm.active[key % E]) {
-          cls = 2; lo = 0; hi = 0;
-        } else {
-          cls = 1;
-          lo = __float_as_uint(s.scores[key]);
-          hi = ((uint64_t)s.last[key] << 24) | (uint64_t)key;
-        }
-        a0 = ((uint64_t)r << 56) | (cls << 48) | lo;
-        a1 = hi;
-        ix = (uint32_t)idx;
-      }
-      k0[i] = a0; k1[i] = a1; sl[i] = ix;
-    }
-    __syncthreads();
-    PLAN_TS(4);
-    sort_records(k0, k1, sl, n);
-    PLAN_TS(5);
-    // the j-th miss assigned to rank r takes the j-th record of r's segment
     if (tid == 0) {
-      int pos = 0;
-      for (int r = 0; r < R; ++r) { sm.seg_start[r] = pos; pos += c.capacities[r]; }
+      int pos = 0, blk = 0;
+      for (int r = 0; r < R; ++r) {
+        sm.seg_start[r] = pos;
+        sm.blk_start[r] = blk;
+        pos += c.capacities[r];
+        blk += (c.capacities[r] + 63) / 64;
+      }
+      sm.blk_start[R] = blk;
     }
+    if (tid < R) sm.n_assigned[tid] = 0;
     __syncthreads();
     for (int i = tid; i < m; i += blockDim.x) {
       const int r = sm.assignment[i];
       int before = 0;  // earlier misses assigned to the same rank
       for (int j = 0; j < i; ++j) before += sm.assignment[j] == r;
-      sm.victim_pos[i] = r >= 0 && r < R ? sm.seg_start[r] + before : -1;
+      sm.victim_pos[i] = before;  // rank-relative for now
+      if (r >= 0 && r < R) atomicMax(&sm.n_assigned[r], before + 1);
     }
     __syncthreads();
+    bool fast = sm.blk_start[R] * 64 <= n;
+    for (int r = 0; r < R; ++r) fast = fast && sm.n_assigned[r] <= 64;
+    for (int i = tid; i < n; i += blockDim.x) { k0[i] = ~0ull; k1[i] = ~0ull; sl[i] = 0xffffffffu; }
+    __syncthreads();
+    for (int i = tid; i < c.total_slots; i += blockDim.x) {
+      const int r = c.slot_rank[i];
+      const int idx = c.slot_index[i];
+      const int key = s.slots[idx];
+      uint64_t cls, lo, hi;
+      if (key < 0) {
+        cls = 0; lo = 0; hi = (uint64_t)(idx - r * c.maxcap);
+      } else if (key / E == L && sm.active[key % E]) {
+        cls = 2; lo = 0; hi = 0;
+      } else {
+        cls = 1;
+        lo = __float_as_uint(s.scores[key]);
+        hi = ((uint64_t)s.last[key] << 24) | (uint64_t)key;
+      }
+      // fast: rank r's records fill its own 64-record blocks (padded)
+      const int pos = fast ? sm.blk_start[r] * 64 + (i - sm.seg_start[r]) : i;
+      k0[pos] = ((uint64_t)r << 56) | (cls << 48) | lo;
+      k1[pos] = hi;
+      sl[pos] = (uint32_t)idx;
+    }
+    __syncthreads();
+    PLAN_TS(4);
+    if (fast) select_lowest64(k0, k1, sl, sm.blk_start, R);
+    else sort_records(k0, k1, sl, n);
+    PLAN_TS(5);
     for (int i = tid; i < m; i += blockDim.x) {
       const int r = sm.assignment[i];
-      const int vp = sm.victim_pos[i];
+      const int j = sm.victim_pos[i];
+      int vp = -1;
+      if (r >= 0 && r < R && j < c.capacities[r])
+        vp = fast ? (sm.blk_start[r + 1] > sm.blk_start[r] ? sm.blk_start[r] * 64 + j : -1)
+                  : sm.seg_start[r] + j;
       if (vp < 0 || vp >= n) { set_err(out.err, DEV_NO_SLOT); continue; }
       const uint64_t rk0 = k0[vp];
       const uint32_t rslot = sl[vp];
       const uint64_t cls = (rk0 >> 48) & 0xff;
-      const bool ok = rslot != 0xffffffffu && (int)(rk0 >> 56) == r && cls < 2 &&
-                      vp < sm.seg_start[r] + c.capacities[r];
+      const bool ok = rslot != 0xffffffffu && (int)(rk0 >> 56) == r && cls < 2;
       if (!ok) { set_err(out.err, DEV_NO_SLOT); continue; }
       const int idx = (int)rslot;
       const int key = base + sm.misses[i];
