@@ -69,8 +69,10 @@ def parse():
     p.add_argument('--batch', type=int, default=64, help='--full-model: sequences per GPU')
     p.add_argument('--prompt-len', type=int, default=1024, help='--full-model: input tokens')
     p.add_argument('--new-tokens', type=int, default=64, help='--full-model: greedy output tokens')
-    p.add_argument('--topology', help='profiled topology JSON (ferry_b200.build_quota_lut) for N > 1; '
-                                      'default: uniform domains')
+    p.add_argument('--topology', default='auto',
+                   help='quota LUT for N > 1: "auto" (default) profiles the host links of these GPUs '
+                        'at start-up (every subset of ranks copying at once) and builds the LUT; '
+                        '"uniform"; or a topology JSON from ferry_b200.build_quota_lut')
     p.add_argument('--per-rank-pool', action='store_true',
                    help='one pinned expert pool per rank (the reference\'s layout) instead of one '
                         'shared pool per node')
@@ -206,6 +208,30 @@ def auto_pool_layers(spec, world, requested):
     return max(1, min(spec.layers, fit))
 
 
+def make_topology(a, spec, rank, world, pool, dev):
+    """(Topology, note): the quota LUT of this run (see --topology)."""
+    from ferry_b200.quota import Topology
+    if world == 1 or a.topology == 'uniform':
+        return Topology.uniform(world, spec.experts), 'uniform'
+    if a.topology != 'auto':
+        return Topology(a.topology, world, spec.experts), a.topology
+    from ferry_b200.build_quota_lut import build
+    from ferry_b200.profile_h2d import profile_ranks
+    target = torch.empty(spec.expert_elements, dtype=torch.bfloat16, device=dev)
+    t0 = time.time()
+    domains = profile_ranks(rank, world, target, pool[0], copies=16, repeats=2)
+    profile = dict(world=world, physical_gpus=list(range(world)), expert_bytes=spec.expert_bytes,
+                   domains=domains)
+    box = [build(profile, spec)['quota_lut'] if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    masks = sorted((d['mask'] for d in domains), key=lambda m: (bin(m).count('1'), m))
+    by_mask = {d['mask']: d for d in domains}
+    topo = Topology.from_arrays(masks, [1.0 / by_mask[m]['gib_per_s'] for m in masks], box[0])
+    singles = [round(by_mask[1 << r]['gib_per_s'], 1) for r in range(world)]
+    return topo, (f'auto: profiled {len(domains)} rank subsets in {time.time() - t0:.1f} s; '
+                  f'single-GPU GiB/s {singles}, all-GPU {round(by_mask[(1 << world) - 1]["gib_per_s"], 1)}')
+
+
 def qwen3_spec(layers):
     from ferry_b200.model import QWEN3_30B_A3B, spec_from_config
     c = dict(QWEN3_30B_A3B)
@@ -227,7 +253,7 @@ def run_ours(a, rank, world, local):
     t0 = time.time()
     wl = SyntheticMoE(spec, seed=0, device=dev, pool_layers=pool_layers, shared=shared)
     setup_s = time.time() - t0
-    topo = Topology(a.topology, world, spec.experts) if a.topology else Topology.uniform(world, spec.experts)
+    topo, topo_note = make_topology(a, spec, rank, world, wl.pool, dev)
     rt = OffloadRuntime(spec, wl.pool, caps, a.policy, topo, n_copy_streams=a.copy_streams,
                         timing=True, sync_fetch=a.sync_fetch)
     # this rank's link alone (ranks take turns), then with every rank copying at once
@@ -327,13 +353,17 @@ def run_ours(a, rank, world, local):
     t_flops = flops / (bf16_tflops * 1e12)
     t_roof = max(t_host, t_nvl, t_flops)
     t_meas = ms_local / 1e3
+    # the job's layer is as slow as its slowest rank: both terms max over ranks
+    t_roof_job = max_over_ranks(t_roof, world)
+    t_meas_job = max_over_ranks(t_meas, world)
     layer_roofline = {'bound': ['host_link', 'nvlink', 'tensor'][int(np.argmax([t_host, t_nvl, t_flops]))],
-                      'frac': round(t_roof / t_meas, 4) if t_meas > 0 else None,
+                      'frac': round(t_roof_job / t_meas_job, 4) if t_meas_job > 0 else None,
+                      'frac_rank0': round(t_roof / t_meas, 4) if t_meas > 0 else None,
                       'host_link_gbs_measured': round(b_host, 2),
                       'host_link_gbs_alone': round(b_alone, 2),
                       'host_link_note': 'measured with every rank copying at once (shared PCIe '
                                         'switches / host memory); alone = this rank only',
-                      'topology': a.topology or 'uniform',
+                      'topology': topo_note,
                       'fetch_gbs_achieved': round(fetch_bytes / t_meas / 1e9, 2),
                       'fetches_per_layer': st.fetches / max(1, st.layers),
                       'nvlink_bytes_per_layer': nvl_bytes / max(1, st.layers),

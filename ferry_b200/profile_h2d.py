@@ -88,6 +88,44 @@ def profile(spec, gpus, copies=64, repeats=5, spin_cycles=100_000_000, max_subse
     return domains
 
 
+def profile_ranks(rank, world, target, source, copies=16, repeats=2, group=None):
+    """The same profile taken by the ranks of a torch.distributed job, one GPU
+    each: for every subset of ranks, after a barrier, the ranks of the subset
+    copy `source` (pinned host row) into `target` (device row) `copies` times
+    at once; returns the profile's domain list (masks over ranks)."""
+    import torch.distributed as dist
+    nbytes = source.numel() * source.element_size()
+    stream = torch.cuda.Stream()
+    ranks = list(range(world))
+    subsets = [s for n in range(1, world + 1) for s in itertools.combinations(ranks, n)]
+    with torch.cuda.stream(stream):  # warm the copy engine
+        for _ in range(4):
+            target.copy_(source, non_blocking=True)
+    stream.synchronize()
+    mine = torch.zeros((repeats, len(subsets)), dtype=torch.float64, device=target.device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for rep in range(repeats):
+        for i, s in enumerate(subsets):
+            dist.barrier(group=group)
+            if rank in s:
+                with torch.cuda.stream(stream):
+                    e0.record(stream)
+                    for _ in range(copies):
+                        target.copy_(source, non_blocking=True)
+                    e1.record(stream)
+                e1.synchronize()
+                mine[rep, i] = copies * nbytes / (e0.elapsed_time(e1) / 1e3) / 2**30
+    allv = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(allv, mine, group=group)
+    per = torch.stack(allv).median(dim=1).values.cpu().numpy()  # [world, subsets]
+    domains = []
+    for i, s in enumerate(subsets):
+        vals = [float(per[g, i]) for g in s]
+        domains.append(dict(gpus=list(s), mask=sum(1 << g for g in s), gib_per_s=sum(vals),
+                            per_gpu_gib_per_s=vals))
+    return domains
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.split('\n\n')[0])
     p.add_argument('--model', choices=sorted(MODELS), default='qwen3',
