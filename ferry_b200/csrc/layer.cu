@@ -401,7 +401,9 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   in.layer = layer;
   in.gflags = c.world > 1 ? reinterpret_cast<const uint64_t*>(half + L->sl.gflag) : nullptr;
   in.seq = seq;
-  in.hist = reinterpret_cast<const int*>(half + L->sl.gather_hist);
+  // one rank: the router's own histogram, which the planner also clears
+  in.hist = c.world > 1 ? reinterpret_cast<const int*>(half + L->sl.gather_hist) : L->hist_local;
+  in.hist_clear = c.world > 1 ? nullptr : L->hist_local;
   PlanOutputs po{L->fetches, L->n_fetches, L->dest, L->counts, L->errs + 0};
   if ((s = plan_launch(L->pc, L->ps, in, po, stream))) return s;
   launches += 1;

@@ -508,6 +508,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   // -- Step 1: demand d[e, r] ----------------------------------------------
   if (in.hist) {
     for (int i = tid; i < E * R; i += blockDim.x) demand[(i % E) * R + i / E] = in.hist[i];
+    if (in.hist_clear) {
+      __syncthreads();
+      for (int i = tid; i < E * R; i += blockDim.x) in.hist_clear[i] = 0;
+    }
   } else for (int i = tid; i < n_tok * K; i += blockDim.x) {
     const int t = i / K;
     const int e = in.ids[i];

@@ -48,6 +48,8 @@ struct PlanInputs {
   const uint64_t* gflags;  // [world] gather flags to wait for (>= seq)
   uint64_t seq;
   const int* hist;         // [world, experts] per-rank demand histograms
+  int* hist_clear;         // non-null (one rank): the router's own histogram, read from
+                           // `hist` and zeroed here for the next layer
 };
 
 struct PlanOutputs {

@@ -100,50 +100,40 @@ __global__ void __launch_bounds__(kRouterThreads)
   }
   __syncthreads();
 
-  // ---- softmax (float32) ----
-  float m = -CUDART_INF_F;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) m = fmaxf(m, logit[e]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0) red[warp] = m;
-  __syncthreads();
-  m = red[0];
-  for (int i = 1; i < nw; ++i) m = fmaxf(m, red[i]);
-  __syncthreads();
-  float s = 0.0f;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    const float v = expf(logit[e] - m);
-    logit[e] = v;
-    s += v;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) red[warp] = s;
-  __syncthreads();
-  s = 0.0f;
-  for (int i = 0; i < nw; ++i) s += red[i];
-  for (int e = threadIdx.x; e < E; e += blockDim.x) logit[e] = logit[e] / s;  // probabilities
-  __syncthreads();
-  if (a.probs_out)
-    for (int e = threadIdx.x; e < E; e += blockDim.x) a.probs_out[(size_t)t * E + e] = logit[e];
-  if (a.prob_tail > 0 && t >= a.tokens_per_rank - a.prob_tail) {
-    const int i = t - (a.tokens_per_rank - a.prob_tail);
-    for (int q = threadIdx.x; q < a.world * E; q += blockDim.x) {
-      const int p = q / E, e = q % E;
-      uint8_t* base = reinterpret_cast<uint8_t*>(a.peer_base[p]) + a.parity * a.buf_stride;
-      reinterpret_cast<float*>(base + a.off_prob)[((size_t)a.rank * a.prob_tail + i) * E + e] = logit[e];
-    }
-  }
-
-  // ---- top-k on warp 0: largest probability, ties to the lower id ----
+  // ---- softmax (float32), top-k and weights: warp 0 alone --------------
+  // lane l holds logits l, l + 32, ... (E <= kMaxRouterExperts)
   if (warp == 0) {
     constexpr int kPer = kMaxRouterExperts / 32;
     float v[kPer];
+    float m = -CUDART_INF_F;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const int e = lane + 32 * i;
-      v[i] = e < E ? logit[e] : -1.0f;
+      v[i] = e < E ? logit[e] : -CUDART_INF_F;
+      m = fmaxf(m, v[i]);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < E ? expf(v[i] - m) : 0.0f;
+      s += v[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E) {
+        v[i] = v[i] / s;  // probabilities
+        logit[e] = v[i];
+      } else {
+        v[i] = -1.0f;
+      }
+    }
+    // top-k: largest probability, ties to the lower id
     for (int j = 0; j < K; ++j) {
       float bv = -2.0f;
       int bi = 0x7fffffff;
@@ -177,6 +167,17 @@ __global__ void __launch_bounds__(kRouterThreads)
       }
     }
   }
+  __syncthreads();  // probabilities in logit[], top_id[] complete
+  if (a.probs_out)
+    for (int e = threadIdx.x; e < E; e += blockDim.x) a.probs_out[(size_t)t * E + e] = logit[e];
+  if (a.prob_tail > 0 && t >= a.tokens_per_rank - a.prob_tail) {
+    const int i = t - (a.tokens_per_rank - a.prob_tail);
+    for (int q = threadIdx.x; q < a.world * E; q += blockDim.x) {
+      const int p = q / E, e = q % E;
+      uint8_t* base = reinterpret_cast<uint8_t*>(a.peer_base[p]) + a.parity * a.buf_stride;
+      reinterpret_cast<float*>(base + a.off_prob)[((size_t)a.rank * a.prob_tail + i) * E + e] = logit[e];
+    }
+  }
   __syncthreads();
   }  // mode 0 / 1
 
@@ -186,6 +187,9 @@ __global__ void __launch_bounds__(kRouterThreads)
     uint8_t* base = reinterpret_cast<uint8_t*>(a.peer_base[p]) + a.parity * a.buf_stride;
     base[a.off_ids + ((size_t)a.rank * a.tokens_per_rank + t) * K + j] = (uint8_t)top_id[j];
   }
+  // With one rank the planner, next on the stream, reads the histogram and
+  // the ids this kernel wrote (the kernel boundary orders them): no flags.
+  if (a.world == 1) return;
   // ---- last CTA: histogram + flags ----
   // One system-scope fence per CTA, by thread 0 after a CTA barrier (the
   // barrier orders the CTA's peer stores before it), then the done counter.
