@@ -67,14 +67,28 @@ __device__ int block_scan(int v, int* warp_sum, int* total) {
   return res;
 }
 
-// Sorted ids of token g's routes that go to `peer` (ascending, insertion sort
-// as in ferry/layout.py:27-33).  Returns the count.
-__device__ __forceinline__ int packet_ids(const uint8_t* ids, const int32_t* dest, int g, int K,
-                                          int peer, int* out, int E, int* err) {
+// One token's routes, loaded with all of its loads in flight at once:
+// v[j] = (destination rank + 1) << 8 | expert id.
+struct TokenRoutes {
+  int v[16];
+};
+
+__device__ __forceinline__ void load_routes(const uint8_t* ids, const int32_t* dest, int g, int K,
+                                            TokenRoutes& r) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    if (j < K) r.v[j] = ((dest[(size_t)g * K + j] + 1) << 8) | ids[(size_t)g * K + j];
+}
+
+// Sorted ids of the token's routes that go to `peer` (ascending, insertion
+// sort as in ferry/layout.py:27-33).  Returns the count.
+__device__ __forceinline__ int packet_ids(const TokenRoutes& r, int K, int peer, int* out, int E,
+                                          int* err) {
   int size = 0;
-  for (int j = 0; j < K; ++j) {
-    if (dest[g * K + j] == peer) {
-      const int e = ids[g * K + j];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (j < K && (r.v[j] >> 8) - 1 == peer) {
+      const int e = r.v[j] & 0xff;
       if (e >= E) {  // never index per-expert tables with an invalid id
         atomicCAS(err, 0, DEV_BAD_INPUT);
         continue;
@@ -149,7 +163,11 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
       const int t = t0 + tid;
       const int g = rank * T + t;
       int size = 0;
-      if (t < T) size = packet_ids(a.ids, a.dest, g, K, peer, ids_buf, E, a.err);
+      if (t < T) {
+        TokenRoutes tr;
+        load_routes(a.ids, a.dest, g, K, tr);
+        size = packet_ids(tr, K, peer, ids_buf, E, a.err);
+      }
       const int has = size > 0;
       const int pos = sent + block_scan(has, sm.warp_sum, &total_sh);
       if (has) {
@@ -187,7 +205,11 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
   for (int g0 = 0; g0 < n_tok; g0 += kChunk) {
     const int g = g0 + tid;
     int size = 0;
-    if (g < n_tok) size = packet_ids(a.ids, a.dest, g, K, rank, ids_buf, E, a.err);
+    if (g < n_tok) {
+      TokenRoutes tr;
+      load_routes(a.ids, a.dest, g, K, tr);
+      size = packet_ids(tr, K, rank, ids_buf, E, a.err);
+    }
     const int has = size > 0;
     const int row = received + block_scan(has, sm.warp_sum, &total_sh);
     if (has) {
@@ -219,7 +241,11 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
     __syncthreads();
     const int g = g0 + tid;
     int size = 0;
-    if (g < n_tok) size = packet_ids(a.ids, a.dest, g, K, rank, ids_buf, E, a.err);
+    if (g < n_tok) {
+      TokenRoutes tr;
+      load_routes(a.ids, a.dest, g, K, tr);
+      size = packet_ids(tr, K, rank, ids_buf, E, a.err);
+    }
     for (int j = 0; j < size; ++j) atomicOr(&sm.mask[ids_buf[j]][tid >> 5], 1u << (tid & 31));
     const int has = size > 0;
     const int row = row_base + block_scan(has, sm.warp_sum, &total_sh);
