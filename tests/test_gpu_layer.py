@@ -157,3 +157,46 @@ def test_forward_deepseek_shared_experts():
     want, _, _ = orc.execute(0, [x], [sel], [w])
     assert_bf16_close(got.cpu(), want[0], 'execute without shared')
     rt.close()
+
+
+@pytest.mark.parametrize('policy,score', [('random', 'frequency'), ('ferry', 'probability')])
+def test_execute_policies_and_scores(policy, score):
+    """FERRY-Random (MT19937 draws, one rank) and the router-probability
+    eviction score (probs_tail rows into the device history) through the full
+    executor: decisions bit-exact, outputs within tolerance."""
+    layers, E, K, H, I, T, cap = 3, 32, 4, 256, 128, 12, 20
+    spec = _spec(layers, E, K, H, I)
+    rt, orc, gates, biases, g = _setup(spec, [cap], seed=8, policy=policy, score=score)
+    for step in range(3 * layers):
+        layer = step % layers
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        sel, w, probs = ref_ops.route_qwen3(x, gates[layer], K, True, biases[layer])
+        pt = probs if score == 'probability' else None
+        want, _, _ = orc.execute(layer, [x], [sel], [w], [pt] if pt is not None else None)
+        got = rt.execute(layer, x.to(DEV), sel.to(DEV), w.to(DEV), pt.to(DEV) if pt is not None else None)
+        torch.cuda.synchronize()
+        assert_bf16_close(got.cpu(), want[0], f'{policy}/{score} step {step}')
+        np.testing.assert_array_equal(rt.controller.slots, orc.ctl.slots, err_msg=f'step {step}')
+        np.testing.assert_array_equal(rt.controller.owner, orc.ctl.owner)
+    np.testing.assert_array_equal(rt.fetches_per_rank, orc.fetches_per_rank)
+    rt.close()
+
+
+@pytest.mark.parametrize('E,K,T', [(256, 16, 1), (256, 8, 3), (16, 1, 5)])
+def test_execute_edge_shapes(E, K, T):
+    """Edge shapes: one token, the maximum of 256 experts (ids travel as
+    uint8) and top-16, top-1."""
+    layers, H, I = 2, 256, 128
+    spec = _spec(layers, E, K, H, I)
+    cap = min(layers * E, max(3 * K * T, E // 2))
+    rt, orc, gates, biases, g = _setup(spec, [cap], seed=E + K + T)
+    for step in range(4):
+        layer = step % layers
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        sel, w, _ = ref_ops.route_qwen3(x, gates[layer], K, True, biases[layer])
+        want, _, _ = orc.execute(layer, [x], [sel], [w])
+        got = rt.execute(layer, x.to(DEV), sel.to(DEV), w.to(DEV), None)
+        torch.cuda.synchronize()
+        assert_bf16_close(got.cpu(), want[0], f'E{E} K{K} T{T} step {step}')
+        np.testing.assert_array_equal(rt.controller.slots, orc.ctl.slots)
+    rt.close()
