@@ -35,6 +35,7 @@ struct LaySmem {
   int lslot[kMaxExpertsL];                   // slot of each expert of the layer on this rank
   int fetch_key[kMaxExpertsL], fetch_slot[kMaxExpertsL];
   int recv_cnt[kMaxWorldL];
+  int lower_cnt[kMaxWorldL];                 // tokens of lower ranks that send to each peer
   int n_groups, n_hit, n_fetch_mine;
 };
 
@@ -155,6 +156,34 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
   }
   __syncthreads();
 
+  // ---- receive rows at every peer, part 1 ---------------------------------
+  // The receive row of local token t at peer p is #{g' < g : g' sends to p}
+  // (g = rank * T + t): the tokens of lower ranks that send to p (counted
+  // here, order-free) plus this rank's earlier tokens that send to p (their
+  // packet positions, from the send side below).
+  if (a.peer_row) {
+    if (tid < R) sm.lower_cnt[tid] = 0;
+    __syncthreads();
+    for (int g0 = 0; g0 < rank * T; g0 += kChunk) {
+      const int g = g0 + tid;
+      unsigned peers = 0;  // bit p: token g sends to p
+      if (g < rank * T) {
+        TokenRoutes tr;
+        load_routes(a.ids, a.dest, g, K, tr);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int d = (tr.v[j] >> 8) - 1;
+          if (j < K && d >= 0 && d < R) peers |= 1u << d;
+        }
+      }
+      for (int p = 0; p < R; ++p) {  // warp-aggregated: one shared atomic per warp and peer
+        const unsigned bal = __ballot_sync(0xffffffffu, (peers >> p) & 1u);
+        if ((tid & 31) == 0 && bal) atomicAdd(&sm.lower_cnt[p], __popc(bal));
+      }
+    }
+    __syncthreads();
+  }
+
   // ---- send side: packets by (peer, token) --------------------------------
   int sent = 0;
   for (int peer = 0; peer < R; ++peer) {
@@ -169,11 +198,14 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
         size = packet_ids(tr, K, peer, ids_buf, E, a.err);
       }
       const int has = size > 0;
-      const int pos = sent + block_scan(has, sm.warp_sum, &total_sh);
+      const int before = block_scan(has, sm.warp_sum, &total_sh);  // this rank's earlier packets to peer
+      const int pos = sent + before;
       if (has) {
         a.send_idx[pos] = t;
         for (int j = 0; j < K; ++j) a.send_ids[(size_t)pos * K + j] = j < size ? ids_buf[j] : -1;
       }
+      if (a.peer_row && t < T)
+        a.peer_row[(size_t)t * R + peer] = has ? sm.lower_cnt[peer] + peer_sent + before : -1;
       sent += total_sh;
       peer_sent += total_sh;
       __syncthreads();
@@ -181,24 +213,6 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
     if (tid == 0) a.send_counts[peer] = peer_sent;
   }
   if (tid == 0) *a.n_send = sent;
-
-  // ---- receive rows of every peer (peer_row) -----------------------------
-  // Receive row of global token g at peer p = #{g' < g : g' sends to p}.
-  if (a.peer_row) {
-    for (int p = 0; p < R; ++p) {
-      int carry = 0;
-      for (int g0 = 0; g0 < n_tok; g0 += kChunk) {
-        const int g = g0 + tid;
-        int has = 0;
-        if (g < n_tok)
-          for (int j = 0; j < K; ++j) has |= a.dest[g * K + j] == p;
-        const int row = carry + block_scan(has, sm.warp_sum, &total_sh);
-        if (g < n_tok && g / T == rank) a.peer_row[(g % T) * R + p] = has ? row : -1;
-        carry += total_sh;
-        __syncthreads();
-      }
-    }
-  }
 
   // ---- receive side pass 1: receive rows, per-expert counts --------------
   int received = 0;

@@ -143,3 +143,40 @@ def test_layout_multi_chunk_random(world, tokens, experts, topk):
         for g, w, name in zip(got, want, ['send_idx', 'send_ids', 'send_counts', 'recv_counts',
                                           'starts', 'rows', 'cols']):
             np.testing.assert_array_equal(g, w, err_msg=f'{name} rank {r}')
+
+
+@pytest.mark.parametrize('world,tokens,experts,topk', [(4, 700, 128, 8), (8, 300, 64, 6), (2, 1500, 32, 4)])
+def test_fused_layout_outputs(world, tokens, experts, topk):
+    """The fused executor's extra layout outputs: peer_row (receive row of each
+    local token at every peer), recv_token and csr_pos, against numpy, for
+    every rank, past one 1,024-token chunk."""
+    from ferry_b200 import _lib
+    from ferry_b200.layout import LayoutBuffers
+    rng = np.random.default_rng(world + tokens)
+    n = world * tokens
+    sel = np.stack([rng.choice(experts, topk, replace=False) for _ in range(n)]).astype(np.int64)
+    dest = rng.integers(0, world, (n, topk))
+    ids_t = torch.as_tensor(sel.astype(np.uint8), device='cuda')
+    dest_t = torch.as_tensor(dest.astype(np.int32), device='cuda')
+    slot_of = torch.arange(experts, dtype=torch.int32, device='cuda')
+    sends = np.stack([(dest == p).any(1) for p in range(world)])  # [world, n]
+    for r in range(world):
+        buf = LayoutBuffers(world, tokens, topk, experts, r, torch.device('cuda'), fused=True)
+        buf.run(ids_t, dest_t, layer_slot=slot_of)
+        torch.cuda.synchronize()
+        _lib.check_device_error(buf.err, 'layout')
+        want_pr = np.full((tokens, world), -1)
+        for p in range(world):
+            before = np.cumsum(sends[p]) - sends[p]
+            g = r * tokens + np.arange(tokens)
+            want_pr[:, p] = np.where(sends[p][g], before[g], -1)
+        np.testing.assert_array_equal(buf.peer_row.cpu().numpy(), want_pr, err_msg=f'peer_row rank {r}')
+        recv = np.flatnonzero(sends[r])
+        n_recv = int(buf.n_recv.item())
+        assert n_recv == recv.size
+        np.testing.assert_array_equal(buf.recv_token[:n_recv].cpu().numpy(), recv)
+        total = int(buf.starts[-1].item())
+        rows, cols = buf.rows[:total].cpu().numpy(), buf.cols[:total].cpu().numpy()
+        want_cp = np.full((n_recv, topk), -1)
+        want_cp[rows, cols] = np.arange(total)
+        np.testing.assert_array_equal(buf.csr_pos[:n_recv].cpu().numpy(), want_cp, err_msg=f'csr_pos rank {r}')
