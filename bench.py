@@ -208,6 +208,10 @@ def auto_pool_layers(spec, world, requested):
     return max(1, min(spec.layers, fit))
 
 
+KERNELS = ['router', 'planner', 'layout', 'dispatch', 'permute', 'gemm_cached', 'gemm_fetched',
+           'combine', 'final_scatter']
+
+
 def make_topology(a, spec, rank, world, pool, dev):
     """(Topology, note): the quota LUT of this run (see --topology)."""
     from ferry_b200.quota import Topology
@@ -392,6 +396,10 @@ def run_ours(a, rank, world, local):
              'combine'])},
         'copy_lane_us_per_layer': {name: round(st.copy_us[i] / layers_timed, 1) for i, name in enumerate(
             ['layout_end_to_first_copy', 'copies', 'last_copy_to_combine_end'])},
+        # per-MoE-layer split on the device clock: each kernel's span (earliest
+        # CTA start to latest CTA end), averaged over the timed layers
+        'kernel_us_per_layer_device_clock': {name: round(st.kernel_us[i] / layers_timed, 1)
+                                             for i, name in enumerate(KERNELS) if st.kernel_launches[i]},
         'setup_s': round(setup_s, 1), 'e2e': e2e, 'clocks': clocks,
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

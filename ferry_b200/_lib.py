@@ -62,7 +62,8 @@ class LayerStats(ctypes.Structure):
                                      'timed_layers')] + [
         ('host_wait_us', _dbl), ('phase_us', _dbl * 5), ('host_us', _dbl * 6),
         ('copy_us', _dbl * 3), ('hit_gemm_kernel_us', _dbl), ('hit_gemm_kernel_launches', _i64),
-        ('dispatch_permute_us', _dbl), ('combine_store_us', _dbl)]
+        ('dispatch_permute_us', _dbl), ('combine_store_us', _dbl),
+        ('kernel_us', _dbl * 9), ('kernel_launches', _i64 * 9)]
 
 
 # name -> (restype, argtypes); every symbol declared in include/ferryb.h.

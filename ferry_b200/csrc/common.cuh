@@ -273,6 +273,15 @@ __device__ __forceinline__ bool wait_flags_bounded(const uint64_t* flags, int n,
   return true;
 }
 
+// Device-clock span of a launch (timing mode): ts[0] is lowered to the
+// earliest CTA start, ts[1] raised to the latest CTA end; null = off.
+__device__ __forceinline__ void span_begin(unsigned long long* ts) {
+  if (ts && threadIdx.x == 0) atomicMin(ts, (unsigned long long)globaltimer_ns());
+}
+__device__ __forceinline__ void span_end(unsigned long long* ts) {
+  if (ts && threadIdx.x == 0) atomicMax(ts + 1, (unsigned long long)globaltimer_ns());
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -75,11 +75,13 @@ struct ferryb_layer {
   // ferryb_layer_collect_timing
   std::vector<cudaEvent_t> tev_pool;
   std::vector<char> tev_fetched;  // per timed layer: copy-lane events recorded
-  // device-clock span of each timed layer's cached-expert GEMM: starts[kTs]
-  // (initially ~0), ends[kTs] (initially 0), in the workspace
-  static constexpr int kTs = 512;
-  unsigned long long* gemm_ts = nullptr;
-  std::vector<char> ts_used;
+  // device-clock spans of each timed layer's kernels, [kTs][kSpans][2]
+  // (start initially ~0, end initially 0), in the workspace; kernel order:
+  // router, planner, layout, dispatch, permute, cached GEMM, fetched GEMM,
+  // combine, final scatter (more than one rank)
+  static constexpr int kTs = 512, kSpans = 9;
+  unsigned long long* spans = nullptr;
+  std::vector<char> ts_used;  // per timed layer: has a span slot
   size_t tev_used = 0;
   cudaEvent_t* tev = nullptr;
   GemmMaps maps{};
@@ -180,7 +182,7 @@ static int64_t workspace_bytes(const ferryb_layer_config& c, uint8_t* base, ferr
     auto peer_base = cv.take<uintptr_t>(R);
     auto ready = cv.take<uint32_t>(2 * E);
     auto queue_dep = cv.take<int>(2 + E);
-    auto gemm_ts = cv.take<unsigned long long>(2 * ferryb_layer::kTs);
+    auto spans = cv.take<unsigned long long>(2 * ferryb_layer::kTs * ferryb_layer::kSpans);
     const int64_t Is = c.shared_intermediate;
     auto shared_act = cv.take<__nv_bfloat16>(Is > 0 ? T * Is : 0);
     auto shared_out = cv.take<__nv_bfloat16>(Is > 0 ? T * H : 0);
@@ -198,7 +200,7 @@ static int64_t workspace_bytes(const ferryb_layer_config& c, uint8_t* base, ferr
       L->peer_base_dev = peer_base;
       L->ready = ready;
       L->queue_dep = queue_dep;
-      L->gemm_ts = gemm_ts;
+      L->spans = spans;
       if (Is > 0) {
         L->shared_act = shared_act; L->shared_out = shared_out; L->shared_ones = shared_ones;
         L->shared_group = shared_group;
@@ -267,9 +269,9 @@ extern "C" int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_
   FB_CUDA(cudaMemcpy(L->peer_base_dev, peer_bases, sizeof(uint64_t) * cfg->world,
                      cudaMemcpyHostToDevice));
   {
-    std::vector<unsigned long long> ts(2 * ferryb_layer::kTs);
-    for (size_t i = 0; i < (size_t)ferryb_layer::kTs; ++i) { ts[2 * i] = ~0ull; ts[2 * i + 1] = 0; }
-    FB_CUDA(cudaMemcpy(L->gemm_ts, ts.data(), ts.size() * sizeof(unsigned long long),
+    std::vector<unsigned long long> ts(2 * ferryb_layer::kTs * ferryb_layer::kSpans);
+    for (size_t i = 0; i < ts.size() / 2; ++i) { ts[2 * i] = ~0ull; ts[2 * i + 1] = 0; }
+    FB_CUDA(cudaMemcpy(L->spans, ts.data(), ts.size() * sizeof(unsigned long long),
                        cudaMemcpyHostToDevice));
   }
   L->shared_w.assign((size_t)planner->layers, nullptr);
@@ -358,9 +360,13 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     L->tev = L->tev_pool.data() + L->tev_used;
     L->tev_used += 10;
     L->tev_fetched.push_back(0);
-    L->ts_used.push_back(0);
+    L->ts_used.push_back(L->ts_used.size() < (size_t)ferryb_layer::kTs ? 1 : 0);
     FB_CUDA(cudaEventRecord(L->tev[0], stream));
   }
+  // device-clock span slot k of this layer (timing mode), or null
+  unsigned long long* const span_base =
+      (timing && !L->ts_used.empty() && L->ts_used.back()) ? L->spans + 2 * ferryb_layer::kSpans * (L->ts_used.size() - 1) : nullptr;
+  auto span_of = [&](int k) { return span_base ? span_base + 2 * k : nullptr; };
 
   // 1 router + all-gather
   RouterArgs ra{};
@@ -386,6 +392,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   ra.off_hist = L->sl.gather_hist;
   ra.off_flag = L->sl.gflag;
   ra.off_prob = prob_offset(c);
+  ra.ts = span_of(0);
   int s = router_launch(ra, seq, stream);
   if (s) return s;
   launches += 1;
@@ -404,6 +411,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   // one rank: the router's own histogram, which the planner also clears
   in.hist = c.world > 1 ? reinterpret_cast<const int*>(half + L->sl.gather_hist) : L->hist_local;
   in.hist_clear = c.world > 1 ? nullptr : L->hist_local;
+  in.ts = span_of(1);
   PlanOutputs po{L->fetches, L->n_fetches, L->dest, L->counts, L->errs + 0};
   if ((s = plan_launch(L->pc, L->ps, in, po, stream))) return s;
   launches += 1;
@@ -424,7 +432,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   la.n_send = L->n_send; la.n_recv = L->n_recv; la.recv_token = L->recv_token;
   la.csr_pos = L->csr_pos; la.peer_row = L->peer_row; la.groups = L->groups;
   la.summary = L->summary_dev; la.err = L->errs + 1;
-  if ((s = layout_launch(la, stream))) return s;
+  if ((s = layout_launch(la, stream, span_of(2)))) return s;
   launches += 1;  // layout
   if (timing) FB_CUDA(cudaEventRecord(L->tev[1], stream));
 
@@ -473,6 +481,10 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   FusedArgs fa = fused_args(L, parity, static_cast<const __nv_bfloat16*>(hidden),
                             static_cast<__nv_bfloat16*>(out));
   if (shared) fa.addend = L->shared_out;
+  fa.ts_dispatch = span_of(3);
+  fa.ts_permute = span_of(4);
+  fa.ts_combine = span_of(7);
+  fa.ts_final = span_of(8);
   if (timing) FB_CUDA(cudaEventRecord(L->tev[8], stream));
   if ((s = fused_dispatch(fa, seq, stream))) return s;
   if ((s = fused_permute(fa, seq, sum.n_routes, stream))) return s;
@@ -483,14 +495,9 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   // 8 grouped SwiGLU (kernel 5), both phases per launch: the experts cached
   //   before this layer (no waits), then the fetched experts, whose tiles
   //   start as their readiness flags arrive
-  unsigned long long* ts = nullptr;
-  if (timing && sum.n_hit > 0 && L->ts_used.size() <= (size_t)ferryb_layer::kTs) {
-    const size_t slot = L->ts_used.size() - 1;
-    ts = L->gemm_ts + 2 * slot;
-    L->ts_used.back() = 1;
-  }
   if ((s = swiglu_fused_launch(L->maps, L->groups, sum.n_hit, sum.n_hit, nullptr, 0, L->queue_dep,
-                               L->route_w, L->act, L->expert_out, L->errs + 2, stream, ts)))
+                               L->route_w, L->act, L->expert_out, L->errs + 2, stream,
+                               span_of(5))))
     return s;
   if (sum.n_hit) launches += 1;
   if (shared) {  // dense shared expert on every local token, in the copies' shadow
@@ -517,7 +524,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   }
   if ((s = swiglu_fused_launch(L->maps, L->groups + sum.n_hit, sum.n_fetch_mine, 0, L->ready,
                                ready_value, L->queue_dep, L->route_w, L->act, L->expert_out,
-                               L->errs + 2, stream)))
+                               L->errs + 2, stream, span_of(6))))
     return s;
   if (sum.n_fetch_mine) launches += 1;
   if (!c.sync_fetch && sum.n_fetch_mine > 1) {
@@ -597,16 +604,25 @@ extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
   }
   L->tev_fetched.clear();
   if (!L->ts_used.empty()) {
-    std::vector<unsigned long long> ts(2 * ferryb_layer::kTs);
-    FB_CUDA(cudaMemcpy(ts.data(), L->gemm_ts, ts.size() * sizeof(unsigned long long),
+    constexpr int S = ferryb_layer::kSpans;
+    std::vector<unsigned long long> ts(2 * ferryb_layer::kTs * S);
+    FB_CUDA(cudaMemcpy(ts.data(), L->spans, ts.size() * sizeof(unsigned long long),
                        cudaMemcpyDeviceToHost));
     for (size_t i = 0; i < L->ts_used.size() && i < (size_t)ferryb_layer::kTs; ++i) {
-      if (!L->ts_used[i] || ts[2 * i + 1] < ts[2 * i]) continue;
-      L->stats.hit_gemm_kernel_us += (double)(ts[2 * i + 1] - ts[2 * i]) / 1000.0;
-      L->stats.hit_gemm_kernel_launches += 1;
+      if (!L->ts_used[i]) continue;
+      for (int k = 0; k < S; ++k) {
+        const unsigned long long t0 = ts[2 * (i * S + k)], t1 = ts[2 * (i * S + k) + 1];
+        if (t1 < t0) continue;  // the kernel did not run in this layer
+        L->stats.kernel_us[k] += (double)(t1 - t0) / 1000.0;
+        L->stats.kernel_launches[k] += 1;
+        if (k == 5) {
+          L->stats.hit_gemm_kernel_us += (double)(t1 - t0) / 1000.0;
+          L->stats.hit_gemm_kernel_launches += 1;
+        }
+      }
     }
-    for (size_t i = 0; i < (size_t)ferryb_layer::kTs; ++i) { ts[2 * i] = ~0ull; ts[2 * i + 1] = 0; }
-    FB_CUDA(cudaMemcpy(L->gemm_ts, ts.data(), ts.size() * sizeof(unsigned long long),
+    for (size_t i = 0; i < ts.size() / 2; ++i) { ts[2 * i] = ~0ull; ts[2 * i + 1] = 0; }
+    FB_CUDA(cudaMemcpy(L->spans, ts.data(), ts.size() * sizeof(unsigned long long),
                        cudaMemcpyHostToDevice));
     L->ts_used.clear();
   }

@@ -103,12 +103,14 @@ __device__ __forceinline__ int packet_ids(const TokenRoutes& r, int K, int peer,
   return size;
 }
 
-__global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs a) {
+__global__ void __launch_bounds__(kLayThreads, 1)
+    layout_kernel(const LayoutArgs a, unsigned long long* ts) {
   __shared__ LaySmem sm;
   __shared__ int total_sh;
   const int tid = threadIdx.x;
   const int R = a.world, T = a.tokens_per_rank, K = a.topk, E = a.experts, rank = a.rank;
   const int n_tok = R * T;
+  span_begin(ts);
   int ids_buf[16];
 
   // ---- fetched experts of this rank, in fetch order -----------------------
@@ -327,6 +329,8 @@ __global__ void __launch_bounds__(kLayThreads, 1) layout_kernel(const LayoutArgs
     __syncthreads();
     if (tid == 0) a.summary->err = atomicAdd(a.err, 0);
   }
+  __syncthreads();
+  span_end(ts);
 }
 
 // layer_slots (ferry/policy.py:197-205) for one rank's slots row.
@@ -340,10 +344,10 @@ __global__ void layer_slots_kernel(const int32_t* slots_row, int capacity, int l
   }
 }
 
-int layout_launch(const LayoutArgs& a, cudaStream_t stream) {
+int layout_launch(const LayoutArgs& a, cudaStream_t stream, unsigned long long* ts) {
   FB_CHECK_ARG(a.experts <= kMaxExpertsL && a.topk <= 16 && a.world >= 1,
                "layout: experts <= %d and topk <= 16 required", kMaxExpertsL);
-  layout_kernel<<<1, kLayThreads, 0, stream>>>(a);
+  layout_kernel<<<1, kLayThreads, 0, stream>>>(a, ts);
   FB_LAUNCH_CHECK();
   return FERRYB_OK;
 }

@@ -11,7 +11,8 @@ constexpr int kMaxWorldL = 32;
 
 using LayoutArgs = ferryb_layout_args;  // include/ferryb.h
 
-int layout_launch(const LayoutArgs& a, cudaStream_t stream);
+// ts: device-clock span of the launch (timing mode) or null
+int layout_launch(const LayoutArgs& a, cudaStream_t stream, unsigned long long* ts = nullptr);
 int layer_slots_launch(const int32_t* slots_row, int capacity, int layer, int experts,
                        int32_t* lookup, cudaStream_t stream);
 

@@ -481,6 +481,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   int64_t* greedy_load = reinterpret_cast<int64_t*>(dsm + c.greedy_offset);  // [G]
 
   PLAN_TS(0);
+  span_begin(in.ts);
   if (tid == 0) {
     sm.status = 0;
     sm.m = 0;
@@ -720,6 +721,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   }
   __syncthreads();
   PLAN_TS(7);
+  span_end(in.ts);
 }
 
 // ---------------------------------------------------------------------------

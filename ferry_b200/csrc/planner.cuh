@@ -50,6 +50,7 @@ struct PlanInputs {
   const int* hist;         // [world, experts] per-rank demand histograms
   int* hist_clear;         // non-null (one rank): the router's own histogram, read from
                            // `hist` and zeroed here for the next layer
+  unsigned long long* ts;  // device-clock span (timing mode) or null
 };
 
 struct PlanOutputs {

@@ -36,6 +36,7 @@ __global__ void __launch_bounds__(kRouterThreads)
   const int H = a.hdim, E = a.experts, K = a.topk;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const __nv_bfloat16* x = a.hidden + (size_t)t * H;
+  span_begin(a.ts);
 
   if (a.mode == 2) {
     // routing given by the caller: gather only
@@ -189,6 +190,7 @@ __global__ void __launch_bounds__(kRouterThreads)
   }
   // With one rank the planner, next on the stream, reads the histogram and
   // the ids this kernel wrote (the kernel boundary orders them): no flags.
+  span_end(a.ts);
   if (a.world == 1) return;
   // ---- last CTA: histogram + flags ----
   // One system-scope fence per CTA, by thread 0 after a CTA barrier (the

@@ -31,6 +31,7 @@ struct RouterArgs {
   int prob_tail;                      // rows per rank of the probability history, 0 = off
   const uintptr_t* peer_base;   // [world] symmetric buffer bases
   size_t buf_stride, off_ids, off_hist, off_flag, off_prob;
+  unsigned long long* ts;       // device-clock span (timing mode) or null
 };
 
 int router_launch(const RouterArgs& a, uint64_t seq, cudaStream_t stream);

@@ -248,6 +248,7 @@ __global__ void fused_dispatch_kernel(const FusedArgs a) {
   const int R = a.world, K = a.topk, H = a.hdim;
   const int g = a.rank * a.tokens_per_rank + t;
   __shared__ int ids_s[kMaxTopK], pos_s[kMaxTopK];
+  span_begin(a.ts_dispatch);
   for (int p = 0; p < R; ++p) {
     const int row = a.peer_row[t * R + p];
     if (row < 0) continue;
@@ -276,6 +277,7 @@ __global__ void fused_dispatch_kernel(const FusedArgs a) {
     }
     __syncthreads();
   }
+  span_end(a.ts_dispatch);
 }
 
 // Raise this rank's flag in every peer's `flag_off` array (after the
@@ -294,6 +296,7 @@ __global__ void signal_kernel(const FusedArgs a, size_t flag_off, uint64_t seq) 
 __global__ void fused_permute_kernel(const FusedArgs a, uint64_t seq) {
   uint8_t* base = reinterpret_cast<uint8_t*>(a.local_base) + a.parity * a.buf_stride;
   __shared__ int ok;
+  span_begin(a.ts_permute);
   if (threadIdx.x == 0)
     ok = a.world == 1 ||
          wait_flags(reinterpret_cast<const uint64_t*>(base + a.off_dflag), a.world, seq, a.err);
@@ -311,6 +314,8 @@ __global__ void fused_permute_kernel(const FusedArgs a, uint64_t seq) {
         reinterpret_cast<const uint4*>(rx + (size_t)row * H)[v];
     if (v == 0) a.route_w[p] = rw[(size_t)row * K + a.cols[p]];
   }
+  __syncthreads();
+  span_end(a.ts_permute);
 }
 
 // o = bf16(float(o) + float(b)) lane-wise (a torch bf16 add)
@@ -328,6 +333,7 @@ __global__ void fused_combine_kernel(const FusedArgs a) {
   const int row = blockIdx.x;
   const int n_recv = *a.n_recv_dev;
   if (row >= n_recv) return;
+  span_begin(a.ts_combine);
   const int H = a.hdim, K = a.topk;
   const int g = a.recv_token[row];
   const int src = g / a.tokens_per_rank, t = g % a.tokens_per_rank;
@@ -365,6 +371,8 @@ __global__ void fused_combine_kernel(const FusedArgs a) {
     if (add) add_bf16x8(o, *reinterpret_cast<const uint4*>(add + c));
     *reinterpret_cast<uint4*>(dst + c) = o;
   }
+  __syncthreads();
+  span_end(a.ts_combine);
 }
 
 // final scatter (source side, world > 1): out[t] = bf16(sum over peers p in
@@ -373,6 +381,7 @@ __global__ void fused_final_kernel(const FusedArgs a, uint64_t seq) {
   const int t = blockIdx.x;
   uint8_t* base = reinterpret_cast<uint8_t*>(a.local_base) + a.parity * a.buf_stride;
   __shared__ int ok;
+  span_begin(a.ts_final);
   if (threadIdx.x == 0)
     ok = wait_flags(reinterpret_cast<const uint64_t*>(base + a.off_cflag), a.world, seq, a.err);
   __syncthreads();
@@ -397,6 +406,8 @@ __global__ void fused_final_kernel(const FusedArgs a, uint64_t seq) {
     if (a.addend) add_bf16x8(o, *reinterpret_cast<const uint4*>(a.addend + (size_t)t * H + c));
     *reinterpret_cast<uint4*>(a.out + (size_t)t * H + c) = o;
   }
+  __syncthreads();
+  span_end(a.ts_final);
 }
 
 int fused_dispatch(const FusedArgs& a, uint64_t seq, cudaStream_t stream) {

@@ -42,6 +42,8 @@ struct FusedArgs {
   __nv_bfloat16* out;         // [T, H]
   const __nv_bfloat16* addend;  // [T, H] or null: out = bf16(bf16(routed) + addend)
   int* err;
+  // device-clock spans (timing mode) or null
+  unsigned long long *ts_dispatch, *ts_permute, *ts_combine, *ts_final;
 };
 
 SymLayout sym_layout(int world, int tokens_per_rank, int topk, int hidden, int experts);

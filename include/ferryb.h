@@ -401,6 +401,11 @@ typedef struct ferryb_layer_stats {
                                  peers' packets included) */
   double combine_store_us;    /* timing mode: the combine kernel alone (this rank's partials
                                  reduced and stored to their source ranks) */
+  double kernel_us[9];        /* timing mode, device clock (earliest CTA start to latest CTA
+                                 end), summed: router, planner, layout, dispatch, permute,
+                                 cached-expert GEMM, fetched-expert GEMM, combine, final
+                                 scatter (more than one rank) */
+  int64_t kernel_launches[9];
 } ferryb_layer_stats;
 
 typedef struct ferryb_layer ferryb_layer;
