@@ -25,7 +25,8 @@ class Planner(ctypes.Structure):
                 ('maxcap', _i32c), ('total_slots', _i32c), ('n_domains', _i32c),
                 ('lut_rows', _i32c)] + [(n, _vp) for n in (
                     'capacities', 'slot_rank', 'slot_index', 'lut', 'masks', 'seconds', 'slots',
-                    'owner', 'last', 'scores', 'ring', 'ring_p', 'hist_count', 'hist_head')]
+                    'owner', 'last', 'scores', 'ring', 'ring_p', 'hist_count', 'hist_head',
+                    'order_meta', 'order_rec')] + [('order_cap', _i32c)]
 
 
 class LayoutSummary(ctypes.Structure):

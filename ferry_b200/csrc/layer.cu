@@ -262,9 +262,8 @@ extern "C" int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_
   c.slot_rank = planner->slot_rank; c.slot_index = planner->slot_index; c.lut = planner->lut;
   c.masks = planner->masks; c.seconds = planner->seconds;
   c.dyn_smem = plan_dyn_smem(c.experts, c.world, c.total_slots, c.n_domains, &c.sort_offset,
-                             &c.greedy_offset, &c.sort_n);
-  L->ps = PlanState{planner->slots, planner->owner, planner->last, planner->scores,
-                    planner->ring, planner->ring_p, planner->hist_count, planner->hist_head};
+                             &c.greedy_offset, &c.sort_n, &c.dirty_offset);
+  L->ps = plan_state(planner);
   FB_CUDA(cudaMemset(workspace, 0, (size_t)workspace_size));
   FB_CUDA(cudaMemcpy(L->peer_base_dev, peer_bases, sizeof(uint64_t) * cfg->world,
                      cudaMemcpyHostToDevice));

@@ -36,6 +36,11 @@
 namespace ferryb {
 
 constexpr int kPlanThreads = 1024;
+// The incremental victim order keeps each thread's entries in registers:
+// up to kMaxIncremental / kPlanThreads of them.
+constexpr int kMaxIncremental = 4096;
+constexpr int kIncPer = kMaxIncremental / kPlanThreads;
+constexpr int kRankSort = kPlanThreads;  // dirty records sorted by counting below this
 constexpr int kPlanWarps = kPlanThreads / 32;
 
 struct SlotRec {
@@ -100,7 +105,8 @@ struct PlanSmem {
   int64_t loads[kMaxWorld];
   int n_assigned[kMaxWorld];
   int seg_start[kMaxWorld + 1];
-  int blk_start[kMaxWorld + 1];  // first 64-record block of each rank (fast victim path)
+  int warp_sum[32];
+  int scan_total;
   float gate[kMaxExperts];
   int owner_layer[kMaxExperts];
   int status;
@@ -416,56 +422,66 @@ __device__ void sort_records(uint64_t* k0, uint64_t* k1, uint32_t* sl, int n) {
   }
 }
 
-// Per rank, the 64 smallest records in ascending order, in the rank's first
-// block.  Rank r owns blocks [blk_start[r], blk_start[r + 1]) of 64 records
-// (padding records are ~0 and sort last).  Every block is sorted in registers
-// by one warp; then, level by level, one warp merges block pairs (left, left
-// + stride) of the same rank into the left block, keeping the lower half:
-// c[i] = min(A[i], B[63 - i]) is the lower 64 of A and B as a bitonic
-// sequence, which six shuffle stages sort.
-__device__ void select_lowest64(uint64_t* k0, uint64_t* k1, uint32_t* sl, const int* blk_start,
-                                int R) {
+// Exclusive block-wide prefix sum of one int per thread; *total (shared
+// memory) gets the sum, visible to every thread on return.
+__device__ int plan_block_scan(int v, int* warp_sum, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int n_warps = blockDim.x >> 5;
-  const int n_blocks = blk_start[R];
-  for (int blk = warp; blk < n_blocks; blk += n_warps) {
-    const int ia = blk * 64 + lane, ib = ia + 32;
-    Rec a{k0[ia], k1[ia], sl[ia]}, b{k0[ib], k1[ib], sl[ib]};
-    for (int size = 2; size <= 64; size <<= 1) warp_stages(a, b, lane, size, size >> 1, lane);
-    k0[ia] = a.k0; k1[ia] = a.k1; sl[ia] = a.sl;
-    k0[ib] = b.k0; k1[ib] = b.k1; sl[ib] = b.sl;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = lane < (int)(blockDim.x >> 5) ? warp_sum[lane] : 0;
+    int wx = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wx, o);
+      if (lane >= o) wx += y;
+    }
+    warp_sum[lane] = wx - w;
+    if (lane == 31) *total = wx;
   }
   __syncthreads();
-  int max_nb = 0;
-  for (int r = 0; r < R; ++r) max_nb = max(max_nb, blk_start[r + 1] - blk_start[r]);
-  for (int stride = 1; stride < max_nb; stride <<= 1) {
-    // merges of this level, rank-major: rank r has ceil((nb_r - stride) / (2 stride))
-    int total = 0;
-    for (int r = 0; r < R; ++r) {
-      const int nb = blk_start[r + 1] - blk_start[r];
-      total += nb > stride ? (nb - stride + 2 * stride - 1) / (2 * stride) : 0;
-    }
-    for (int item = warp; item < total; item += n_warps) {
-      int r = 0, q = item;
-      for (; r < R; ++r) {
-        const int nb = blk_start[r + 1] - blk_start[r];
-        const int cnt = nb > stride ? (nb - stride + 2 * stride - 1) / (2 * stride) : 0;
-        if (q < cnt) break;
-        q -= cnt;
-      }
-      const int left = blk_start[r] + 2 * stride * q, right = left + stride;
-      const int ia = left * 64 + lane, ja = right * 64 + lane;
-      const Rec a0{k0[ia], k1[ia], sl[ia]}, a1{k0[ia + 32], k1[ia + 32], sl[ia + 32]};
-      const Rec b0{k0[ja], k1[ja], sl[ja]}, b1{k0[ja + 32], k1[ja + 32], sl[ja + 32]};
-      const Rec rb1 = shfl_rec(b1, 31), rb0 = shfl_rec(b0, 31);  // B[63 - i]
-      Rec c0 = rec_lt(rb1, a0) ? rb1 : a0;
-      Rec c1 = rec_lt(rb0, a1) ? rb0 : a1;
-      warp_stages(c0, c1, lane, 64, 32, lane);
-      k0[ia] = c0.k0; k1[ia] = c0.k1; sl[ia] = c0.sl;
-      k0[ia + 32] = c1.k0; k1[ia + 32] = c1.k1; sl[ia + 32] = c1.sl;
-    }
-    __syncthreads();
+  const int res = warp_sum[warp] + x - v;
+  __syncthreads();
+  return res;
+}
+
+// Number of records of (k0, k1)[0, len) (ascending) that are smaller than key.
+__device__ __forceinline__ int count_less(const uint64_t* k0, const uint64_t* k1, int len, uint64_t a0,
+                                          uint64_t a1) {
+  int lo = 0, hi = len;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    const bool less = k0[mid] < a0 || (k0[mid] == a0 && k1[mid] < a1);
+    if (less) lo = mid + 1;
+    else hi = mid;
   }
+  return lo;
+}
+
+// The eviction record of slot `idx` (rank r) holding `key` in layer L's plan:
+// k0 = rank << 56 | class << 48 | score bits, k1 = last use << 24 | key;
+// class 0 empty (by slot index), 1 eligible, 2 holds an expert active in L.
+__device__ __forceinline__ void slot_record(const PlanConfig& c, const PlanState& s, const int* active,
+                                            int r, int idx, int key, int L, uint64_t& a0, uint64_t& a1) {
+  const int E = c.experts;
+  uint64_t cls, lo, hi;
+  if (key < 0) {
+    cls = 0; lo = 0; hi = (uint64_t)(idx - r * c.maxcap);
+  } else if (key / E == L && active[key % E]) {
+    cls = 2; lo = 0; hi = (uint64_t)key;
+  } else {
+    cls = 1;
+    lo = __float_as_uint(s.scores[key]);
+    hi = ((uint64_t)s.last[key] << 24) | (uint64_t)key;
+  }
+  a0 = ((uint64_t)r << 56) | (cls << 48) | lo;
+  a1 = hi;
 }
 
 __global__ void __launch_bounds__(kPlanThreads, 1)
@@ -616,79 +632,153 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     if (tid == 0) {
       set_err(out.err, sm.status);
       *out.n_fetches = 0;
+      // this layer's scores changed above: the saved victim order is stale
+      if (s.order_meta) s.order_meta[0] = 0;
     }
     return;
   }
 
   // -- Step 4: victims (one ordering of every slot) and the commit ---------
-  // The j-th miss assigned to rank r takes the j-th smallest slot record of
-  // rank r.  When every rank needs at most 64 victims and the ranks' slots
-  // fit whole 64-record blocks, each rank keeps only its 64 smallest records
-  // (select_lowest64); otherwise all records are sorted (sort_records).
+  // The j-th miss assigned to rank r takes the j-th record of rank r's
+  // segment of the order of all slot records.  That order is saved between
+  // layers: a record changes only when its slot's content changes or when
+  // its key belongs to a layer planned since the order was saved (scores at
+  // the start of a plan, last uses and installs at its end) or to this layer
+  // (class 2), so only those records are re-keyed, sorted among themselves
+  // and merged into the rest.  Without a valid saved order every record is
+  // sorted.
+  const int words = (c.layers + 63) / 64;
+  const bool can_save = s.order_meta != nullptr && c.dirty_offset != 0 && s.order_cap >= c.sort_n;
   if (m > 0) {
     const int n = c.sort_n;  // power of two >= total_slots, >= 64
     uint64_t* k0 = reinterpret_cast<uint64_t*>(recs);
     uint64_t* k1 = k0 + n;
     uint32_t* sl = reinterpret_cast<uint32_t*>(k1 + n);
     if (tid == 0) {
-      int pos = 0, blk = 0;
-      for (int r = 0; r < R; ++r) {
-        sm.seg_start[r] = pos;
-        sm.blk_start[r] = blk;
-        pos += c.capacities[r];
-        blk += (c.capacities[r] + 63) / 64;
-      }
-      sm.blk_start[R] = blk;
+      int pos = 0;
+      for (int r = 0; r < R; ++r) { sm.seg_start[r] = pos; pos += c.capacities[r]; }
     }
-    if (tid < R) sm.n_assigned[tid] = 0;
-    __syncthreads();
     for (int i = tid; i < m; i += blockDim.x) {
       const int r = sm.assignment[i];
       int before = 0;  // earlier misses assigned to the same rank
       for (int j = 0; j < i; ++j) before += sm.assignment[j] == r;
-      sm.victim_pos[i] = before;  // rank-relative for now
-      if (r >= 0 && r < R) atomicMax(&sm.n_assigned[r], before + 1);
+      sm.victim_pos[i] = before;  // rank-relative
     }
-    __syncthreads();
-    bool fast = sm.blk_start[R] * 64 <= n;
-    for (int r = 0; r < R; ++r) fast = fast && sm.n_assigned[r] <= 64;
-    for (int i = tid; i < n; i += blockDim.x) { k0[i] = ~0ull; k1[i] = ~0ull; sl[i] = 0xffffffffu; }
-    __syncthreads();
-    for (int i = tid; i < c.total_slots; i += blockDim.x) {
-      const int r = c.slot_rank[i];
-      const int idx = c.slot_index[i];
-      const int key = s.slots[idx];
-      uint64_t cls, lo, hi;
-      if (key < 0) {
-        cls = 0; lo = 0; hi = (uint64_t)(idx - r * c.maxcap);
-      } else if (key / E == L && sm.active[key % E]) {
-        cls = 2; lo = 0; hi = 0;
-      } else {
-        cls = 1;
-        lo = __float_as_uint(s.scores[key]);
-        hi = ((uint64_t)s.last[key] << 24) | (uint64_t)key;
-      }
-      // fast: rank r's records fill its own 64-record blocks (padded)
-      const int pos = fast ? sm.blk_start[r] * 64 + (i - sm.seg_start[r]) : i;
-      k0[pos] = ((uint64_t)r << 56) | (cls << 48) | lo;
-      k1[pos] = hi;
-      sl[pos] = (uint32_t)idx;
-    }
-    __syncthreads();
+    const bool incremental = can_save && s.order_meta[0] != 0;
     PLAN_TS(4);
-    if (fast) select_lowest64(k0, k1, sl, sm.blk_start, R);
-    else sort_records(k0, k1, sl, n);
+    // the order the commit reads: the saved one, or the records in smem
+    const uint64_t* o0 = k0;
+    const uint32_t* osl = sl;
+    if (!incremental) {
+      for (int i = tid; i < n; i += blockDim.x) {
+        uint64_t a0 = ~0ull, a1 = ~0ull;
+        uint32_t ix = 0xffffffffu;
+        if (i < c.total_slots) {
+          const int r = c.slot_rank[i], idx = c.slot_index[i];
+          slot_record(c, s, sm.active, r, idx, s.slots[idx], L, a0, a1);
+          ix = (uint32_t)idx;
+        }
+        k0[i] = a0; k1[i] = a1; sl[i] = ix;
+      }
+      __syncthreads();
+      sort_records(k0, k1, sl, n);
+      if (can_save) {
+        for (int i = tid; i < n; i += blockDim.x) {
+          s.ord_k0[i] = k0[i]; s.ord_k1[i] = k1[i]; s.ord_sl[i] = sl[i];
+        }
+      }
+    } else {
+      uint64_t* dk0 = reinterpret_cast<uint64_t*>(dsm + c.dirty_offset);
+      uint64_t* dk1 = dk0 + n;
+      uint32_t* dsl = reinterpret_cast<uint32_t*>(dk1 + n);
+      const int64_t* changed = s.order_meta + 1;  // layers planned since the order was saved
+      // each thread's saved entries i = tid + q * blockDim.x, in registers
+      const int nq = (n + (int)blockDim.x - 1) / (int)blockDim.x;  // <= kIncPer
+      uint64_t e0[kIncPer], e1[kIncPer];
+      uint32_t es[kIncPer];
+      bool dirty[kIncPer];
+#pragma unroll
+      for (int q = 0; q < kIncPer; ++q) {
+        const int i = tid + q * (int)blockDim.x;
+        dirty[q] = false;
+        if (q < nq && i < n) {
+          e0[q] = s.ord_k0[i]; e1[q] = s.ord_k1[i]; es[q] = s.ord_sl[i];
+          if (es[q] != 0xffffffffu) {
+            const int key = s.slots[es[q]];
+            const int cls = (int)((e0[q] >> 48) & 0xff);
+            const int saved_key = cls == 0 ? -1 : (int)(e1[q] & 0xffffff);
+            const int kl = key >= 0 ? key / E : -1;
+            dirty[q] = key != saved_key ||
+                       (key >= 0 && (kl == L || ((changed[kl >> 6] >> (kl & 63)) & 1)));
+          }
+        }
+      }
+      // stable compaction of the clean entries (saved order kept) into k0/k1/sl;
+      // the dirty ones are re-keyed into dk0/dk1/dsl (entry i has i - cpos
+      // dirty entries before it)
+      int clean_base = 0;
+#pragma unroll
+      for (int q = 0; q < kIncPer; ++q) {
+        if (q >= nq) break;
+        const int i = tid + q * (int)blockDim.x;
+        const bool live = i < n;
+        const int cpos = clean_base + plan_block_scan(live && !dirty[q], sm.warp_sum, &sm.scan_total);
+        clean_base += sm.scan_total;
+        const int dpos = i - cpos;
+        if (live && !dirty[q]) { k0[cpos] = e0[q]; k1[cpos] = e1[q]; sl[cpos] = es[q]; }
+        if (live && dirty[q]) {
+          const int idx = (int)es[q];
+          const int r = idx / c.maxcap;
+          uint64_t a0, a1;
+          slot_record(c, s, sm.active, r, idx, s.slots[idx], L, a0, a1);
+          dk0[dpos] = a0; dk1[dpos] = a1; dsl[dpos] = es[q];
+        }
+      }
+      const int nc = clean_base, nd = n - clean_base;
+      __syncthreads();
+      if (nd <= kRankSort) {
+        // up to one dirty record per thread: each one's place is the number
+        // of dirty records below it (their keys are unique); all reads are
+        // done before the barrier, so the records move in place
+        uint64_t a0 = 0, a1 = 0;
+        uint32_t ax = 0;
+        int place = 0;
+        if (tid < nd) {
+          a0 = dk0[tid]; a1 = dk1[tid]; ax = dsl[tid];
+          for (int k = 0; k < nd; ++k) place += dk0[k] < a0 || (dk0[k] == a0 && dk1[k] < a1);
+        }
+        __syncthreads();
+        if (tid < nd) { dk0[place] = a0; dk1[place] = a1; dsl[place] = ax; }
+        __syncthreads();
+      } else {
+        int dn = 64;
+        while (dn < nd) dn <<= 1;
+        for (int j = nd + tid; j < dn; j += blockDim.x) { dk0[j] = ~0ull; dk1[j] = ~0ull; dsl[j] = 0xffffffffu; }
+        __syncthreads();
+        sort_records(dk0, dk1, dsl, dn);
+      }
+      // merge: a clean record's position is its index plus the dirty records
+      // below it, and the other way round (keys of real records are unique)
+      for (int i = tid; i < nc; i += blockDim.x) {
+        const int pos = i + count_less(dk0, dk1, nd, k0[i], k1[i]);
+        s.ord_k0[pos] = k0[i]; s.ord_k1[pos] = k1[i]; s.ord_sl[pos] = sl[i];
+      }
+      for (int j = tid; j < nd; j += blockDim.x) {
+        const int pos = j + count_less(k0, k1, nc, dk0[j], dk1[j]);
+        s.ord_k0[pos] = dk0[j]; s.ord_k1[pos] = dk1[j]; s.ord_sl[pos] = dsl[j];
+      }
+      __syncthreads();
+      o0 = s.ord_k0; osl = s.ord_sl;
+    }
+    __syncthreads();
     PLAN_TS(5);
     for (int i = tid; i < m; i += blockDim.x) {
       const int r = sm.assignment[i];
       const int j = sm.victim_pos[i];
-      int vp = -1;
-      if (r >= 0 && r < R && j < c.capacities[r])
-        vp = fast ? (sm.blk_start[r + 1] > sm.blk_start[r] ? sm.blk_start[r] * 64 + j : -1)
-                  : sm.seg_start[r] + j;
+      const int vp = (r >= 0 && r < R && j < c.capacities[r]) ? sm.seg_start[r] + j : -1;
       if (vp < 0 || vp >= n) { set_err(out.err, DEV_NO_SLOT); continue; }
-      const uint64_t rk0 = k0[vp];
-      const uint32_t rslot = sl[vp];
+      const uint64_t rk0 = o0[vp];
+      const uint32_t rslot = osl[vp];
       const uint64_t cls = (rk0 >> 48) & 0xff;
       const bool ok = rslot != 0xffffffffu && (int)(rk0 >> 56) == r && cls < 2;
       if (!ok) { set_err(out.err, DEV_NO_SLOT); continue; }
@@ -702,6 +792,16 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
       out.fetches[i * 3 + 1] = key;
       out.fetches[i * 3 + 2] = idx - r * c.maxcap;
     }
+    // the saved order now holds every record as of this plan; this layer's
+    // records change at its commit, so they are re-keyed next time
+    __syncthreads();
+    if (can_save && tid == 0) {
+      s.order_meta[0] = 1;
+      for (int w = 0; w < words; ++w) s.order_meta[1 + w] = 0;
+      s.order_meta[1 + (L >> 6)] = (int64_t)(1ull << (L & 63));
+    }
+  } else if (can_save && tid == 0 && s.order_meta[0] != 0) {
+    s.order_meta[1 + (L >> 6)] |= (int64_t)(1ull << (L & 63));  // no commit, but scores and last uses change
   }
   __syncthreads();
   PLAN_TS(6);
@@ -857,7 +957,7 @@ int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
 }
 
 size_t plan_dyn_smem(int experts, int world, int total_slots, int n_domains, size_t* sort_off,
-                     size_t* greedy_off, int* sort_n) {
+                     size_t* greedy_off, int* sort_n, size_t* dirty_off) {
   size_t off = (size_t)experts * world * sizeof(int);
   off = (off + 15) & ~size_t(15);
   int n = 64;  // the sort works on whole 64-record warp blocks
@@ -867,6 +967,12 @@ size_t plan_dyn_smem(int experts, int world, int total_slots, int n_domains, siz
   off += (size_t)n * sizeof(SlotRec);
   *greedy_off = off;
   off += (size_t)(n_domains > 0 ? n_domains : 1) * sizeof(int64_t);
+  off = (off + 15) & ~size_t(15);
+  *dirty_off = 0;
+  if (n <= kMaxIncremental) {  // the incremental order's dirty records: up to n of them
+    *dirty_off = off;
+    off += (size_t)n * sizeof(SlotRec);
+  }
   return off;
 }
 
@@ -908,11 +1014,10 @@ extern "C" int ferryb_plan_layer(const ferryb_planner* p, int64_t event, int32_t
   c.lut_rows = p->lut_rows; c.capacities = p->capacities; c.slot_rank = p->slot_rank;
   c.slot_index = p->slot_index; c.lut = p->lut; c.masks = p->masks; c.seconds = p->seconds;
   c.dyn_smem = plan_dyn_smem(c.experts, c.world, c.total_slots, c.n_domains, &c.sort_offset,
-                             &c.greedy_offset, &c.sort_n);
+                             &c.greedy_offset, &c.sort_n, &c.dirty_offset);
   FB_CHECK_ARG(c.dyn_smem + plan_static_smem() <= 225 * 1024,
                "cache too large for the one-CTA planner (%d slots)", c.total_slots);
-  PlanState s{p->slots, p->owner, p->last, p->scores, p->ring, p->ring_p, p->hist_count,
-              p->hist_head};
+  const PlanState s = plan_state(p);
   PlanInputs in{};
   in.ids = ids; in.n_tokens = n_tokens; in.tokens_per_rank = tokens_per_rank;
   in.origins = origins; in.gate_scores = gate_scores; in.prob_rows = prob_rows;

@@ -20,7 +20,7 @@ struct PlanConfig {
   const int64_t* masks;       // [n_domains]
   const double* seconds;      // [n_domains]
   // derived launch geometry
-  size_t dyn_smem, sort_offset, greedy_offset;
+  size_t dyn_smem, sort_offset, greedy_offset, dirty_offset;  // dirty_offset 0: no room
   int sort_n;
 };
 
@@ -33,7 +33,26 @@ struct PlanState {
   float* ring_p;    // [layers, window, experts] (probability score) or null
   int32_t* hist_count;
   int32_t* hist_head;
+  // saved victim order (null = off): meta [1 + ceil(layers / 64)], records SoA
+  int64_t* order_meta;
+  uint64_t *ord_k0, *ord_k1;
+  uint32_t* ord_sl;
+  int order_cap;
 };
+
+// PlanState of a planner (the saved order's SoA views of order_rec).
+inline PlanState plan_state(const ferryb_planner* p) {
+  PlanState s{p->slots, p->owner, p->last, p->scores, p->ring, p->ring_p, p->hist_count,
+              p->hist_head, nullptr, nullptr, nullptr, nullptr, 0};
+  if (p->order_meta && p->order_rec && p->order_cap >= 64) {
+    s.order_meta = p->order_meta;
+    s.ord_k0 = reinterpret_cast<uint64_t*>(p->order_rec);
+    s.ord_k1 = s.ord_k0 + p->order_cap;
+    s.ord_sl = reinterpret_cast<uint32_t*>(s.ord_k1 + p->order_cap);
+    s.order_cap = p->order_cap;
+  }
+  return s;
+}
 
 struct PlanInputs {
   const uint8_t* ids;  // [n_tokens, topk] gathered expert ids
@@ -63,8 +82,11 @@ struct PlanOutputs {
 
 int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
                 const PlanOutputs& out, cudaStream_t stream);
+// Dynamic shared memory of the planner: demand, the slot records, greedy
+// loads and (room permitting) the dirty-record buffer of the incremental
+// victim order (*dirty_off = 0 when there is no room).
 size_t plan_dyn_smem(int experts, int world, int total_slots, int n_domains, size_t* sort_off,
-                     size_t* greedy_off, int* sort_n);
+                     size_t* greedy_off, int* sort_n, size_t* dirty_off);
 size_t plan_static_smem();
 
 }  // namespace ferryb

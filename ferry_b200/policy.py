@@ -150,6 +150,7 @@ class Controller:
                 self._ring_p.zero_()
             self._hist_count.zero_()
             self._hist_head.zero_()
+            self._order_meta.zero_()  # the saved victim order is rebuilt on the next plan
             return
         dev, L, E, W, K = self.device, self.spec.layers, self.spec.experts, self.window, self.topk
         self._slots = torch.full((self.world, self.maxcap), -1, dtype=torch.int32, device=dev)
@@ -161,6 +162,14 @@ class Controller:
                         if self.score == 'probability' else None)
         self._hist_count = torch.zeros(L, dtype=torch.int32, device=dev)
         self._hist_head = torch.zeros(L, dtype=torch.int32, device=dev)
+        # saved victim order: [valid, bitmask of changed layers], records of
+        # order_cap slots (the planner's sort size: a power of two >= 64)
+        total = int(self.capacities.sum())
+        cap = 64
+        while cap < total:
+            cap <<= 1
+        self._order_meta = torch.zeros(1 + (L + 63) // 64, dtype=torch.int64, device=dev)
+        self._order_rec = torch.zeros(cap * 20, dtype=torch.uint8, device=dev)
         s = _lib.Planner()
         s.world, s.experts, s.layers, s.topk, s.window = self.world, E, L, K, W
         s.policy, s.balance_tol_bps, s.salt = self.policy, self.balance_tol_bps, self.salt
@@ -171,8 +180,10 @@ class Controller:
                         ('seconds', self._seconds), ('slots', self._slots), ('owner', self._owner),
                         ('last', self._last), ('scores', self._scores), ('ring', self._ring),
                         ('ring_p', self._ring_p), ('hist_count', self._hist_count),
-                        ('hist_head', self._hist_head)):
+                        ('hist_head', self._hist_head), ('order_meta', self._order_meta),
+                        ('order_rec', self._order_rec)):
             setattr(s, name, addr(t))
+        s.order_cap = cap
         self._struct = s
 
     # host views of the device state (the reference exposes numpy arrays)

@@ -140,6 +140,17 @@ typedef struct ferryb_planner {
   float* ring_p;             /* [layers, window, experts] probability history, or NULL */
   int32_t* hist_count;       /* [layers] */
   int32_t* hist_head;        /* [layers] */
+  /* The saved victim order (slot records sorted by eviction key as of the
+   * last planned layer), updated incrementally from one layer to the next.
+   * NULL = always sort every slot.  order_meta [1 + ceil(layers / 64)] int64:
+   * a valid flag, then a bitmask of the layers whose records changed since
+   * the order was saved; zero it whenever the state above is changed by
+   * anything but ferryb_plan_layer (a reset), which makes the next call sort
+   * every slot again.  order_rec: order_cap * 20 bytes, order_cap >= the
+   * power of two >= max(64, total_slots). */
+  int64_t* order_meta;
+  uint8_t* order_rec;
+  int32_t order_cap;
 } ferryb_planner;
 
 /* ids: [n_tokens, topk] uint8 gathered expert ids (rank-major when origins is

@@ -42,4 +42,4 @@ def test_struct_sizes_match_c_layout():
     assert ctypes.sizeof(_lib.LayerConfig) == 14 * 4
     assert ctypes.sizeof(_lib.LayerStats) == 10 * 8 + 8 + 5 * 8 + 6 * 8 + 3 * 8 + 8 + 8 + 8 + 8 + 9 * 8 + 9 * 8
     # 6 int32, 2 int64, 4 int32, 14 pointers
-    assert ctypes.sizeof(_lib.Planner) == 24 + 16 + 16 + 14 * 8
+    assert ctypes.sizeof(_lib.Planner) == 24 + 16 + 16 + 16 * 8 + 8  # + order_cap, padded
