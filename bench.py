@@ -208,6 +208,15 @@ def auto_pool_layers(spec, world, requested):
     return max(1, min(spec.layers, fit))
 
 
+def bench_config(spec, world, T, caps, policy):
+    """The workload both arms run (the driver compares their lines)."""
+    return {'workload': f'config 1 (Qwen3-30B-A3B MoE layer, decode batch {T}/GPU) in the '
+                        f'{spec.layers}-layer MoE stack, 30% global expert cache, all experts in '
+                        'pinned host memory',
+            'moe_layers': spec.layers, 'global_batch': world * T, 'tokens_per_gpu': T, 'seq_len': 1,
+            'parallelism': f'dp{world}-ep{world}', 'cache_slots_per_rank': caps, 'policy': policy}
+
+
 KERNELS = ['router', 'planner', 'layout', 'dispatch', 'permute', 'gemm_cached', 'gemm_fetched',
            'combine', 'final_scatter']
 
@@ -380,14 +389,9 @@ def run_ours(a, rank, world, local):
         'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': ms / a.steps,
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
         'data': 'synthetic: random-init N(0,0.02) weights, N(0,1) hidden states rho=0.5, Zipf(1.1) router bias',
-        'config': {'workload': 'config 1 (Qwen3-30B-A3B MoE layer, decode batch 64/GPU) in the 48-layer MoE stack, '
-                               '30% global expert cache, all experts in pinned host memory',
-                   'model': 'Qwen3-30B-A3B MoE layers', 'moe_layers': L, 'global_batch': world * T,
-                   'tokens_per_gpu': T, 'seq_len': 1, 'parallelism': f'dp{world}-ep{world}',
-                   'cache_slots_per_rank': caps, 'pool_layers': pool_layers,
-                   'pool': 'one shared pinned pool per node' if shared else 'pinned pool per rank',
-                   'policy': a.policy,
-                   'l2': 'no flush: each layer step reads > 126 MB of expert weights (> L2)'},
+        'config': dict(bench_config(spec, world, T, caps, a.policy), pool_layers=pool_layers,
+                   pool='one shared pinned pool per node' if shared else 'pinned pool per rank',
+                   l2='no flush: each layer step reads > 126 MB of expert weights (> L2)'),
         'roofline': roofline, 'layer_roofline': layer_roofline, 'layer_split_us': split,
         'gpu_launches': int(st.launches), 'h2d_expert_copies': int(fetch_copies),
         'host_wait_us_per_layer': round(st.host_wait_us / max(1, st.layers), 1),
@@ -490,7 +494,7 @@ def run_full_model(a, rank, world, local):
             'fetches_per_rank': m['fetches_per_rank'], 'decode_fetches_per_rank': m['decode_fetches_per_rank']}
 
 
-def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None):
+def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None, policy='ferry'):
     """Run the reference's CPU path (oracle port) over consecutive layers for
     about `seconds`; returns (layers_done, elapsed)."""
     from oracle import expert_ops as ops
@@ -499,7 +503,7 @@ def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None)
     masks = np.asarray([1 << r for r in range(world)], np.int64)
     sec = np.ones(world)
     lut = op.build_lut(spec.experts, world, masks, sec)
-    orc = OracleRuntime(spec, wl.pool, caps, 'ferry', masks, sec, lut)
+    orc = OracleRuntime(spec, wl.pool, caps, policy, masks, sec, lut)
     gates = [g.cpu() for g in wl.gate]
     biases = [b.cpu() for b in wl.bias]
     g = torch.Generator().manual_seed(11)
@@ -547,12 +551,12 @@ def run_reference(a, rank, world):
     wl.pool = (torch.randn(spec.experts, spec.expert_elements, generator=g) * 0.02).to(torch.bfloat16)
     layers_per_step = 4
     for _ in range(a.warmup):
-        cpu_layers(spec, wl, caps, T, world, 0.0, min_layers=1, max_layers=1)
+        cpu_layers(spec, wl, caps, T, world, 0.0, min_layers=1, max_layers=1, policy=a.policy)
     t0 = time.perf_counter()
     total_layers = 0
     for _ in range(a.steps):
         done, _ = cpu_layers(spec, wl, caps, T, world, 0.0, min_layers=layers_per_step,
-                             max_layers=layers_per_step)
+                             max_layers=layers_per_step, policy=a.policy)
         total_layers += done
     el = time.perf_counter() - t0
     per_layer = el / total_layers
@@ -562,11 +566,8 @@ def run_reference(a, rank, world):
             'warmup': a.warmup, 'ms_per_step': step_s * 1e3, 'higher_is_better': True,
             'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'impl': 'reference',
             'data': 'synthetic: random-init N(0,0.02) weights, N(0,1) hidden states, Zipf(1.1) router bias',
-            'config': {'workload': 'config 1 (Qwen3-30B-A3B MoE layer, decode batch 64/GPU) in the '
-                                   '48-layer MoE stack, 30% global expert cache',
-                       'model': 'Qwen3-30B-A3B MoE layers', 'moe_layers': spec.layers,
-                       'global_batch': world * T, 'tokens_per_gpu': T, 'seq_len': 1,
-                       'parallelism': f'dp{world}-ep{world} (emulated on the host)'},
+            'config': dict(bench_config(spec, world, T, caps, a.policy),
+                           execution=f'{world} rank(s) emulated in one host process'),
             'cpu_baseline': {'value': value, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
                              'sample': f'{layers_per_step} MoE layers per step x {a.steps} steps, '
                                        f'{world} rank(s) emulated in one process, scaled to '
