@@ -56,6 +56,11 @@ def parse():
     p.add_argument('--cache-ratio', type=float, default=0.3)
     p.add_argument('--pool-layers', type=int, default=0, help='0 = as many as host RAM allows')
     p.add_argument('--policy', default='ferry', choices=['ferry', 'random'])
+    # the reference's run_cell.py options of the policy
+    p.add_argument('--history-window', type=int, default=128)
+    p.add_argument('--eviction-score', default='frequency', choices=['frequency', 'probability'])
+    p.add_argument('--balance-tol-bps', type=int, default=200)
+    p.add_argument('--salt', type=int, default=1)
     p.add_argument('--copy-streams', type=int, default=1)
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--no-cpu-baseline', action='store_true')
@@ -208,6 +213,11 @@ def auto_pool_layers(spec, world, requested):
     return max(1, min(spec.layers, fit))
 
 
+def policy_opts(a):
+    return dict(window=a.history_window, balance_tol_bps=a.balance_tol_bps, salt=a.salt,
+                score=a.eviction_score)
+
+
 def bench_config(spec, world, T, caps, policy):
     """The workload both arms run (the driver compares their lines)."""
     return {'workload': f'config 1 (Qwen3-30B-A3B MoE layer, decode batch {T}/GPU) in the '
@@ -267,8 +277,9 @@ def run_ours(a, rank, world, local):
     wl = SyntheticMoE(spec, seed=0, device=dev, pool_layers=pool_layers, shared=shared)
     setup_s = time.time() - t0
     topo, topo_note = make_topology(a, spec, rank, world, wl.pool, dev)
-    rt = OffloadRuntime(spec, wl.pool, caps, a.policy, topo, n_copy_streams=a.copy_streams,
-                        timing=True, sync_fetch=a.sync_fetch)
+    rt = OffloadRuntime(spec, wl.pool, caps, a.policy, topo, history_window=a.history_window,
+                        balance_tol_bps=a.balance_tol_bps, salt=a.salt, eviction_score=a.eviction_score,
+                        n_copy_streams=a.copy_streams, timing=True, sync_fetch=a.sync_fetch)
     # this rank's link alone (ranks take turns), then with every rank copying at once
     b_alone = 0.0
     for r in range(world):
@@ -389,7 +400,7 @@ def run_ours(a, rank, world, local):
         'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': ms / a.steps,
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
         'data': 'synthetic: random-init N(0,0.02) weights, N(0,1) hidden states rho=0.5, Zipf(1.1) router bias',
-        'config': dict(bench_config(spec, world, T, caps, a.policy), pool_layers=pool_layers,
+        'config': dict(bench_config(spec, world, T, caps, a.policy), **policy_opts(a), pool_layers=pool_layers,
                    pool='one shared pinned pool per node' if shared else 'pinned pool per rank',
                    l2='no flush: each layer step reads > 126 MB of expert weights (> L2)'),
         'roofline': roofline, 'layer_roofline': layer_roofline, 'layer_split_us': split,
@@ -407,7 +418,7 @@ def run_ours(a, rank, world, local):
         'setup_s': round(setup_s, 1), 'e2e': e2e, 'clocks': clocks,
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        result['cpu_baseline'] = cpu_baseline(spec, wl, caps, T, a.cpu_seconds)
+        result['cpu_baseline'] = cpu_baseline(spec, wl, caps, T, a.cpu_seconds, a)
     rt.close()
     return result
 
@@ -494,7 +505,8 @@ def run_full_model(a, rank, world, local):
             'fetches_per_rank': m['fetches_per_rank'], 'decode_fetches_per_rank': m['decode_fetches_per_rank']}
 
 
-def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None, policy='ferry'):
+def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None, policy='ferry',
+               opts=None):
     """Run the reference's CPU path (oracle port) over consecutive layers for
     about `seconds`; returns (layers_done, elapsed)."""
     from oracle import expert_ops as ops
@@ -503,7 +515,9 @@ def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None,
     masks = np.asarray([1 << r for r in range(world)], np.int64)
     sec = np.ones(world)
     lut = op.build_lut(spec.experts, world, masks, sec)
-    orc = OracleRuntime(spec, wl.pool, caps, policy, masks, sec, lut)
+    o = dict(window=128, balance_tol_bps=200, salt=1, score='frequency')
+    o.update(opts or {})
+    orc = OracleRuntime(spec, wl.pool, caps, policy, masks, sec, lut, **o)
     gates = [g.cpu() for g in wl.gate]
     biases = [b.cpu() for b in wl.bias]
     g = torch.Generator().manual_seed(11)
@@ -516,17 +530,18 @@ def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None,
             x = torch.randn(T, spec.hidden, generator=g).to(torch.bfloat16)
             xs.append(x if prev[r] is None else (x.float() + prev[r].float()).to(torch.bfloat16))
         routed = [ops.route_qwen3(x, gates[layer], spec.topk, True, biases[layer]) for x in xs]
-        prev, _, _ = orc.execute(layer, xs, [r[0] for r in routed], [r[1] for r in routed])
+        probs = [r[2] for r in routed] if o['score'] == 'probability' else None
+        prev, _, _ = orc.execute(layer, xs, [r[0] for r in routed], [r[1] for r in routed], probs)
         done += 1
         el = time.perf_counter() - t0
         if (el >= seconds and done >= min_layers) or (max_layers and done >= max_layers):
             return done, el
 
 
-def cpu_baseline(spec, wl, caps, T, seconds):
+def cpu_baseline(spec, wl, caps, T, seconds, a):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    done, el = cpu_layers(spec, wl, caps, T, 1, seconds)
+    done, el = cpu_layers(spec, wl, caps, T, 1, seconds, policy=a.policy, opts=policy_opts(a))
     per_layer = el / done
     return {'value': T / (per_layer * spec.layers), 'unit': 'tokens/s', 'cores': threads,
             'kind': 'port',
@@ -551,12 +566,13 @@ def run_reference(a, rank, world):
     wl.pool = (torch.randn(spec.experts, spec.expert_elements, generator=g) * 0.02).to(torch.bfloat16)
     layers_per_step = 4
     for _ in range(a.warmup):
-        cpu_layers(spec, wl, caps, T, world, 0.0, min_layers=1, max_layers=1, policy=a.policy)
+        cpu_layers(spec, wl, caps, T, world, 0.0, min_layers=1, max_layers=1, policy=a.policy,
+                   opts=policy_opts(a))
     t0 = time.perf_counter()
     total_layers = 0
     for _ in range(a.steps):
         done, _ = cpu_layers(spec, wl, caps, T, world, 0.0, min_layers=layers_per_step,
-                             max_layers=layers_per_step, policy=a.policy)
+                             max_layers=layers_per_step, policy=a.policy, opts=policy_opts(a))
         total_layers += done
     el = time.perf_counter() - t0
     per_layer = el / total_layers
@@ -566,7 +582,7 @@ def run_reference(a, rank, world):
             'warmup': a.warmup, 'ms_per_step': step_s * 1e3, 'higher_is_better': True,
             'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'impl': 'reference',
             'data': 'synthetic: random-init N(0,0.02) weights, N(0,1) hidden states, Zipf(1.1) router bias',
-            'config': dict(bench_config(spec, world, T, caps, a.policy),
+            'config': dict(bench_config(spec, world, T, caps, a.policy), **policy_opts(a),
                            execution=f'{world} rank(s) emulated in one host process'),
             'cpu_baseline': {'value': value, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
                              'sample': f'{layers_per_step} MoE layers per step x {a.steps} steps, '

@@ -200,3 +200,28 @@ def test_execute_edge_shapes(E, K, T):
         assert_bf16_close(got.cpu(), want[0], f'E{E} K{K} T{T} step {step}')
         np.testing.assert_array_equal(rt.controller.slots, orc.ctl.slots)
     rt.close()
+
+
+def test_forward_probability_score():
+    """The router in the loop with the probability eviction score: kernel 1
+    writes each rank's router-probability tail into the history; the layer
+    output matches the oracle fed the kernel's own routing (outputs do not
+    depend on which experts were cached), and the cache stays consistent."""
+    layers, E, K, H, I, T, cap = 2, 32, 4, 256, 128, 16, 24
+    spec = _spec(layers, E, K, H, I)
+    rt, orc, gates, biases, g = _setup(spec, [cap], seed=21, score='probability')
+    for step in range(6):
+        layer = step % layers
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+        sel_out = torch.empty((T, K), dtype=torch.int64, device=DEV)
+        w_out = torch.empty((T, K), dtype=torch.bfloat16, device=DEV)
+        got = rt.forward(layer, x.to(DEV), gates[layer].to(DEV), biases[layer].to(DEV), sel_out, w_out)
+        torch.cuda.synchronize()
+        _, _, probs = ref_ops.route_qwen3(x, gates[layer], K, True, biases[layer])
+        want, _, _ = orc.execute(layer, [x], [sel_out.cpu()], [w_out.cpu()], [probs])
+        assert_bf16_close(got.cpu(), want[0], f'forward/probability step {step}')
+        slots = rt.controller.slots[0]
+        owner = rt.controller.owner
+        held = slots[slots >= 0]
+        assert len(set(held.tolist())) == held.size and (owner[held] == 0).all()
+    rt.close()
