@@ -23,7 +23,7 @@
 namespace ferryb {
 
 constexpr int kLayThreads = 1024;
-constexpr int kChunk = 1024;  // tokens per pass (one per thread)
+constexpr int kChunk = 1024;  // tokens per pass
 
 struct LaySmem {
   uint32_t mask[kMaxExpertsL][kChunk / 32];  // expert -> token bitmask of the chunk
@@ -39,8 +39,8 @@ struct LaySmem {
   int n_groups, n_hit, n_fetch_mine;
 };
 
-// Exclusive block scan of one int per thread (any multiple of 32 threads up
-// to 1024); returns the exclusive prefix and writes the total to *total.
+// Exclusive block scan of one int per thread (1024 threads); returns the
+// exclusive prefix and writes the total to *total.
 __device__ int block_scan(int v, int* warp_sum, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int x = v;
@@ -52,7 +52,7 @@ __device__ int block_scan(int v, int* warp_sum, int* total) {
   if (lane == 31) warp_sum[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    int w = lane < (int)(blockDim.x >> 5) ? warp_sum[lane] : 0;  // the block may have < 32 warps
+    int w = warp_sum[lane];
     int wx = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
     }
   }
   {
-    const int nf = a.n_fetches ? *a.n_fetches : 0;  // <= experts <= threads
+    const int nf = a.n_fetches ? *a.n_fetches : 0;  // <= experts <= 1024 threads
     int mine = 0, key = 0, slot = 0;
     if (tid < nf) {
       mine = a.fetches[tid * 3 + 0] == rank;
@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
   if (a.peer_row) {
     if (tid < R) sm.lower_cnt[tid] = 0;
     __syncthreads();
-    for (int g0 = 0; g0 < rank * T; g0 += (int)blockDim.x) {
+    for (int g0 = 0; g0 < rank * T; g0 += kChunk) {
       const int g = g0 + tid;
       unsigned peers = 0;  // bit p: token g sends to p
       if (g < rank * T) {
@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
   int sent = 0;
   for (int peer = 0; peer < R; ++peer) {
     int peer_sent = 0;
-    for (int t0 = 0; t0 < T; t0 += (int)blockDim.x) {
+    for (int t0 = 0; t0 < T; t0 += kChunk) {
       const int t = t0 + tid;
       const int g = rank * T + t;
       int size = 0;
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
 
   // ---- receive side pass 1: receive rows, per-expert counts --------------
   int received = 0;
-  for (int g0 = 0; g0 < n_tok; g0 += (int)blockDim.x) {
+  for (int g0 = 0; g0 < n_tok; g0 += kChunk) {
     const int g = g0 + tid;
     int size = 0;
     if (g < n_tok) {
@@ -252,8 +252,8 @@ __global__ void __launch_bounds__(kLayThreads, 1)
 
   // ---- receive side pass 2: CSR positions ---------------------------------
   int row_base = 0;
-  for (int g0 = 0; g0 < n_tok; g0 += (int)blockDim.x) {
-    for (int i = tid; i < E * (kChunk / 32); i += blockDim.x) (&sm.mask[0][0])[i] = 0;  // whole rows
+  for (int g0 = 0; g0 < n_tok; g0 += kChunk) {
+    for (int i = tid; i < E * (kChunk / 32); i += blockDim.x) (&sm.mask[0][0])[i] = 0;
     __syncthreads();
     const int g = g0 + tid;
     int size = 0;
@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
     __syncthreads();
     for (int e = tid; e < E; e += blockDim.x) {
       int tot = 0;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += __popc(sm.mask[e][w]);
+      for (int w = 0; w < kChunk / 32; ++w) tot += __popc(sm.mask[e][w]);
       sm.expert_count[e] += tot;
     }
     row_base += total_sh;

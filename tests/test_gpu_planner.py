@@ -180,3 +180,43 @@ def test_fused_layout_outputs(world, tokens, experts, topk):
         want_cp = np.full((n_recv, topk), -1)
         want_cp[rows, cols] = np.arange(total)
         np.testing.assert_array_equal(buf.csr_pos[:n_recv].cpu().numpy(), want_cp, err_msg=f'csr_pos rank {r}')
+
+
+@pytest.mark.parametrize('world,caps_per_rank,layers,experts,topk,tokens', [
+    (1, 300, 6, 64, 6, 48), (2, 90, 5, 64, 4, 40), (4, 40, 4, 128, 8, 24)])
+def test_saved_victim_order_matches_full_sort(world, caps_per_rank, layers, experts, topk, tokens):
+    """The incrementally maintained victim order against a controller that
+    sorts every slot at every plan (its saved order cleared before each call):
+    identical fetch lists, destinations and cache state over many layers,
+    with Zipf-skewed routing, the device GateHistory and layers revisited out
+    of order (including the same layer twice in a row)."""
+    from ferry_b200.policy import Controller, _Spec
+    from ferry_b200.quota import Topology
+    rng = np.random.default_rng(world * 100 + layers)
+    caps = [caps_per_rank] * world
+    topo = Topology.uniform(world, experts)
+    spec = _Spec(layers, experts, topk)
+    inc = Controller(spec, caps, 'ferry', topo)
+    full = Controller(spec, caps, 'ferry', topo)
+    p = 1.0 / np.arange(1, experts + 1) ** 1.1
+    p /= p.sum()
+    order = [l % layers for l in range(3 * layers)] + list(rng.integers(0, layers, 3 * layers))
+    order[5] = order[4]
+    n = world * tokens
+    for event, layer in enumerate(order):
+        perm = rng.permutation(experts)
+        sel = np.stack([perm[rng.choice(experts, topk, replace=False, p=p)] for _ in range(n)])
+        ids = torch.as_tensor(sel.astype(np.uint8), device='cuda')
+        full._order_meta.zero_()
+        outs = []
+        for ctl in (inc, full):
+            dest = torch.empty(ids.shape, dtype=torch.int32, device='cuda')
+            ctl.plan_device(event, layer, ids, dest, tokens_per_rank=tokens)
+            torch.cuda.synchronize()
+            assert int(ctl._err.item()) == 0
+            m = int(ctl._n_fetches.item())
+            outs.append((ctl._fetches[:m].cpu().numpy(), dest.cpu().numpy()))
+        np.testing.assert_array_equal(outs[0][0], outs[1][0], err_msg=f'event {event} fetches')
+        np.testing.assert_array_equal(outs[0][1], outs[1][1], err_msg=f'event {event} dest')
+        np.testing.assert_array_equal(inc.slots, full.slots, err_msg=f'event {event} slots')
+    assert int(inc._order_meta[0].item()) == 1
