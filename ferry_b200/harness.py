@@ -127,7 +127,7 @@ def generate(model, input_ids, new_tokens):
 
 def decode_metrics(times_ms, batch, world):
     """TTFT, TPOT and decode tokens/s, max over ranks."""
-    t = torch.tensor(times_ms, dtype=torch.float64, device='cuda')
+    t = torch.tensor(times_ms, dtype=torch.float64, device='cuda' if world > 1 else 'cpu')
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t = t.cpu().tolist()

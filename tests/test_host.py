@@ -108,3 +108,43 @@ def test_quota_lut_builder_and_topology_file(tmp_path):
         Topology(path, 8, spec.experts)
     with pytest.raises(ValueError):
         select_domains(dict(prof, domains=prof['domains'][:4]), '0,1:2,3')
+
+
+def test_decode_metrics_run_cell_semantics():
+    """TTFT = first token, TPOT = (last - first) / (n - 1), decode tokens/s =
+    R * B * (n - 1) / (last - first) (scripts/run_cell.py:147-158)."""
+    from ferry_b200.harness import decode_metrics
+    m = decode_metrics([100.0, 110.0, 120.0, 130.0], batch=64, world=1)
+    assert m['ttft_ms'] == 100.0 and m['tpot_ms'] == 10.0
+    assert abs(m['decode_tokens_per_s'] - 64 * 3 / 0.030) < 1e-6
+    assert abs(m['total_tokens_per_s'] - 64 * 4 / 0.130) < 1e-6
+    assert decode_metrics([50.0], batch=8, world=1)['decode_tokens_per_s'] is None
+
+
+def test_bench_helpers():
+    """The bench's workload description and pool sizing."""
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+    spec = bench.qwen3_spec(48)
+    cfg = bench.bench_config(spec, 2, 64, [922, 921], 'ferry')
+    assert cfg['global_batch'] == 128 and cfg['parallelism'] == 'dp2-ep2' and 'model' not in cfg
+    assert bench.auto_pool_layers(spec, 8, 5) == 5
+    assert 1 <= bench.auto_pool_layers(spec, 1, 0) <= 48
+
+
+def test_clock_sampler_parses_reasons():
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+    cs = bench.ClockSampler()
+    cs.proc = type('P', (), {'terminate': lambda self: None, 'wait': lambda self, timeout=None: 0})()
+    cs.thread = type('T', (), {'join': lambda self, timeout=None: None})()
+    cs.rows = [['0', '1965', '1965', '700', '0x0', 'Not Active', 'Not Active', 'Not Active', 'Not Active'],
+               ['0', '1700', '1965', '990', '0x4', 'Not Active', 'Not Active', 'Not Active', 'Active'],
+               ['1', '900', '1965', '100', '0x0', 'Active', 'Not Active', 'Not Active', 'Not Active']]
+    out = cs.stop([0])
+    assert out['sm_max_mhz'] == 1965.0 and out['samples'] == 2
+    assert out['reasons'] == ['sw_power_cap']
