@@ -2,8 +2,8 @@
 
 TEST INFRASTRUCTURE ONLY.  This package restates the reference algorithms on
 the CPU so that the CUDA kernels of ``ferry_b200`` can be checked against them.
-Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
-``bench.py`` may import it; the product path never does, and fails loudly when
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU legs of ``bench.py``
+(``cpu_baseline`` and ``--impl reference``) may import it; the product path never does, and fails loudly when
 its CUDA library is missing instead of falling back here.
 
 Contents
@@ -15,7 +15,9 @@ Contents
                unpack_dispatch, execute_experts, reduce_partials,
                scatter_returned) and of the MoE-hook routers.
   layer        one MoE layer over R emulated ranks, end to end on the CPU
-               (the CPU baseline timed by bench.py).
+               (the CPU baseline and the --impl reference arm of bench.py).
+  dist_layer   the same layer across gloo processes with real collectives.
+  build_ref    builds the reference's own expert_ops extension into _ref/.
 
 Parity pin: tests/golden/ holds vectors produced by running the reference's
 own numba/numpy code (tests/golden/make_golden.py); the integer algorithms are
