@@ -176,3 +176,57 @@ def test_shared_pinned_pool_world3():
     for r in range(3):
         assert torch.equal(res[r]['first'], want)
         assert float(res[r]['after'][5, 39]) == 7.0
+
+
+def _transport_worker(rank, world, port, out_dir):
+    """ferry_b200.transport.Transport over gloo with the oracle's CPU ops
+    standing in for the kernels: with identity experts, dispatch then combine
+    returns each token times its number of routes."""
+    import torch.distributed as dist
+    from ferry_b200.transport import Transport
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    T, H, K, E = 12, 64, 4, 16
+    g = torch.Generator().manual_seed(77)
+    sels, xs = [], []
+    for r in range(world):
+        sels.append(torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]))
+        xs.append((torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16))
+    ids = torch.cat(sels).numpy()
+    owner = np.arange(E) % world
+    dest = owner[ids]
+    send_idx, send_ids, send_counts, recv_counts, starts, rows, cols = op.build_layout(ids, dest, T, rank, E)
+    groups = [(int(e), torch.from_numpy(rows[starts[e]:starts[e + 1]]), torch.from_numpy(cols[starts[e]:starts[e + 1]]), 0)
+              for e in np.flatnonzero(starts[1:] > starts[:-1])]
+    layout = dict(send_idx=torch.from_numpy(send_idx), send_ids=torch.from_numpy(send_ids),
+                  send_counts=send_counts.tolist(), recv_counts=recv_counts.tolist(), groups=groups)
+    class _CpuOps:  # the oracle's ops under the reference's signatures (expert_ops.cpp:144-157)
+        pack_dispatch = staticmethod(ops.pack_dispatch)
+        unpack_dispatch = staticmethod(ops.unpack_dispatch)
+        scatter_returned = staticmethod(ops.scatter_returned)
+
+        @staticmethod
+        def reduce_partials(parts, rows, received, hidden, like):
+            return ops.reduce_partials(parts, rows, received, hidden)
+    tr = Transport(_CpuOps, K, E)
+    w = torch.ones(T, K).to(torch.bfloat16)
+    xr, wr = tr.dispatch(xs[rank], sels[rank], w, layout)
+    parts = [xr.index_select(0, grp[1]) for grp in groups]  # identity experts
+    out = tr.combine(xs[rank], parts, layout)
+    torch.save({'out': out, 'x': xs[rank], 'db': tr.dispatch_bytes, 'cb': tr.combine_bytes,
+                'send': send_counts, 'recv': recv_counts}, os.path.join(out_dir, f't{rank}.pt'))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_transport_compat_world2_gloo():
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_transport_worker, args=(2, 29655, tmp), nprocs=2)
+        res = [torch.load(os.path.join(tmp, f't{r}.pt'), weights_only=False) for r in range(2)]
+    K, H = 4, 64
+    for r, d in enumerate(res):
+        assert_bf16_close(d['out'], (d['x'].float() * K).to(torch.bfloat16), f'rank {r}')
+        send, recv = d['send'], d['recv']
+        assert d['db'] == (int(send.sum()) - int(send[r])) * (2 * H + 3 * K)
+        assert d['cb'] == (int(recv.sum()) - int(recv[r])) * H * 2
