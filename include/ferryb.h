@@ -383,6 +383,10 @@ typedef struct ferryb_layer_config {
                                 weights per MoE layer via ferryb_layer_set_shared */
 } ferryb_layer_config;
 
+/* Counters of the executor.  `fetches` and host_wait_us take the place of
+ * OffloadRuntime.fetches_per_rank (this rank's entry) and serial_wait_ns
+ * (ferry/runtime.py:60-62, updated at :70 and :79-81); the per-rank and
+ * decode-only splits come from ferryb_layer_last_summary's counts. */
 typedef struct ferryb_layer_stats {
   int64_t layers, fetches, routes, recv_rows, dispatch_bytes, combine_bytes;
   int64_t launches;          /* kernels launched by the executor */
