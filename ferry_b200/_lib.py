@@ -191,6 +191,21 @@ def require_cuda(*tensors):
             raise FerrybError('expected CUDA tensors (this path has no CPU fallback)')
 
 
+def check_tensor(t, name, shape, dtype=None, contiguous=False):
+    """Raise FerrybError unless `t` has `shape` (None entries match any size),
+    `dtype` and, if asked, a contiguous layout.  The C ABI receives bare
+    pointers, so every buffer size it relies on is checked here first."""
+    if t is None:
+        raise FerrybError(f'{name} is required')
+    if t.dim() != len(shape) or any(s is not None and t.shape[i] != s for i, s in enumerate(shape)):
+        want = ', '.join('*' if s is None else str(s) for s in shape)
+        raise FerrybError(f'{name} must have shape [{want}], got {list(t.shape)}')
+    if dtype is not None and t.dtype != dtype:
+        raise FerrybError(f'{name} must be {dtype}, got {t.dtype}')
+    if contiguous and not t.is_contiguous():
+        raise FerrybError(f'{name} must be contiguous')
+
+
 def host_i64(values):
     arr = (ctypes.c_int64 * max(1, len(values)))(*[int(v) for v in values])
     return arr

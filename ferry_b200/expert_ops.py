@@ -56,7 +56,11 @@ def pack_dispatch(hidden, selected, weights, send_idx, send_ids, experts):
     """ferry/csrc/expert_ops.cpp:50-66 -> uint8 [n, 2H + 3k] packets."""
     require_cuda(hidden, selected, weights, send_idx, send_ids)
     _check(hidden.dtype == BF16 and weights.dtype == BF16, 'hidden and weights must be bf16')
+    _check(hidden.dim() == 2 and selected.dim() == 2 and send_idx.dim() == 1 and send_ids.dim() == 2,
+           'hidden, selected and send_ids must be 2-D, send_idx 1-D')
     n, h, k = send_idx.shape[0], hidden.shape[1], send_ids.shape[1]
+    _check(selected.shape == (hidden.shape[0], k) and weights.shape == selected.shape
+           and send_ids.shape[0] == n, 'selected/weights must be [tokens, k], send_ids [n, k]')
     payload = torch.empty((n, 2 * h + 3 * k), dtype=torch.uint8, device=hidden.device)
     if n:
         hid = hidden.contiguous()
@@ -64,7 +68,6 @@ def pack_dispatch(hidden, selected, weights, send_idx, send_ids, experts):
         w = weights.contiguous()
         si, sids = send_idx.contiguous().long(), send_ids.contiguous().long()
         err = torch.zeros(1, dtype=torch.int32, device=hidden.device)
-        _check(sel.shape[1] == k, 'selected and send_ids must have the same top-k width')
         call('ferryb_pack_dispatch', ptr(hid), hid.shape[0], h, ptr(sel), ptr(w), k, ptr(si),
              ptr(sids), n, experts, ptr(payload), ptr(err), stream_ptr(hidden.device))
         _lib.check_device_error(err, 'pack_dispatch')
@@ -74,6 +77,8 @@ def pack_dispatch(hidden, selected, weights, send_idx, send_ids, experts):
 def unpack_dispatch(raw, hidden, topk):
     """ferry/csrc/expert_ops.cpp:68-73 -> (x [m, H] bf16, w [m, k] bf16)."""
     require_cuda(raw)
+    _check(raw.dtype == torch.uint8 and raw.dim() == 2 and raw.shape[1] == 2 * hidden + 3 * topk,
+           f'raw must be uint8 [m, 2*hidden + 3*topk = {2 * hidden + 3 * topk}]')
     m = raw.shape[0]
     x = torch.empty((m, hidden), dtype=BF16, device=raw.device)
     w = torch.empty((m, topk), dtype=BF16, device=raw.device)
@@ -83,24 +88,18 @@ def unpack_dispatch(raw, hidden, topk):
     return x, w
 
 
-def _segment_sum(src, keys, n_keys, hidden, name):
-    out = torch.empty((n_keys, hidden), dtype=BF16, device=src.device)
-    n = src.shape[0]
-    ws_bytes = _lib.lib().ferryb_segment_sum_workspace(n, n_keys)
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=src.device)
-    s, k = src.contiguous(), keys.contiguous().long()
-    call(name, ptr(s), ptr(k), n, n_keys, hidden, ptr(out), ptr(ws), ws_bytes, stream_ptr(src.device))
-    return out
-
-
 def reduce_partials(parts, rows, received, hidden, like):
     """ferry/csrc/expert_ops.cpp:76-83: float32 sum of the groups' outputs per
     receive row (in group order), returned as bf16 [received, hidden]."""
-    require_cuda(like)
+    require_cuda(like, *parts)
+    _check(len(parts) == len(rows), 'parts and rows must have equal length')
+    for p, r in zip(parts, rows):
+        _check(p.dim() == 2 and p.shape[1] == hidden and p.shape[0] == r.numel(),
+               'each part must be [len(rows[i]), hidden]')
     if not parts:
         return torch.zeros((received, hidden), dtype=BF16, device=like.device)
     src = torch.cat([p.to(BF16) for p in parts])
-    keys = torch.cat([r.reshape(-1) for r in rows])
+    keys = torch.cat([r.reshape(-1) for r in rows]).to(like.device)
     if src.shape[0] == 0:
         return torch.zeros((received, hidden), dtype=BF16, device=like.device)
     out = torch.empty((received, hidden), dtype=BF16, device=like.device)
@@ -115,6 +114,8 @@ def scatter_returned(returned, send_idx, tokens):
     """ferry/csrc/expert_ops.cpp:86-92: float32 sum of returned partials per
     token (in packet order), bf16 [tokens, hidden]."""
     require_cuda(returned, send_idx)
+    _check(returned.dim() == 2 and send_idx.numel() == returned.shape[0],
+           'returned must be [n, hidden] with one send_idx per row')
     hidden = returned.shape[1]
     if returned.shape[0] == 0:
         return torch.zeros((tokens, hidden), dtype=returned.dtype, device=returned.device)

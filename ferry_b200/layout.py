@@ -67,11 +67,21 @@ def _device():
     return torch.device('cuda', torch.cuda.current_device())
 
 
+def _check_shapes(sel_shape, dest_shape, n_local):
+    """selected and destinations: the same [world * n_local, k] shape (the
+    kernel reads both through bare pointers)."""
+    if (len(sel_shape) != 2 or tuple(dest_shape) != tuple(sel_shape) or n_local <= 0
+            or sel_shape[0] % n_local):
+        raise _lib.FerrybError(f'selected {list(sel_shape)} and destinations {list(dest_shape)} must '
+                               f'be equal [world * {n_local}, k] arrays')
+
+
 def build_layout(selected, destinations, n_local, rank, experts):
     """ferry/layout.py:12-75 -> (send_idx, send_ids, send_counts, recv_counts,
     starts, rows, cols) as int64 numpy arrays."""
     dev = _device()
     sel = np.asarray(selected)
+    _check_shapes(sel.shape, np.shape(destinations), n_local)
     world = sel.shape[0] // n_local
     topk = sel.shape[1]
     ids = torch.as_tensor(sel.astype(np.uint8), device=dev)
@@ -94,6 +104,7 @@ def device_layout(selected, destinations, tokens_per_rank, rank, experts, slot_o
         if not torch.is_tensor(selected) else selected.to(dev, torch.uint8)
     dst = torch.as_tensor(np.asarray(destinations).astype(np.int32), device=dev) \
         if not torch.is_tensor(destinations) else destinations.to(dev, torch.int32)
+    _check_shapes(tuple(sel.shape), tuple(dst.shape), tokens_per_rank)
     world = sel.shape[0] // tokens_per_rank
     topk = sel.shape[1]
     buf = LayoutBuffers(world, tokens_per_rank, topk, experts, rank, dev, fused=False)

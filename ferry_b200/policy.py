@@ -32,10 +32,18 @@ def _t(a, dtype, dev):
     return torch.as_tensor(np.ascontiguousarray(a), device=dev).to(dtype)
 
 
+def _require(cond, msg):
+    """The kernels get bare pointers: every array length they rely on is
+    checked here (the reference's numba code would read out of bounds)."""
+    if not cond:
+        raise _lib.FerrybError(msg)
+
+
 def _demand(selected, origins, experts, world):
     """ferry/policy.py:25-33."""
     dev = _dev()
     sel, org = _t(selected, torch.int64, dev), _t(origins, torch.int64, dev)
+    _require(sel.dim() == 2 and org.shape == (sel.shape[0],), 'origins must have one entry per token')
     d = torch.zeros((experts, world), dtype=torch.int64, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     call('ferryb_demand', ptr(sel), ptr(org), sel.shape[0], sel.shape[1], experts, world, ptr(d),
@@ -50,6 +58,9 @@ def _admission_capacity(slots, capacities, layer, active, experts):
     sl = _t(slots, torch.int32, dev)
     caps = _t(capacities, torch.int32, dev)
     act = _t(np.asarray(active, np.uint8), torch.uint8, dev)
+    _require(sl.dim() == 2 and sl.shape[0] == len(capacities) and max(capacities) <= sl.shape[1],
+             'slots must be [world, maxcap] with maxcap >= every capacity')
+    _require(act.numel() >= experts, 'active must have one entry per expert')
     u = torch.zeros(len(capacities), dtype=torch.int64, device=dev)
     call('ferryb_admission_capacity', ptr(sl), sl.shape[1], ptr(caps), len(capacities), layer,
          ptr(act), experts, ptr(u), stream_ptr(dev))
@@ -62,6 +73,9 @@ def load_balanced_assignment(demand, misses, owner, layer, quota, balance_tol_bp
     demand = np.asarray(demand, np.int64)
     experts, world = demand.shape
     m = len(misses)
+    _require(len(quota) == world and np.asarray(owner).size >= (layer + 1) * experts,
+             'quota must be [world] and owner cover the layer')
+    _require(m == 0 or (0 <= np.min(misses) and np.max(misses) < experts), 'miss out of range')
     ans = torch.zeros(max(m, 1), dtype=torch.int64, device=dev)
     # keep every argument tensor referenced until the kernel has run
     d_t = _t(demand, torch.int64, dev)
@@ -77,6 +91,12 @@ def _choose_slot(rank, layer, active, slots, capacities, last, scores, experts):
     """ferry/policy.py:109-127 -> slot index or -1."""
     dev = _dev()
     slots = np.asarray(slots)
+    keys = np.asarray(scores).size
+    _require(slots.ndim == 2 and slots.shape[0] == len(capacities) and 0 <= rank < len(capacities)
+             and capacities[rank] <= slots.shape[1], 'slots must be [world, maxcap], rank < world')
+    _require(np.asarray(last).size == keys and np.asarray(active).size >= experts
+             and np.max(slots[rank, :capacities[rank]], initial=-1) < keys,
+             'last and scores must cover every cached key, active every expert')
     res = torch.zeros(1, dtype=torch.int64, device=dev)
     a_t = _t(np.asarray(active, np.uint8), torch.uint8, dev)
     s_t = _t(slots, torch.int32, dev)
@@ -92,6 +112,7 @@ def layer_slots(slots_row, capacity, layer, experts):
     """ferry/policy.py:197-205."""
     dev = _dev()
     row = _t(slots_row, torch.int32, dev)
+    _require(row.dim() == 1 and row.numel() >= capacity, 'slots_row must hold capacity entries')
     out = torch.empty(experts, dtype=torch.int32, device=dev)
     call('ferryb_layer_slots', ptr(row), int(capacity), int(layer), int(experts), ptr(out),
          stream_ptr(dev))
@@ -218,6 +239,9 @@ class Controller:
         """ferry/policy.py:225-228 -> (fetches [m, 3], destinations, counts), numpy int64."""
         dev = self.device
         sel = np.asarray(selected)
+        _require(sel.ndim == 2 and sel.shape[1] == self.topk and np.asarray(origins).shape == (sel.shape[0],)
+                 and np.asarray(gate_scores).size == self.spec.experts,
+                 'selected must be [n, topk], origins [n], gate_scores [experts]')
         ids = torch.as_tensor(sel.astype(np.uint8), device=dev)
         org = torch.as_tensor(np.asarray(origins, np.int64), device=dev)
         gs = torch.as_tensor(np.asarray(gate_scores, np.float32), device=dev)

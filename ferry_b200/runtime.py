@@ -21,7 +21,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from ._lib import call, ptr, stream_ptr
+from ._lib import call, check_tensor, ptr, stream_ptr
 from .expert_ops import H2DEngine
 from .policy import Controller
 from .symm import SymmetricBuffer
@@ -101,7 +101,9 @@ class OffloadRuntime:
         self.pool = pool
         self.group = group
         self.rank, self.world = _rank_world(group)
-        self.device = torch.device('cuda', torch.cuda.current_device()) if device is None else torch.device(device)
+        self.device = torch.device(device if device is not None else 'cuda')
+        if self.device.index is None:
+            self.device = torch.device('cuda', torch.cuda.current_device())
         self.capacities = list(capacities)
         self.cap = self.capacities[self.rank]
         self.window = history_window
@@ -142,16 +144,30 @@ class OffloadRuntime:
         self.decode_fetches_per_rank = np.zeros(self.world, np.int64)
         self.serial_wait_ns = 0
 
+    def _check_inputs(self, tensors):
+        """Shapes, dtypes and device of the tensors handed to the executor as
+        bare pointers (the reference's TORCH_CHECKs, ferry/csrc/expert_ops.cpp:20-25)."""
+        for name, t, shape, dtype in tensors:
+            if t is None:
+                continue
+            check_tensor(t, name, shape, dtype)
+            if t.device != self.device:
+                raise _lib.FerrybError(f'{name} is on {t.device}, the runtime on {self.device}')
+
     def execute(self, layer, hidden, selected, weights, probs_tail):
         """ferry/runtime.py:64-89: routing given by the MoE hook."""
-        tokens = hidden.shape[0]
+        tokens, k = hidden.shape[0], self.spec.topk
+        score = self.eviction_score == 'probability'
+        self._check_inputs([('hidden', hidden, (tokens, self.spec.hidden), torch.bfloat16),
+                            ('selected', selected, (tokens, k), None),
+                            ('weights', weights, (tokens, k), None),
+                            ('probs_tail', probs_tail if score else None, (None, self.spec.experts), None)])
         ex = self._executor(tokens)
         out = torch.empty_like(hidden)
         h = hidden.contiguous()
         sel = selected.contiguous().long()
         w = weights.contiguous().to(torch.bfloat16)
-        pt = probs_tail.float().contiguous() if (probs_tail is not None and
-                                                 self.eviction_score == 'probability') else None
+        pt = probs_tail.float().contiguous() if (probs_tail is not None and score) else None
         before = ex.stats().host_wait_us
         call('ferryb_layer_execute', ex.h, self.event, int(layer), ptr(h), ptr(sel), ptr(w), ptr(pt),
              0 if pt is None else pt.shape[0], ptr(out), stream_ptr(self.device))
@@ -160,7 +176,17 @@ class OffloadRuntime:
 
     def forward(self, layer, hidden, gate_weight, gate_bias=None, selected_out=None, weights_out=None):
         """execute() with the MoE hook's router fused into kernel 1."""
-        tokens = hidden.shape[0]
+        tokens, k, spec = hidden.shape[0], self.spec.topk, self.spec
+        self._check_inputs([('hidden', hidden, (tokens, spec.hidden), torch.bfloat16),
+                            ('gate_weight', gate_weight, (spec.experts, spec.hidden), torch.bfloat16),
+                            ('gate_bias', gate_bias, (spec.experts,), torch.float32),
+                            ('selected_out', selected_out, (tokens, k), torch.int64),
+                            ('weights_out', weights_out, (tokens, k), torch.bfloat16)])
+        for name, t in (('gate_weight', gate_weight), ('gate_bias', gate_bias),
+                        ('selected_out', selected_out), ('weights_out', weights_out)):
+            if t is not None and not t.is_contiguous():
+                raise _lib.FerrybError(f'{name} must be contiguous')
+        hidden = hidden.contiguous()
         ex = self._executor(tokens)
         out = torch.empty_like(hidden)
         before = ex.stats().host_wait_us
