@@ -558,9 +558,7 @@ def run_reference(a, rank, world):
     caps = spec.cache_slots(a.cache_ratio, world)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-
-    class _Pool:  # the CPU path reads weights straight from a host pool
-        pass
+    # the CPU path reads the expert weights straight from a host pool
     wl = SyntheticMoE(spec, seed=0, device='cpu', pool_layers=1, build_pool=False)
     g = torch.Generator().manual_seed(1)
     wl.pool = (torch.randn(spec.experts, spec.expert_elements, generator=g) * 0.02).to(torch.bfloat16)

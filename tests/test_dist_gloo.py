@@ -13,7 +13,6 @@ import os
 import tempfile
 
 import numpy as np
-import pytest
 import torch
 import torch.multiprocessing as mp
 

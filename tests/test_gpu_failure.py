@@ -6,7 +6,6 @@ sequence flag no rank sets, and a peer rank that never joins the layer."""
 import ctypes
 import time
 
-import numpy as np
 import pytest
 import torch
 

@@ -10,7 +10,6 @@ workspace-based ferryb_execute_experts within the BF16 tolerance; it also
 checks that an oversized call is refused with a clear error.  The file is named
 to be collected last.
 """
-import ctypes
 
 import pytest
 import torch

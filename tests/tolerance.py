@@ -1,7 +1,6 @@
 """The BF16 tolerance of the north star, written once for every test:
 max abs error <= 2e-2 and max abs error <= 1e-2 * max |reference| on the
 compared hidden states."""
-import torch
 
 ABS_TOL = 2e-2
 REL_TOL = 1e-2
