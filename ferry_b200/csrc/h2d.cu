@@ -78,22 +78,20 @@ extern "C" int ferryb_h2d_create(void* cache, int64_t cache_slots, int64_t row_b
   h->pool = static_cast<const uint8_t*>(pool);
   h->pool_rows = pool_rows;
   h->streams.resize(n_streams);
-  for (auto& s : h->streams) {
-    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) {
-      delete h;
-      return fail(FERRYB_ECUDA, "h2d_create: cudaStreamCreate failed");
-    }
-  }
-  if (cudaStreamCreateWithFlags(&h->flag_stream, cudaStreamNonBlocking) != cudaSuccess) {
-    delete h;
+  h->copy_done.assign(cache_slots, nullptr);
+  h->used.assign(cache_slots, nullptr);
+  h->used_valid.assign(cache_slots, 0);
+  bool ok = cudaStreamCreateWithFlags(&h->flag_stream, cudaStreamNonBlocking) == cudaSuccess;
+  for (auto& s : h->streams)
+    ok = ok && cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess;
+  if (!ok) {
+    ferryb_h2d_destroy(h);  // releases what was created
     return fail(FERRYB_ECUDA, "h2d_create: cudaStreamCreate failed");
   }
-  h->copy_done.resize(cache_slots);
-  h->used.resize(cache_slots);
-  h->used_valid.assign(cache_slots, 0);
   for (int64_t i = 0; i < cache_slots; ++i) {
     if (cudaEventCreateWithFlags(&h->copy_done[i], cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&h->used[i], cudaEventDisableTiming) != cudaSuccess) {
+      ferryb_h2d_destroy(h);
       return fail(FERRYB_ECUDA, "h2d_create: cudaEventCreate failed");
     }
   }
@@ -166,6 +164,7 @@ extern "C" int ferryb_h2d_destroy(ferryb_h2d* h) {
   if (!h) return FERRYB_OK;
   DeviceGuard g(h->device);
   for (auto s : h->streams) {
+    if (!s) continue;
     cudaStreamSynchronize(s);
     cudaStreamDestroy(s);
   }
@@ -173,8 +172,10 @@ extern "C" int ferryb_h2d_destroy(ferryb_h2d* h) {
     cudaStreamSynchronize(h->flag_stream);
     cudaStreamDestroy(h->flag_stream);
   }
-  for (auto e : h->copy_done) cudaEventDestroy(e);
-  for (auto e : h->used) cudaEventDestroy(e);
+  for (auto e : h->copy_done)
+    if (e) cudaEventDestroy(e);
+  for (auto e : h->used)
+    if (e) cudaEventDestroy(e);
   delete h;
   return FERRYB_OK;
 }

@@ -219,6 +219,11 @@ extern "C" int64_t ferryb_layer_symm_bytes(const ferryb_layer_config* cfg, int32
   return (int64_t)layout_of(*cfg, window).half * 2;
 }
 
+static int init_layer(ferryb_layer* L, const ferryb_layer_config* cfg,
+                      const ferryb_planner* planner, void* cache, int64_t cache_slots,
+                      ferryb_h2d* h2d, void* symm_local, const uint64_t* peer_bases,
+                      void* workspace, int64_t workspace_size);
+
 extern "C" int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_planner* planner,
                                    void* cache, int64_t cache_slots, ferryb_h2d* h2d,
                                    void* symm_local, const uint64_t* peer_bases, void* workspace,
@@ -243,6 +248,20 @@ extern "C" int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_
                  "which the per-copy readiness flags need");
   }
   auto* L = new ferryb_layer();
+  s = init_layer(L, cfg, planner, cache, cache_slots, h2d, symm_local, peer_bases, workspace,
+                 workspace_size);
+  if (s) {
+    ferryb_layer_destroy(L);  // frees whatever init_layer got to
+    return s;
+  }
+  *out = L;
+  return FERRYB_OK;
+}
+
+static int init_layer(ferryb_layer* L, const ferryb_layer_config* cfg,
+                      const ferryb_planner* planner, void* cache, int64_t cache_slots,
+                      ferryb_h2d* h2d, void* symm_local, const uint64_t* peer_bases,
+                      void* workspace, int64_t workspace_size) {
   L->cfg = *cfg;
   L->planner = *planner;
   L->cache = cache;
@@ -286,11 +305,8 @@ extern "C" int ferryb_layer_create(const ferryb_layer_config* cfg, const ferryb_
   FB_CUDA(cudaHostAlloc(&L->errs_host, 8 * sizeof(int32_t), cudaHostAllocDefault));
   FB_CUDA(cudaEventCreateWithFlags(&L->summary_ev, cudaEventDisableTiming));
   const int64_t routes = (int64_t)cfg->world * cfg->tokens_per_rank * cfg->topk;
-  s = make_gemm_maps(&L->maps, cache, cache_slots, L->x_sorted, L->act, routes, cfg->hidden,
-                     cfg->intermediate);
-  if (s) { delete L; return s; }
-  *out = L;
-  return FERRYB_OK;
+  return make_gemm_maps(&L->maps, cache, cache_slots, L->x_sorted, L->act, routes, cfg->hidden,
+                        cfg->intermediate);
 }
 
 static FusedArgs fused_args(ferryb_layer* L, int parity, const __nv_bfloat16* hidden,
