@@ -185,3 +185,36 @@ def test_errors_carry_library_message():
     cfg = _lib.LayerConfig()  # all zero: rejected by the size query
     assert lib.ferryb_layer_workspace_bytes(cfg) < 0
     assert lib.ferryb_last_error()
+
+
+def test_golden_inputs_pass_the_checks(calls):
+    """Every argument set the GPU parity tests take from the reference's
+    goldens gets through the checks to the library call."""
+    from oracle import planner as op
+    from tests.goldens import PLAN_CASES, PlanCase, load
+    d = load('assignment')
+    for i in range(int(d['n'])):
+        policy.load_balanced_assignment(d[f'c{i}_demand'], d[f'c{i}_misses'], d[f'c{i}_owner'],
+                                        int(d[f'c{i}_layer']), d[f'c{i}_quota'], int(d[f'c{i}_bps']))
+    d = load('choose_slot')
+    for i in range(int(d['n'])):
+        policy._choose_slot(int(d[f'c{i}_rank']), int(d[f'c{i}_layer']), d[f'c{i}_active'],
+                            d[f'c{i}_slots'], d[f'c{i}_caps'], d[f'c{i}_last'], d[f'c{i}_scores'],
+                            int(d[f'c{i}_experts']))
+    assert calls.count('ferryb_choose_slot') == int(d['n'])
+    from ferry_b200.quota import Topology
+    for name in PLAN_CASES:
+        c = PlanCase(name)
+        ctl = policy.Controller(policy._Spec(c.layers, c.experts, c.topk), c.caps, c.policy,
+                                Topology.from_arrays(c.masks, c.seconds, c.lut), c.bps, c.salt,
+                                window=c.window)
+        s = c.step(0)
+        ctl.plan(s['event'], s['layer'], s['selected'], c.origins(), s['scores'])
+        policy._demand(s['selected'], c.origins(), c.experts, c.world)
+        active = op.demand(s['selected'], c.origins(), c.experts, c.world).sum(1) > 0
+        slots = np.full((c.world, int(max(c.caps))), -1, np.int64)
+        policy._admission_capacity(slots, c.caps, s['layer'], active, c.experts)
+        for r in range(c.world):
+            policy.layer_slots(slots[r], c.caps[r], s['layer'], c.experts)
+            layout._check_shapes(s['selected'].shape, s['selected'].shape, c.tokens)
+    assert calls.count('ferryb_plan_layer') == len(PLAN_CASES)
