@@ -6,7 +6,7 @@ Run in a container where the FERRY reference is mounted (read-only):
 
 It imports the reference's own ferry.policy, ferry.quota, ferry.layout and
 ferry.metadata (numba/numpy, CPU), drives them on seeded synthetic inputs at
-the BASELINE config shapes and on edge cases, and writes compressed .npz
+the benchmark configurations' shapes and on edge cases, and writes compressed .npz
 fixtures.  The fixtures travel with the repository; nothing at test time reads
 the reference.  Routing ids are drawn as Zipf(1.1)-skewed top-k (Gumbel top-k
 over log-popularity of a seeded expert permutation), the same distribution as
@@ -116,7 +116,7 @@ def topology_random(quota_mod, world, experts, rng, subsets=True):
     return topo
 
 
-def quota_cases(quota_mod, rng):
+def quota_cases(quota_mod, rng, write=True):
     rec = {}
     n = 0
     for world in (1, 2, 3, 4, 8):
@@ -156,11 +156,12 @@ def quota_cases(quota_mod, rng):
             rec[f'lut{world}_{kind}_seconds'] = seconds
             rec[f'lut{world}_{kind}'] = quota_mod.build_lut(64, world, masks, seconds)
     rec['n'] = np.int64(n)
-    np.savez_compressed(OUT / 'quota.npz', **rec)
+    if write:
+        np.savez_compressed(OUT / 'quota.npz', **rec)
     print('quota cases', n)
 
 
-def assignment_cases(policy_mod, rng):
+def assignment_cases(policy_mod, rng, write=True):
     rec = {}
     n = 0
     for world in (1, 2, 4, 8):
@@ -187,11 +188,12 @@ def assignment_cases(policy_mod, rng):
                     rec[f'c{n}_{k}'] = v
                 n += 1
     rec['n'] = np.int64(n)
-    np.savez_compressed(OUT / 'assignment.npz', **rec)
+    if write:
+        np.savez_compressed(OUT / 'assignment.npz', **rec)
     print('assignment cases', n)
 
 
-def choose_slot_cases(policy_mod, rng):
+def choose_slot_cases(policy_mod, rng, write=True):
     rec = {}
     n = 0
     for trial in range(60):
@@ -219,11 +221,12 @@ def choose_slot_cases(policy_mod, rng):
             rec[f'c{n}_{k}'] = v
         n += 1
     rec['n'] = np.int64(n)
-    np.savez_compressed(OUT / 'choose_slot.npz', **rec)
+    if write:
+        np.savez_compressed(OUT / 'choose_slot.npz', **rec)
     print('choose_slot cases', n)
 
 
-def history_cases(metadata_mod, rng):
+def history_cases(metadata_mod, rng, write=True):
     rec = {}
     layers, experts, window = 2, 16, 8
     h = metadata_mod.GateHistory(layers, experts, window)
@@ -243,7 +246,8 @@ def history_cases(metadata_mod, rng):
         n += 1
     rec['n'] = np.int64(n)
     rec['layers'], rec['experts'], rec['window'] = np.int64(layers), np.int64(experts), np.int64(window)
-    np.savez_compressed(OUT / 'history.npz', **rec)
+    if write:
+        np.savez_compressed(OUT / 'history.npz', **rec)
     print('history cases', n)
 
 
@@ -335,58 +339,94 @@ def main(a):
     import ferry.quota as quota
     ref = dict(policy=policy, quota=quota, layout=layout, metadata=metadata)
     rng = np.random.default_rng(2024)
+    only = set(a.only.split(',')) if a.only else None
 
-    mt_cases()
-    quota_cases(quota, rng)
-    assignment_cases(policy, rng)
-    choose_slot_cases(policy, rng)
-    history_cases(metadata, rng)
-    route_gather_cases(a.reference)
+    if only is None:
+        mt_cases()
+        quota_cases(quota, rng)
+        assignment_cases(policy, rng)
+        choose_slot_cases(policy, rng)
+        history_cases(metadata, rng)
+        route_gather_cases(a.reference)
+    else:  # the random topologies below draw from rng after the cases above
+        quota_cases(quota, rng, write=False)
+        assignment_cases(policy, rng, write=False)
+        choose_slot_cases(policy, rng, write=False)
+        history_cases(metadata, rng, write=False)
+
+    def plan_sequence_sel(ref_, name, **kw):
+        if only is None or name in only:
+            plan_sequence(ref_, name, **kw)
 
     U = quota.Topology.uniform
     # config 0: DeepSeek-V2-Lite layer, 4 ranks x 16 tokens, top-6 of 64, 8 steps
-    plan_sequence(ref, 'cfg0_caps19', layers=1, experts=64, topk=6, world=4, tokens=16,
+    plan_sequence_sel(ref, 'cfg0_caps19', layers=1, experts=64, topk=6, world=4, tokens=16,
                   caps=[19] * 4, policy='ferry', topology=U(4, 64), steps=8)
-    plan_sequence(ref, 'cfg0_caps5554', layers=1, experts=64, topk=6, world=4, tokens=16,
+    plan_sequence_sel(ref, 'cfg0_caps5554', layers=1, experts=64, topk=6, world=4, tokens=16,
                   caps=[5, 5, 5, 4], policy='ferry', topology=U(4, 64), steps=8)
     # config 0 inside a 26-layer DeepSeek-V2-Lite stack (global 30% budget, 499 slots)
-    plan_sequence(ref, 'cfg0_stack', layers=26, experts=64, topk=6, world=4, tokens=16,
+    plan_sequence_sel(ref, 'cfg0_stack', layers=26, experts=64, topk=6, world=4, tokens=16,
                   caps=[125, 125, 125, 124], policy='ferry', topology=U(4, 64), steps=52, state_every=4)
     # config 1: Qwen3 layer at one GPU, 64 tokens, top-8 of 128; 30% of a 4-layer stack
-    plan_sequence(ref, 'cfg1_l4', layers=4, experts=128, topk=8, world=1, tokens=64,
+    plan_sequence_sel(ref, 'cfg1_l4', layers=4, experts=128, topk=8, world=1, tokens=64,
                   caps=[153], policy='ferry', topology=U(1, 128), steps=24)
     # multi-rank Qwen3 shapes, tight caches so eviction and the greedy fallback run
-    plan_sequence(ref, 'qwen_r4', layers=3, experts=128, topk=8, world=4, tokens=64,
+    plan_sequence_sel(ref, 'qwen_r4', layers=3, experts=128, topk=8, world=4, tokens=64,
                   caps=[40, 40, 35, 30], policy='ferry', topology=U(4, 128), steps=18)
-    plan_sequence(ref, 'qwen_r4_strict', layers=3, experts=128, topk=8, world=4, tokens=64,
+    plan_sequence_sel(ref, 'qwen_r4_strict', layers=3, experts=128, topk=8, world=4, tokens=64,
                   caps=[40, 40, 35, 30], policy='ferry', topology=U(4, 128), steps=12, bps=0)
-    plan_sequence(ref, 'qwen_r8', layers=2, experts=128, topk=8, world=8, tokens=64,
+    plan_sequence_sel(ref, 'qwen_r8', layers=2, experts=128, topk=8, world=8, tokens=64,
                   caps=[20] * 8, policy='ferry', topology=U(8, 128), steps=12)
-    plan_sequence(ref, 'qwen_r4_topo', layers=3, experts=128, topk=8, world=4, tokens=64,
+    plan_sequence_sel(ref, 'qwen_r4_topo', layers=3, experts=128, topk=8, world=4, tokens=64,
                   caps=[48, 30, 30, 24], policy='ferry', topology=topology_random(quota, 4, 128, rng),
                   steps=18)
-    plan_sequence(ref, 'qwen_r8_topo', layers=2, experts=128, topk=8, world=8, tokens=16,
+    plan_sequence_sel(ref, 'qwen_r8_topo', layers=2, experts=128, topk=8, world=8, tokens=16,
                   caps=[20, 20, 20, 20, 18, 18, 18, 18], policy='ferry',
                   topology=topology_random(quota, 8, 128, rng, subsets=False), steps=10)
-    plan_sequence(ref, 'random_r4', layers=3, experts=128, topk=8, world=4, tokens=64,
+    plan_sequence_sel(ref, 'random_r4', layers=3, experts=128, topk=8, world=4, tokens=64,
                   caps=[40, 40, 35, 30], policy='random', topology=U(4, 128), steps=18, salt=1)
-    plan_sequence(ref, 'random_r3_bigseed', layers=2, experts=64, topk=6, world=3, tokens=16,
+    plan_sequence_sel(ref, 'random_r3_bigseed', layers=2, experts=64, topk=6, world=3, tokens=16,
                   caps=[30, 25, 25], policy='random', topology=U(3, 64), steps=10, salt=7919,
                   event0=5000)
-    plan_sequence(ref, 'r2_t1', layers=2, experts=16, topk=2, world=2, tokens=1,
+    plan_sequence_sel(ref, 'r2_t1', layers=2, experts=16, topk=2, world=2, tokens=1,
                   caps=[3, 2], policy='ferry', topology=U(2, 16), steps=20)
-    plan_sequence(ref, 'r1_small', layers=3, experts=8, topk=2, world=1, tokens=2,
+    plan_sequence_sel(ref, 'r1_small', layers=3, experts=8, topk=2, world=1, tokens=2,
                   caps=[5], policy='ferry', topology=U(1, 8), steps=20)
-    plan_sequence(ref, 'overflow', layers=1, experts=64, topk=6, world=2, tokens=16,
+    plan_sequence_sel(ref, 'overflow', layers=1, experts=64, topk=6, world=2, tokens=16,
                   caps=[4, 4], policy='ferry', topology=U(2, 64), steps=2)
-    plan_sequence(ref, 'prob_r2', layers=2, experts=64, topk=6, world=2, tokens=16,
+    plan_sequence_sel(ref, 'prob_r2', layers=2, experts=64, topk=6, world=2, tokens=16,
                   caps=[34, 30], policy='ferry', topology=U(2, 64), steps=12, score='probability')
     # the bench workload: config 1's layer inside Qwen3's 48-layer MoE stack, 30% cache
-    plan_sequence(ref, 'cfg1_stack48', layers=48, experts=128, topk=8, world=1, tokens=64,
+    plan_sequence_sel(ref, 'cfg1_stack48', layers=48, experts=128, topk=8, world=1, tokens=64,
                   caps=[1843], policy='ferry', topology=U(1, 128), steps=56, state_every=8)
+    # the 8-GPU bench workload: the 48-layer stack's 30% cache over 8 ranks, a
+    # profiled-style LUT over all 255 rank subsets; layers 0-7 revisited after
+    # the cache has filled
+    plan_sequence_sel(ref, 'cfg4_stack48_r8', layers=48, experts=128, topk=8, world=8, tokens=64,
+                      caps=[231, 231, 231, 230, 230, 230, 230, 230], policy='ferry',
+                      topology=topology_random(quota, 8, 128, rng), steps=24, state_every=8,
+                      layer_order=list(range(16)) + list(range(8)))
+    # DeepSeek-V2-Lite's 26-layer stack over 8 ranks (30% cache: 499 slots)
+    plan_sequence_sel(ref, 'dsv2_stack26_r8', layers=26, experts=64, topk=6, world=8, tokens=16,
+                      caps=[63, 63, 63, 62, 62, 62, 62, 62], policy='ferry', topology=U(8, 64),
+                      steps=30, state_every=6, layer_order=list(range(20)) + list(range(10)))
+    # history windows other than 128: probability rows replacing the ring
+    # every update (4 x 16 rows = W), frequency rows appending and wrapping
+    plan_sequence_sel(ref, 'prob_qwen_r4_w64', layers=3, experts=128, topk=8, world=4, tokens=64,
+                      caps=[40, 40, 35, 30], policy='ferry', topology=U(4, 128), steps=12,
+                      window=64, score='probability')
+    plan_sequence_sel(ref, 'qwen_r2_w256', layers=2, experts=128, topk=8, world=2, tokens=64,
+                      caps=[80, 70], policy='ferry', topology=U(2, 128), steps=12, window=256)
+    # the largest expert count the uint8 ids carry, with top-16
+    plan_sequence_sel(ref, 'e256_k16_r2', layers=2, experts=256, topk=16, world=2, tokens=8,
+                      caps=[100, 100], policy='ferry', topology=U(2, 256), steps=12)
+    # prefill-sized layers (every expert active), several layout chunks per rank
+    plan_sequence_sel(ref, 'prefill_r2_t1024', layers=2, experts=128, topk=8, world=2, tokens=1024,
+                      caps=[100, 90], policy='ferry', topology=U(2, 128), steps=4)
 
 
 if __name__ == '__main__':
     p = argparse.ArgumentParser()
     p.add_argument('--reference', default='/root/reference')
+    p.add_argument('--only', default='', help='comma-separated plan_<name> cases to (re)generate')
     main(p.parse_args())
