@@ -423,6 +423,18 @@ def main(a):
     # prefill-sized layers (every expert active), several layout chunks per rank
     plan_sequence_sel(ref, 'prefill_r2_t1024', layers=2, experts=128, topk=8, world=2, tokens=1024,
                       caps=[100, 90], policy='ferry', topology=U(2, 128), steps=4)
+    # six ranks over a 63-subset LUT, a wide balance tolerance, RANDOM at eight
+    # ranks and RANDOM with the probability score
+    plan_sequence_sel(ref, 'qwen_r6_topo', layers=3, experts=128, topk=8, world=6, tokens=32,
+                      caps=[30, 30, 28, 28, 26, 26], policy='ferry',
+                      topology=topology_random(quota, 6, 128, rng), steps=12)
+    plan_sequence_sel(ref, 'qwen_r4_bps1000', layers=3, experts=128, topk=8, world=4, tokens=64,
+                      caps=[40, 40, 35, 30], policy='ferry', topology=U(4, 128), steps=12, bps=1000)
+    plan_sequence_sel(ref, 'random_r8', layers=2, experts=128, topk=8, world=8, tokens=16,
+                      caps=[20] * 8, policy='random', topology=U(8, 128), steps=10, salt=3)
+    plan_sequence_sel(ref, 'random_prob_r4', layers=2, experts=64, topk=6, world=4, tokens=16,
+                      caps=[20, 20, 18, 18], policy='random', topology=U(4, 64), steps=10,
+                      score='probability')
 
 
 if __name__ == '__main__':
