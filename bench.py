@@ -233,26 +233,8 @@ KERNELS = ['router', 'planner', 'layout', 'dispatch', 'permute', 'gemm_cached', 
 
 def make_topology(a, spec, rank, world, pool, dev):
     """(Topology, note): the quota LUT of this run (see --topology)."""
-    from ferry_b200.quota import Topology
-    if world == 1 or a.topology == 'uniform':
-        return Topology.uniform(world, spec.experts), 'uniform'
-    if a.topology != 'auto':
-        return Topology(a.topology, world, spec.experts), a.topology
-    from ferry_b200.build_quota_lut import build
-    from ferry_b200.profile_h2d import profile_ranks
-    target = torch.empty(spec.expert_elements, dtype=torch.bfloat16, device=dev)
-    t0 = time.time()
-    domains = profile_ranks(rank, world, target, pool[0], copies=16, repeats=2)
-    profile = dict(world=world, physical_gpus=list(range(world)), expert_bytes=spec.expert_bytes,
-                   domains=domains)
-    box = [build(profile, spec)['quota_lut'] if rank == 0 else None]
-    dist.broadcast_object_list(box, src=0)
-    masks = sorted((d['mask'] for d in domains), key=lambda m: (bin(m).count('1'), m))
-    by_mask = {d['mask']: d for d in domains}
-    topo = Topology.from_arrays(masks, [1.0 / by_mask[m]['gib_per_s'] for m in masks], box[0])
-    singles = [round(by_mask[1 << r]['gib_per_s'], 1) for r in range(world)]
-    return topo, (f'auto: profiled {len(domains)} rank subsets in {time.time() - t0:.1f} s; '
-                  f'single-GPU GiB/s {singles}, all-GPU {round(by_mask[(1 << world) - 1]["gib_per_s"], 1)}')
+    from ferry_b200.build_quota_lut import topology_for_run
+    return topology_for_run(a.topology, spec, rank, world, pool_row=pool[0], device=dev)
 
 
 def qwen3_spec(layers):
@@ -498,7 +480,7 @@ def run_full_model(a, rank, world, local):
             'config': {'workload': f'config {"3/4" if a.full_model == "qwen3" else "2"}: full {name}',
                        'batch_per_gpu': a.batch, 'prompt_len': a.prompt_len, 'new_tokens': a.new_tokens,
                        'cache_ratio': a.cache_ratio, 'layers': layers or cfg['num_hidden_layers'],
-                       'policy': a.policy, 'topology': a.topology or 'uniform',
+                       'policy': a.policy, 'topology': m['topology'],
                        'parallelism': f'dp{world}-ep{world}'},
             'ttft_ms': round(m['ttft_ms'], 1), 'tpot_ms': round(m['tpot_ms'], 2),
             'total_tokens_per_s': m['total_tokens_per_s'],

@@ -42,6 +42,40 @@ def build(profile, spec, groups=None, lut_fn=None):
                 model_type=spec.model_type, domains=domains, quota_lut=[list(map(int, r)) for r in lut])
 
 
+def topology_for_run(topology, spec, rank, world, pool_row=None, device=None, group=None):
+    """(Topology, note) of a run.  topology: None or 'uniform' (equal
+    singleton links), a topology JSON path, or 'auto': with several ranks,
+    every subset of ranks copies `pool_row` (one pinned expert row) into HBM
+    at once (profile_h2d.profile_ranks), rank 0 builds the table and
+    broadcasts it; one rank needs no profile (the even table is exact)."""
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from .profile_h2d import profile_ranks
+    from .quota import Topology
+    if topology in (None, '', 'uniform') or (topology == 'auto' and world == 1):
+        return Topology.uniform(world, spec.experts), 'uniform'
+    if topology != 'auto':
+        return Topology(topology, world, spec.experts), str(topology)
+    if pool_row is None:
+        raise ValueError("topology 'auto' needs a pinned expert row to copy")
+    target = torch.empty(pool_row.numel(), dtype=pool_row.dtype, device=device)
+    t0 = time.time()
+    domains = profile_ranks(rank, world, target, pool_row, copies=16, repeats=2, group=group)
+    profile = dict(world=world, physical_gpus=list(range(world)), expert_bytes=spec.expert_bytes,
+                   domains=domains)
+    box = [build(profile, spec)['quota_lut'] if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0, group=group)
+    masks = sorted((d['mask'] for d in domains), key=lambda m: (bin(m).count('1'), m))
+    by_mask = {d['mask']: d for d in domains}
+    topo = Topology.from_arrays(masks, [1.0 / by_mask[m]['gib_per_s'] for m in masks], box[0])
+    singles = [round(by_mask[1 << r]['gib_per_s'], 1) for r in range(world)]
+    return topo, (f'auto: profiled {len(domains)} rank subsets in {time.time() - t0:.1f} s; '
+                  f'single-GPU GiB/s {singles}, all-GPU {round(by_mask[(1 << world) - 1]["gib_per_s"], 1)}')
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.split('\n\n')[0])
     p.add_argument('--profile', required=True)

@@ -140,8 +140,10 @@ def decode_metrics(times_ms, batch, world):
 
 def run(cfg_dict, *, batch, prompt_len, new_tokens, cache_ratio=0.3, seed=0, layers=None, warmup=1,
         rank=0, world=1, device=None, timing=False, policy='ferry', topology=None):
-    """Build, hook and run one generation (after `warmup` untimed ones)."""
-    from .quota import Topology
+    """Build, hook and run one generation (after `warmup` untimed ones).
+    topology: None/'uniform', 'auto' (profile the ranks' host links now) or a
+    topology JSON path (ferry_b200.build_quota_lut.topology_for_run)."""
+    from .build_quota_lut import topology_for_run
     from .runtime import OffloadRuntime
     from .workload import SyntheticMoE
     device = device or torch.device('cuda', torch.cuda.current_device())
@@ -149,7 +151,7 @@ def run(cfg_dict, *, batch, prompt_len, new_tokens, cache_ratio=0.3, seed=0, lay
     model, spec = build_model(cfg_dict, device, seed, **overrides)
     wl = SyntheticMoE(spec, seed=seed + 1, device=device, shared=world > 1)
     caps = spec.cache_slots(cache_ratio, world)
-    topo = Topology(topology, world, spec.experts) if topology else Topology.uniform(world, spec.experts)
+    topo, topo_note = topology_for_run(topology, spec, rank, world, pool_row=wl.pool[0], device=device)
     rt = OffloadRuntime(spec, wl.pool, caps, policy, topo,
                         norm_topk_prob=bool(cfg_dict.get('norm_topk_prob', True)),
                         routed_scaling_factor=float(cfg_dict.get('routed_scaling_factor', 1.0)),
@@ -169,5 +171,5 @@ def run(cfg_dict, *, batch, prompt_len, new_tokens, cache_ratio=0.3, seed=0, lay
     wall = time.perf_counter() - t0
     m = decode_metrics(times, batch, world)
     m.update(fetches_per_rank=rt.fetches_per_rank.tolist(),
-             decode_fetches_per_rank=rt.decode_fetches_per_rank.tolist(), wall_s=wall)
+             decode_fetches_per_rank=rt.decode_fetches_per_rank.tolist(), wall_s=wall, topology=topo_note)
     return model, rt, tokens, m

@@ -229,3 +229,48 @@ def test_transport_compat_world2_gloo():
         send, recv = d['send'], d['recv']
         assert d['db'] == (int(send.sum()) - int(send[r])) * (2 * H + 3 * K)
         assert d['cb'] == (int(recv.sum()) - int(recv[r])) * H * 2
+
+
+def _topology_worker(rank, world, port, out_dir):
+    """topology_for_run('auto') over gloo ranks with the GPU copy profile
+    replaced by a stand-in that reports fixed per-subset bandwidths."""
+    import json
+    import torch.distributed as dist
+    from ferry_b200 import profile_h2d, quota
+    from ferry_b200.build_quota_lut import topology_for_run
+    from ferry_b200.model import QWEN3_30B_A3B, spec_from_config
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    quota.build_lut = lambda *a: op.build_lut(*a)
+
+    def fake_profile(rank_, world_, target, source, copies=16, repeats=2, group=None):
+        import itertools
+        doms = []
+        for n in range(1, world_ + 1):
+            for s in itertools.combinations(range(world_), n):
+                per = [50.0 / (1 + 0.5 * (len(s) - 1))] * len(s)  # links shared as more ranks copy
+                doms.append(dict(gpus=list(s), mask=sum(1 << g for g in s), gib_per_s=sum(per),
+                                 per_gpu_gib_per_s=per))
+        return doms
+    profile_h2d.profile_ranks = fake_profile
+    spec = spec_from_config(QWEN3_30B_A3B)
+    topo, note = topology_for_run('auto', spec, rank, world, pool_row=torch.zeros(16, dtype=torch.bfloat16))
+    with open(os.path.join(out_dir, f'{rank}.json'), 'w') as f:
+        json.dump(dict(masks=topo.masks.tolist(), lut=topo.lut.tolist(), note=note), f)
+    dist.destroy_process_group()
+
+
+def test_auto_topology_world3_gloo():
+    """Every rank gets rank 0's table, over all 7 rank subsets, and it is the
+    oracle's build_lut of that profile."""
+    import json
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_topology_worker, args=(3, 29656, tmp), nprocs=3)
+        res = [json.load(open(os.path.join(tmp, f'{r}.json'))) for r in range(3)]
+    assert res[0] == res[1] == res[2]
+    masks = res[0]['masks']
+    assert masks == [1, 2, 4, 3, 5, 6, 7] and res[0]['note'].startswith('auto: profiled 7 rank subsets')
+    gib = [50.0 / (1 + 0.5 * (bin(m).count('1') - 1)) * bin(m).count('1') for m in masks]
+    want = op.build_lut(128, 3, np.asarray(masks, np.int64), np.asarray([1.0 / g for g in gib]))
+    assert np.array_equal(np.asarray(res[0]['lut']), want)

@@ -148,3 +148,27 @@ def test_clock_sampler_parses_reasons():
     out = cs.stop([0])
     assert out['sm_max_mhz'] == 1965.0 and out['samples'] == 2
     assert out['reasons'] == ['sw_power_cap']
+
+
+def test_topology_for_run(tmp_path, monkeypatch):
+    """--topology resolution shared by bench.py and the full-model harness:
+    'uniform'/None and 'auto' at one rank give the even table, a path is read
+    with the reference's checks, 'auto' at several ranks needs a pinned row."""
+    import json
+    from ferry_b200 import quota
+    from ferry_b200.build_quota_lut import build, topology_for_run
+    from ferry_b200.model import QWEN3_30B_A3B, spec_from_config
+    from oracle import planner as op
+    spec = spec_from_config(QWEN3_30B_A3B)
+    monkeypatch.setattr(quota, 'build_lut', lambda *a: op.build_lut(*a))  # no GPU here
+    for arg, world in ((None, 1), ('uniform', 4), ('auto', 1)):
+        topo, note = topology_for_run(arg, spec, 0, world)
+        assert note == 'uniform' and list(topo.masks) == [1 << r for r in range(world)]
+    path = tmp_path / 'topo.json'
+    path.write_text(json.dumps(build(_profile(4), spec, lut_fn=lambda *a: op.build_lut(*a))))
+    topo, note = topology_for_run(str(path), spec, 0, 4)
+    assert note == str(path) and len(topo.masks) == 15
+    with pytest.raises(ValueError):
+        topology_for_run(str(path), spec, 0, 2)
+    with pytest.raises(ValueError):
+        topology_for_run('auto', spec, 0, 4)
