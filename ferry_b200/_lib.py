@@ -118,6 +118,8 @@ SIGNATURES = {
                                    _vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_vp)]),
     'ferryb_layer_forward': (_i32, [_vp, _i64, _i32c, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     'ferryb_layer_execute': (_i32, [_vp, _i64, _i32c, _vp, _vp, _vp, _vp, _i32c, _vp, _vp]),
+    'ferryb_layer_status': (_i32, [_vp, _vp]),
+    'ferryb_layer_set_fault_hooks': (_i32, [_vp, ctypes.c_uint32, ctypes.c_uint64]),
     'ferryb_layer_get_stats': (_i32, [_vp, ctypes.POINTER(LayerStats)]),
     'ferryb_layer_reset_stats': (_i32, [_vp]),
     'ferryb_layer_set_shared': (_i32, [_vp, _i32c, _vp]),
@@ -132,6 +134,12 @@ _lib = None
 
 class FerrybError(RuntimeError):
     pass
+
+
+# ferryb_layer_set_fault_hooks bits (include/ferryb.h)
+HOOK_NO_READY_FLAGS = 1
+HOOK_NO_DISPATCH_SIGNAL = 2
+HOOK_NO_COMBINE_SIGNAL = 4
 
 
 def lib():

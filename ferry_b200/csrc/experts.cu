@@ -318,8 +318,10 @@ struct FusedParams {
   __nv_bfloat16* act;
   __nv_bfloat16* out;
   const __nv_bfloat16* route_w;
-  const uint32_t* ready;  // [fetched] readiness flags, fetch order
+  const uint32_t* ready;  // [fetched] readiness flags, fetch order; null: the stream
+                          // already waited for the copies
   uint32_t ready_value;
+  uint64_t ready_wait_ns;  // bound on one readiness wait
   int* queue;  // [1] claim counter, zero at launch
   int* done;   // [1] CTAs finished; the last one zeroes queue/dep/done for the next launch
   int* dep;    // [n_groups] phase-1 epilogue-warp completions, zero at launch
@@ -362,14 +364,16 @@ __device__ __forceinline__ int ld_acquire_s32_gpu(const int* p) {
   return v;
 }
 
-// Bounded spin until *flag >= value (readiness) / *cnt >= target (deps).
-__device__ bool spin_ready(const uint32_t* flag, uint32_t value, volatile int* abort_flag, int* err) {
+// Bounded spin until *flag >= value (readiness, at most limit_ns) / *cnt >=
+// target (deps).
+__device__ bool spin_ready(const uint32_t* flag, uint32_t value, uint64_t limit_ns,
+                           volatile int* abort_flag, int* err) {
   if (ld_acquire_u32(flag) >= value) return true;
   const uint64_t t0 = global_ns();
   while (ld_acquire_u32(flag) < value) {
     __nanosleep(128);
     if (*abort_flag) return false;
-    if (global_ns() - t0 > kWaitNs) { *abort_flag = 1; atomicCAS(err, 0, DEV_WAIT_TIMEOUT); return false; }
+    if (global_ns() - t0 > limit_ns) { *abort_flag = 1; atomicCAS(err, 0, DEV_WAIT_TIMEOUT); return false; }
   }
   return true;
 }
@@ -449,7 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const FusedItem it = decode_item(p, item);
         const GemmGroup g = p.groups[it.group];
         // dependencies: copy readiness, then (phase 2) the group's phase-1 tiles
-        if (it.fetched >= 0 && !spin_ready(p.ready + it.fetched, p.ready_value, abort_flag, p.err)) {
+        if (it.fetched >= 0 && p.ready &&
+            !spin_ready(p.ready + it.fetched, p.ready_value, p.ready_wait_ns, abort_flag, p.err)) {
           ok = false; break;
         }
         if (it.phase == 2 && !spin_count(p.dep + it.group, 4 * p.mt1, abort_flag, p.err)) {
@@ -629,11 +634,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups, int n_hit,
                         const uint32_t* ready, uint32_t ready_value, int* queue_dep,
                         const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
-                        int* err, cudaStream_t stream, unsigned long long* ts) {
+                        int* err, cudaStream_t stream, unsigned long long* ts,
+                        uint64_t ready_wait_ns) {
   if (n_groups == 0) return FERRYB_OK;
   int device = 0;
   FB_CUDA(cudaGetDevice(&device));
   FusedParams p{};
+  p.ready_wait_ns = ready_wait_ns ? ready_wait_ns : kWaitNs;
   p.ts = ts;
   p.groups = groups;
   p.n_groups = n_groups;

@@ -86,6 +86,13 @@ struct ferryb_layer {
   cudaEvent_t* tev = nullptr;
   GemmMaps maps{};
   ferryb_layer_stats stats{};
+  // error attribution: the last layer enqueued, and the last event whose GEMM
+  // and transport error words were read back clean
+  int64_t last_event = -1, clean_event = -1;
+  int32_t last_layer = -1;
+  // failure injection (ferryb_layer_set_fault_hooks)
+  uint32_t hooks = 0;
+  uint64_t hook_wait_ns = 0;
 };
 
 namespace {
@@ -336,7 +343,33 @@ static FusedArgs fused_args(ferryb_layer* L, int parity, const __nv_bfloat16* hi
   a.expert_out = L->expert_out;
   a.out = out;
   a.err = L->errs + 3;
+  a.poison = L->errs + 2;
+  a.wait_ns = L->hook_wait_ns;
+  a.skip_signals = (int)((L->hooks >> 1) & 3u);
   return a;
+}
+
+// GEMM / transport error words ([2], [3]) as read back in `e`, for every layer
+// enqueued up to L->last_event: FERRYB_OK, or FERRYB_ETIMEOUT / FERRYB_EDEVICE
+// naming the layer whose kernels set them.  The words are sticky, so once a
+// layer has failed every later call reports it until the runtime is reset.
+static int exec_errors(ferryb_layer* L, const int32_t* e) {
+  const int w = e[2] ? e[2] : e[3];
+  if (!w) {
+    L->clean_event = L->last_event;
+    return FERRYB_OK;
+  }
+  const char* what =
+      e[2] ? (w == DEV_WAIT_TIMEOUT ? "the expert GEMM gave up waiting for a fetched expert's copy"
+                                    : "the expert GEMM reported a device error")
+           : (w == DEV_WAIT_TIMEOUT ? "dispatch/combine gave up waiting for a peer rank's flags"
+                                    : "dispatch/combine reported a device error");
+  const int code = w == DEV_WAIT_TIMEOUT ? FERRYB_ETIMEOUT : FERRYB_EDEVICE;
+  if (L->last_event == L->clean_event + 1)
+    return fail(code, "MoE layer %d (event %lld): %s (device code %d); its output rows are NaN",
+                L->last_layer, (long long)L->last_event, what, w);
+  return fail(code, "a MoE layer between events %lld and %lld: %s (device code %d); its output "
+              "rows are NaN", (long long)(L->clean_event + 1), (long long)L->last_event, what, w);
 }
 
 static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const void* hidden,
@@ -465,12 +498,11 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     h_prev = now;
   }
   const ferryb_layout_summary sum = *L->summary_host;
-  // error words: [0] planner, [1] layout, [2] GEMM, [3] transport (earlier layers)
+  // error words: [0] planner, [1] layout (this layer), [2] GEMM, [3] transport
+  // (the layers enqueued before this one)
+  if ((s = exec_errors(L, L->errs_host))) return s;
   const int plan_err = L->errs_host[0];
-  if (sum.err || plan_err || L->errs_host[2] || L->errs_host[3]) {
-    if (L->errs_host[2] || L->errs_host[3])
-      return fail(FERRYB_EDEVICE, "device error in an earlier layer (GEMM %d, transport %d)",
-                  L->errs_host[2], L->errs_host[3]);
+  if (sum.err || plan_err) {
     if (plan_err == DEV_CAPACITY || sum.err == DEV_CAPACITY)
       return fail(FERRYB_ECAPACITY, "missing experts exceed the total admission capacity");
     if (plan_err == DEV_WAIT_TIMEOUT)
@@ -485,10 +517,16 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     fkeys[i] = sum.fetch_keys[i];
   }
   const uint32_t ready_value = (uint32_t)seq;
+  // failure injection: copies that never raise their readiness flags
+  const bool no_flags = (L->hooks & FERRYB_HOOK_NO_READY_FLAGS) != 0;
+  auto fetch = [&](int first, int n) {
+    if (no_flags) return ferryb_h2d_fetch(L->h2d, fslots.data() + first, fkeys.data() + first, n);
+    return ferryb_h2d_fetch_flagged(L->h2d, fslots.data() + first, fkeys.data() + first, n,
+                                    L->ready + first, ready_value);
+  };
   if (sum.n_fetch_mine > 0) {
     if (timing && (s = h2d_record_event(L->h2d, L->tev[6], 0))) return s;
-    if ((s = ferryb_h2d_fetch_flagged(L->h2d, fslots.data(), fkeys.data(), 1, L->ready, ready_value)))
-      return s;
+    if ((s = fetch(0, 1))) return s;
   }
   host_mark(1);
 
@@ -512,7 +550,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   //   start as their readiness flags arrive
   if ((s = swiglu_fused_launch(L->maps, L->groups, sum.n_hit, sum.n_hit, nullptr, 0, L->queue_dep,
                                L->route_w, L->act, L->expert_out, L->errs + 2, stream,
-                               span_of(5))))
+                               span_of(5), L->hook_wait_ns)))
     return s;
   if (sum.n_hit) launches += 1;
   if (shared) {  // dense shared expert on every local token, in the copies' shadow
@@ -528,25 +566,19 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   if (c.sync_fetch) {
     // profiler-safe order: every copy is issued (and its flag raised) before
     // the fetched-expert GEMM, which the compute stream makes wait for them
-    if (sum.n_fetch_mine > 1) {
-      if ((s = ferryb_h2d_fetch_flagged(L->h2d, fslots.data() + 1, fkeys.data() + 1,
-                                        sum.n_fetch_mine - 1, L->ready + 1, ready_value)))
-        return s;
-    }
+    if (sum.n_fetch_mine > 1 && (s = fetch(1, sum.n_fetch_mine - 1))) return s;
     if (sum.n_fetch_mine > 0) {
       if ((s = ferryb_h2d_wait_device(L->h2d, fslots.data(), sum.n_fetch_mine, stream))) return s;
     }
   }
-  if ((s = swiglu_fused_launch(L->maps, L->groups + sum.n_hit, sum.n_fetch_mine, 0, L->ready,
-                               ready_value, L->queue_dep, L->route_w, L->act, L->expert_out,
-                               L->errs + 2, stream, span_of(6))))
+  // with sync_fetch the stream has already waited for every copy: no flag waits
+  if ((s = swiglu_fused_launch(L->maps, L->groups + sum.n_hit, sum.n_fetch_mine, 0,
+                               c.sync_fetch ? nullptr : L->ready, ready_value, L->queue_dep,
+                               L->route_w, L->act, L->expert_out, L->errs + 2, stream, span_of(6),
+                               L->hook_wait_ns)))
     return s;
   if (sum.n_fetch_mine) launches += 1;
-  if (!c.sync_fetch && sum.n_fetch_mine > 1) {
-    if ((s = ferryb_h2d_fetch_flagged(L->h2d, fslots.data() + 1, fkeys.data() + 1,
-                                      sum.n_fetch_mine - 1, L->ready + 1, ready_value)))
-      return s;
-  }
+  if (!c.sync_fetch && sum.n_fetch_mine > 1 && (s = fetch(1, sum.n_fetch_mine - 1))) return s;
   if (timing && sum.n_fetch_mine > 0) {
     if ((s = h2d_record_event(L->h2d, L->tev[7], 1))) return s;
     L->tev_fetched.back() = 1;
@@ -566,6 +598,8 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     FB_CUDA(cudaMemcpyAsync(weights_out, L->weights, 2 * (size_t)c.tokens_per_rank * c.topk,
                             cudaMemcpyDeviceToDevice, stream));
 
+  L->last_event = event;
+  L->last_layer = layer;
   // counters (the reference's fetches_per_rank, copies, dispatch/combine bytes)
   L->stats.layers += 1;
   L->stats.launches += launches;
@@ -674,6 +708,23 @@ extern "C" int ferryb_layer_set_shared(ferryb_layer* L, int32_t moe_layer, const
   FB_CHECK_ARG(reinterpret_cast<uintptr_t>(weights) % 16 == 0,
                "layer_set_shared: weights must be 16-byte aligned");
   L->shared_w[moe_layer] = weights;
+  return FERRYB_OK;
+}
+
+extern "C" int ferryb_layer_status(ferryb_layer* L, cudaStream_t stream) {
+  FB_CHECK_ARG(L, "layer_status: null argument");
+  FB_CUDA(cudaMemcpyAsync(L->errs_host, L->errs, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                          stream));
+  FB_CUDA(cudaStreamSynchronize(stream));
+  return exec_errors(L, L->errs_host);
+}
+
+extern "C" int ferryb_layer_set_fault_hooks(ferryb_layer* L, uint32_t hooks, uint64_t wait_ns) {
+  FB_CHECK_ARG(L, "layer_set_fault_hooks: null argument");
+  FB_CHECK_ARG((hooks & ~7u) == 0, "layer_set_fault_hooks: unknown hook bits 0x%x", hooks);
+  FB_CHECK_ARG(wait_ns <= 10000000000ull, "layer_set_fault_hooks: wait limit above 10 s");
+  L->hooks = hooks;
+  L->hook_wait_ns = wait_ns;
   return FERRYB_OK;
 }
 

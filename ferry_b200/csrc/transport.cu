@@ -22,8 +22,22 @@
 
 namespace ferryb {
 
-__device__ __forceinline__ bool wait_flags(const uint64_t* flags, int n, uint64_t seq, int* err) {
-  return wait_flags_bounded(flags, n, seq, err);
+__device__ __forceinline__ bool wait_flags(const uint64_t* flags, int n, uint64_t seq, int* err,
+                                           uint64_t limit_ns) {
+  return wait_flags_bounded(flags, n, seq, err, limit_ns ? limit_ns : 2000000000ull);
+}
+
+// True when this rank's expert GEMM or transport recorded an error for the
+// data the combine is about to sum.
+__device__ __forceinline__ bool poisoned(const FusedArgs& a) {
+  if (!a.poison) return false;
+  const volatile int* w = a.poison;
+  return (w[0] | w[1]) != 0;
+}
+
+__device__ __forceinline__ uint4 nan_bf16x8() {
+  const uint32_t q = 0x7FC07FC0u;  // two bf16 quiet NaNs
+  return make_uint4(q, q, q, q);
 }
 
 // ---------------------------------------------------------------------------
@@ -298,8 +312,8 @@ __global__ void fused_permute_kernel(const FusedArgs a, uint64_t seq) {
   __shared__ int ok;
   span_begin(a.ts_permute);
   if (threadIdx.x == 0)
-    ok = a.world == 1 ||
-         wait_flags(reinterpret_cast<const uint64_t*>(base + a.off_dflag), a.world, seq, a.err);
+    ok = a.world == 1 || wait_flags(reinterpret_cast<const uint64_t*>(base + a.off_dflag), a.world,
+                                    seq, a.err, a.wait_ns);
   __syncthreads();
   if (!ok) return;
   const int H = a.hdim, K = a.topk;
@@ -347,6 +361,13 @@ __global__ void fused_combine_kernel(const FusedArgs a) {
     dst = reinterpret_cast<__nv_bfloat16*>(base + a.off_ret) +
           ((size_t)a.rank * a.tokens_per_rank + t) * H;
   }
+  if (poisoned(a)) {
+    for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(dst + c) = nan_bf16x8();
+    __syncthreads();
+    span_end(a.ts_combine);
+    return;
+  }
   int pos[kMaxTopK];
   int np = 0;
   for (int j = 0; j < K; ++j) {
@@ -377,16 +398,26 @@ __global__ void fused_combine_kernel(const FusedArgs a) {
 
 // final scatter (source side, world > 1): out[t] = bf16(sum over peers p in
 // rank order with a packet of float(ret[p][t])); tokens without any route get 0.
+// When a peer's partials never arrived (the flag wait ran out) or this rank's
+// own GEMM/transport failed, the row is NaN.
 __global__ void fused_final_kernel(const FusedArgs a, uint64_t seq) {
   const int t = blockIdx.x;
   uint8_t* base = reinterpret_cast<uint8_t*>(a.local_base) + a.parity * a.buf_stride;
   __shared__ int ok;
   span_begin(a.ts_final);
   if (threadIdx.x == 0)
-    ok = wait_flags(reinterpret_cast<const uint64_t*>(base + a.off_cflag), a.world, seq, a.err);
+    ok = wait_flags(reinterpret_cast<const uint64_t*>(base + a.off_cflag), a.world, seq, a.err,
+                    a.wait_ns) &&
+         !poisoned(a);
   __syncthreads();
-  if (!ok) return;
   const int H = a.hdim, R = a.world;
+  if (!ok) {
+    for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(a.out + (size_t)t * H + c) = nan_bf16x8();
+    __syncthreads();
+    span_end(a.ts_final);
+    return;
+  }
   const __nv_bfloat16* ret = reinterpret_cast<const __nv_bfloat16*>(base + a.off_ret);
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     float acc[8];
@@ -413,7 +444,7 @@ __global__ void fused_final_kernel(const FusedArgs a, uint64_t seq) {
 int fused_dispatch(const FusedArgs& a, uint64_t seq, cudaStream_t stream) {
   if (a.tokens_per_rank > 0)
     fused_dispatch_kernel<<<a.tokens_per_rank, 256, 0, stream>>>(a);
-  if (a.world > 1) signal_kernel<<<1, 32, 0, stream>>>(a, a.off_dflag, seq);
+  if (a.world > 1 && !(a.skip_signals & 1)) signal_kernel<<<1, 32, 0, stream>>>(a, a.off_dflag, seq);
   FB_LAUNCH_CHECK();
   return FERRYB_OK;
 }
@@ -433,7 +464,7 @@ int fused_combine(const FusedArgs& a, uint64_t seq, int n_recv_hint, cudaStream_
   if (n_recv_hint > 0) fused_combine_kernel<<<n_recv_hint, 256, 0, stream>>>(a);
   if (after_stores) FB_CUDA(cudaEventRecord(after_stores, stream));
   if (a.world > 1) {
-    signal_kernel<<<1, 32, 0, stream>>>(a, a.off_cflag, seq);
+    if (!(a.skip_signals & 2)) signal_kernel<<<1, 32, 0, stream>>>(a, a.off_cflag, seq);
     if (a.tokens_per_rank > 0) fused_final_kernel<<<a.tokens_per_rank, 256, 0, stream>>>(a, seq);
   }
   FB_LAUNCH_CHECK();

@@ -42,6 +42,12 @@ struct FusedArgs {
   __nv_bfloat16* out;         // [T, H]
   const __nv_bfloat16* addend;  // [T, H] or null: out = bf16(bf16(routed) + addend)
   int* err;
+  // error words of this rank's expert GEMM and transport (2 ints) or null: when
+  // either is set the combine writes NaN rows instead of sums, so output that
+  // misses an expert's contribution never passes for a valid layer
+  const int* poison;
+  uint64_t wait_ns;  // bound on one flag wait (0: 2 s)
+  int skip_signals;  // failure injection: 1 = no dispatch flags, 2 = no combine flags
   // device-clock spans (timing mode) or null
   unsigned long long *ts_dispatch, *ts_permute, *ts_combine, *ts_final;
 };

@@ -70,6 +70,11 @@ class _Executor:
         call('ferryb_layer_get_stats', self.h, ctypes.byref(st))
         return st
 
+    def status(self, device):
+        """Raise FerrybError if a layer enqueued on this executor failed on the
+        device (its GEMM or transport error words; ferryb_layer_status)."""
+        call('ferryb_layer_status', self.h, stream_ptr(device))
+
     def close(self):
         if self.h:
             _lib.lib().ferryb_layer_destroy(self.h)
@@ -118,6 +123,7 @@ class OffloadRuntime:
                                      score=eviction_score, topk=spec.topk)
         self.h2d = None
         self._executors = {}
+        self._error_reported = False
         self.reset()
 
     def _executor(self, tokens):
@@ -126,12 +132,53 @@ class OffloadRuntime:
             ex = self._executors[tokens] = _Executor(self, tokens)
         return ex
 
+    def check(self):
+        """Raise FerrybError if any layer run so far failed on the device.
+
+        execute()/forward() return once the layer is enqueued, so a device
+        error of a layer's expert GEMM or dispatch/combine (a bounded wait that
+        ran out, an index out of range) surfaces at the next execute()/forward()
+        or here; this waits for the runtime's stream.  The failed layer's
+        output rows are NaN.  The reference raises inside the op itself
+        (TORCH_CHECK, ferry/csrc/expert_ops.cpp:20-34)."""
+        try:
+            for ex in self._executors.values():
+                ex.status(self.device)
+        except _lib.FerrybError:
+            self._error_reported = True
+            raise
+
+    def _pending_error(self):
+        """A device error not yet raised to the caller, or None."""
+        if self._error_reported:
+            return None
+        try:
+            self.check()
+        except _lib.FerrybError as exc:
+            return exc
+        return None
+
+    def _run(self, name, *args):
+        try:
+            call(name, *args)
+        except _lib.FerrybError:
+            self._error_reported = True
+            raise
+
+    def set_fault_hooks(self, tokens, hooks, wait_ns=0):
+        """Failure injection for the failure-detection tests (host-side
+        omissions of flag stores; ferryb_layer_set_fault_hooks)."""
+        call('ferryb_layer_set_fault_hooks', self._executor(tokens).h, int(hooks), int(wait_ns))
+
     def reset(self):
         """Empty expert cache and routing history (start of every measured run,
-        ferry/runtime.py:51-62)."""
+        ferry/runtime.py:51-62).  A device error of an earlier layer that was
+        not yet reported is raised after the reset, so the runtime is clean
+        for the next run either way."""
         if self.h2d is not None:
             self.h2d.synchronize()
         torch.cuda.synchronize(self.device)
+        pending = self._pending_error() if self.h2d is not None else None
         for ex in self._executors.values():
             ex.close()
         self._executors = {}
@@ -143,6 +190,9 @@ class OffloadRuntime:
         self.fetches_per_rank = np.zeros(self.world, np.int64)
         self.decode_fetches_per_rank = np.zeros(self.world, np.int64)
         self.serial_wait_ns = 0
+        self._error_reported = False
+        if pending is not None:
+            raise pending
 
     def _check_inputs(self, tensors):
         """Shapes, dtypes and device of the tensors handed to the executor as
@@ -169,7 +219,7 @@ class OffloadRuntime:
         w = weights.contiguous().to(torch.bfloat16)
         pt = probs_tail.float().contiguous() if (probs_tail is not None and score) else None
         before = ex.stats().host_wait_us
-        call('ferryb_layer_execute', ex.h, self.event, int(layer), ptr(h), ptr(sel), ptr(w), ptr(pt),
+        self._run('ferryb_layer_execute', ex.h, self.event, int(layer), ptr(h), ptr(sel), ptr(w), ptr(pt),
              0 if pt is None else pt.shape[0], ptr(out), stream_ptr(self.device))
         self._after(ex, before)
         return out
@@ -190,7 +240,7 @@ class OffloadRuntime:
         ex = self._executor(tokens)
         out = torch.empty_like(hidden)
         before = ex.stats().host_wait_us
-        call('ferryb_layer_forward', ex.h, self.event, int(layer), ptr(hidden), ptr(gate_weight),
+        self._run('ferryb_layer_forward', ex.h, self.event, int(layer), ptr(hidden), ptr(gate_weight),
              ptr(gate_bias), ptr(out), ptr(selected_out), ptr(weights_out), stream_ptr(self.device))
         self._after(ex, before)
         return out
@@ -227,8 +277,13 @@ class OffloadRuntime:
         return sum(ex.stats().combine_bytes for ex in self._executors.values())
 
     def close(self):
+        """Release the executors; raises a device error of an earlier layer
+        that was not yet reported (after releasing them)."""
         if self.h2d is not None:
             self.h2d.synchronize()
+        pending = self._pending_error()
         for ex in self._executors.values():
             ex.close()
         self._executors = {}
+        if pending is not None:
+            raise pending

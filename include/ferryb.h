@@ -447,6 +447,27 @@ FERRYB_API int ferryb_layer_execute(ferryb_layer* layer, int64_t event, int32_t 
                                     const void* hidden, const int64_t* selected,
                                     const void* weights, const float* probs_tail,
                                     int32_t n_probs_tail, void* out, ferryb_stream_t stream);
+/* Errors of the layers already enqueued.  forward/execute return after
+ * enqueueing the layer, so a device error of its expert GEMM or transport
+ * (a bounded wait that ran out: FERRYB_ETIMEOUT; another device error word:
+ * FERRYB_EDEVICE) is reported by the next forward/execute of this executor or
+ * by this call, which waits for `stream` and names the failing MoE layer.
+ * The output rows of a failed layer are NaN, never a partial sum.  Errors are
+ * sticky: every later call reports them until the executor is destroyed.
+ * Replaces the reference's raise at the call itself (TORCH_CHECK,
+ * ferry/csrc/expert_ops.cpp:20-34), which needs a host sync per op. */
+FERRYB_API int ferryb_layer_status(ferryb_layer* layer, ferryb_stream_t stream);
+/* Failure injection for the failure-detection tests: host-side omissions
+ * only (a flag store that is never issued), so every wait that depends on it
+ * runs out after wait_ns (0 = the default 2 s) and reports FERRYB_ETIMEOUT;
+ * no kernel is made to fault.  No counterpart in the reference. */
+#define FERRYB_HOOK_NO_READY_FLAGS 1u     /* copies raise no readiness flags: the
+                                             fetched-expert GEMM's wait runs out */
+#define FERRYB_HOOK_NO_DISPATCH_SIGNAL 2u /* this rank raises no dispatch flags: the
+                                             owners' permute waits run out */
+#define FERRYB_HOOK_NO_COMBINE_SIGNAL 4u  /* this rank raises no combine flags: the
+                                             sources' final-scatter waits run out */
+FERRYB_API int ferryb_layer_set_fault_hooks(ferryb_layer* layer, uint32_t hooks, uint64_t wait_ns);
 FERRYB_API int ferryb_layer_get_stats(const ferryb_layer* layer, ferryb_layer_stats* out);
 /* Timing mode: wait for the recorded phase events and add them to the stats. */
 FERRYB_API int ferryb_layer_collect_timing(ferryb_layer* layer);

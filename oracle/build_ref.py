@@ -23,7 +23,10 @@ REF_DIR = HERE / '_ref'
 NAME = 'ferry_expert_ops'
 
 
-def build(reference='/root/reference', verbose=False):
+def build(reference=None, verbose=False):
+    reference = reference or os.environ.get('FERRY_REFERENCE')
+    if not reference:
+        raise ValueError('no FERRY checkout given: pass --reference or set FERRY_REFERENCE')
     src = Path(reference) / 'ferry' / 'csrc'
     if not (src / 'expert_ops.cpp').exists():
         return None
@@ -56,6 +59,6 @@ def load_ref():
 
 if __name__ == '__main__':
     p = argparse.ArgumentParser()
-    p.add_argument('--reference', default='/root/reference')
+    p.add_argument('--reference', default=None, help='FERRY checkout (default: $FERRY_REFERENCE)')
     a = p.parse_args()
     print(build(a.reference, verbose=True))

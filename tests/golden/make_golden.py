@@ -439,6 +439,8 @@ def main(a):
 
 if __name__ == '__main__':
     p = argparse.ArgumentParser()
-    p.add_argument('--reference', default='/root/reference')
+    p.add_argument('--reference', default=os.environ.get('FERRY_REFERENCE'),
+                   required='FERRY_REFERENCE' not in os.environ,
+                   help='FERRY checkout (default: $FERRY_REFERENCE)')
     p.add_argument('--only', default='', help='comma-separated plan_<name> cases to (re)generate')
     main(p.parse_args())

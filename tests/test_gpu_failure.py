@@ -90,3 +90,73 @@ def test_missing_peer_rank_times_out(monkeypatch):
     ex.close()
     rt.h2d.close()
     _context_still_usable()
+
+
+def _small_runtime(sync_fetch=False):
+    from ferry_b200.model import ModelSpec
+    from ferry_b200.quota import Topology
+    from ferry_b200.runtime import OffloadRuntime
+    from ferry_b200.workload import cpu_pool
+    spec = ModelSpec('qwen3_moe', (0, 1), 32, 4, 256, 128)
+    pool = cpu_pool(spec, spec.layers, 0).pin_memory()
+    return spec, OffloadRuntime(spec, pool, [12], 'ferry', Topology.uniform(1, spec.experts),
+                                sync_fetch=sync_fetch)
+
+
+def _routing(spec, T, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, spec.hidden, generator=g).to(torch.bfloat16)
+    # routes among 8 of the experts, so that every layer fits the 12-slot cache
+    sel = torch.stack([torch.randperm(8, generator=g)[:spec.topk] for _ in range(T)]) + 8 * seed
+    w = torch.full((T, spec.topk), 1.0 / spec.topk).to(torch.bfloat16)
+    return x.to(DEV), sel.to(DEV), w.to(DEV)
+
+
+def test_fetched_expert_gemm_wait_times_out():
+    """The fetched-expert GEMM waits on the device for each copy's readiness
+    flag.  With the flag stores left out on the host (FERRYB_HOOK_NO_READY_FLAGS)
+    and a 0.3 s limit, that wait runs out: the layer's output is NaN (never a
+    sum that silently lacks the fetched experts), check() raises FerrybError
+    naming the MoE layer, the next execute() raises before any fetch or GEMM
+    of its own, and reset() leaves a runtime that runs the next layer
+    correctly."""
+    from ferry_b200 import _lib
+    spec, rt = _small_runtime()
+    T = 16
+    x, sel, w = _routing(spec, T, 0)
+    rt.set_fault_hooks(T, _lib.HOOK_NO_READY_FLAGS, wait_ns=300_000_000)
+    t0 = time.time()
+    out = rt.execute(0, x, sel, w, None)  # enqueued; the failure is found on the device
+    with pytest.raises(_lib.FerrybError, match=r'MoE layer 0 \(event 0\).*fetched expert'):
+        rt.check()
+    assert time.time() - t0 > 0.25
+    assert torch.isnan(out.float()).all()
+    with pytest.raises(_lib.FerrybError, match='MoE layer 0'):
+        rt.execute(1, x, sel, w, None)  # errors are sticky until reset
+    rt.reset()  # already reported: the reset itself does not raise
+    out = rt.execute(0, x, sel, w, None)
+    rt.check()
+    assert torch.isfinite(out.float()).all()
+    rt.close()
+    _context_still_usable()
+
+
+def test_unreported_failure_raises_at_reset_and_close():
+    """A failed layer that nobody checked is reported by reset() (after the
+    runtime has been reset) and by close() (after it has been released)."""
+    from ferry_b200 import _lib
+    spec, rt = _small_runtime()
+    T = 16
+    x, sel, w = _routing(spec, T, 1)
+    rt.set_fault_hooks(T, _lib.HOOK_NO_READY_FLAGS, wait_ns=200_000_000)
+    rt.execute(0, x, sel, w, None)
+    with pytest.raises(_lib.FerrybError, match='MoE layer 0'):
+        rt.reset()
+    out = rt.execute(0, x, sel, w, None)  # the reset took effect
+    rt.check()
+    assert torch.isfinite(out.float()).all()
+    rt.set_fault_hooks(T, _lib.HOOK_NO_READY_FLAGS, wait_ns=200_000_000)
+    rt.execute(1, x, sel, w, None)
+    with pytest.raises(_lib.FerrybError, match='MoE layer 1'):
+        rt.close()
+    _context_still_usable()

@@ -19,14 +19,14 @@ def _spec(layers, experts, topk, hidden, inter, kind='qwen3_moe'):
     return ModelSpec(kind, tuple(range(layers)), experts, topk, hidden, inter)
 
 
-def _setup(spec, caps, seed=0, policy='ferry', score='frequency'):
+def _setup(spec, caps, seed=0, policy='ferry', score='frequency', sync_fetch=False):
     from ferry_b200.quota import Topology
     from ferry_b200.runtime import OffloadRuntime
     from ferry_b200.workload import cpu_pool, zipf_bias
     torch.manual_seed(seed)
     pool = cpu_pool(spec, spec.layers, seed).pin_memory()
     topo = Topology.uniform(len(caps), spec.experts)
-    rt = OffloadRuntime(spec, pool, caps, policy, topo, eviction_score=score)
+    rt = OffloadRuntime(spec, pool, caps, policy, topo, eviction_score=score, sync_fetch=sync_fetch)
     orc = OracleRuntime(spec, pool, caps, policy, topo.masks, topo.seconds, topo.lut, score=score)
     g = torch.Generator().manual_seed(seed + 7)
     gates = [(torch.randn(spec.experts, spec.hidden, generator=g) * 0.02).to(torch.bfloat16)
@@ -43,11 +43,15 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize('sync_fetch', [False, True], ids=['flags', 'sync_fetch'])
 @pytest.mark.parametrize('case', CASES, ids=lambda c: f'E{c[1]}_k{c[2]}_H{c[3]}_T{c[5]}')
-def test_execute_matches_oracle(case):
+def test_execute_matches_oracle(case, sync_fetch):
+    """Both fetch modes: readiness flags waited on by the GEMM (default) and
+    sync_fetch (every copy waited for by the stream first; smoke() and
+    profiler runs use it)."""
     layers, E, K, H, I, T, cap = case
     spec = _spec(layers, E, K, H, I)
-    rt, orc, gates, biases, g = _setup(spec, [cap])
+    rt, orc, gates, biases, g = _setup(spec, [cap], sync_fetch=sync_fetch)
     for step in range(3 * layers):
         layer = step % layers
         x = torch.randn(T, H, generator=g).to(torch.bfloat16)
