@@ -24,7 +24,11 @@ e2e      = the same through the public API with each step's inputs copied from
            pinned host memory and the step's output read back.
 --impl reference times the reference's CPU path (the oracle port of
            ferry's planner/layout + the torch-CPU restatement of expert_ops)
-           on this host's cores, on a bounded sample of layers per step.
+           on this host's cores: the same full 48-layer steps, on the same
+           seeded inputs and weights, with one persistent runtime whose cache
+           warms over the warm-up steps exactly like the GPU arm's (rank 0
+           alone, every rank of the job emulated in its process; the GPU only
+           fills the expert pool before timing).
 """
 import argparse
 import json
@@ -218,15 +222,32 @@ def policy_opts(a):
                 score=a.eviction_score)
 
 
-def bench_config(spec, world, T, caps, policy):
-    """The workload both arms run (the driver compares their lines)."""
+def bench_config(a, spec, world, T, caps):
+    """The workload both arms run; the driver compares the two lines' config."""
     return {'workload': f'config 1 (Qwen3-30B-A3B MoE layer, decode batch {T}/GPU) in the '
                         f'{spec.layers}-layer MoE stack, 30% global expert cache, all experts in '
                         'pinned host memory',
             'moe_layers': spec.layers, 'global_batch': world * T, 'tokens_per_gpu': T, 'seq_len': 1,
-            'parallelism': f'dp{world}-ep{world}', 'cache_slots_per_rank': caps, 'policy': policy}
+            'parallelism': f'dp{world}-ep{world}', 'cache_slots_per_rank': caps, 'policy': a.policy,
+            **policy_opts(a),
+            'inputs': 'seeded: router gates + Zipf(1.1) biases seed 0, expert pool seed 1 '
+                      '(N(0,0.02) bf16), hidden states seed 1000+rank (N(0,1), rho 0.5), '
+                      'layer l routes x_l + out_(l-1)',
+            'l2': 'no flush: each layer step reads > 126 MB of expert weights (> L2)'}
 
 
+def make_inputs(spec, T, world, ranks, n_steps):
+    """inputs[r][i]: rank r's [layers, T, H] bf16 hidden states of step i (CPU),
+    the same for every arm."""
+    from ferry_b200.workload import HiddenStream
+    out = {}
+    for r in ranks:
+        hs = HiddenStream(spec, T, 0.5, 1000 + r, 'cpu')
+        out[r] = [torch.stack([hs.next(l) for l in range(spec.layers)]) for _ in range(n_steps)]
+    return out
+
+
+SPAN_LAYERS = 4096  # device-clock spans recorded per collect (ferryb_layer_stats.kernel_us)
 KERNELS = ['router', 'planner', 'layout', 'dispatch', 'permute', 'gemm_cached', 'gemm_fetched',
            'combine', 'final_scatter']
 
@@ -270,9 +291,9 @@ def run_ours(a, rank, world, local):
             b_alone = host_link_gbs(rt.cache, wl.pool)
     barrier(world)
     b_host = host_link_gbs(rt.cache, wl.pool)
-    stream = wl.hidden_stream(T, seed=1, world=world, rank=rank)
     n_steps = a.warmup + a.steps
-    inputs = [torch.stack([stream.next(l) for l in range(L)]) for _ in range(n_steps)]
+    host = make_inputs(spec, T, world, [rank], n_steps)[rank]
+    inputs = [x.to(dev) for x in host]
 
     def step(inp):
         prev = None
@@ -310,7 +331,7 @@ def run_ours(a, rank, world, local):
     # e2e: inputs from pinned host memory each step, output read back each step
     e2e = None
     if not a.no_e2e:
-        host_inputs = [x.cpu().pin_memory() for x in inputs[a.warmup:]]
+        host_inputs = [x.pin_memory() for x in host[a.warmup:]]
         barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -328,6 +349,7 @@ def run_ours(a, rank, world, local):
 
     hbm_gbs, bf16_tflops, peak_kind = measured_peaks()
     layers_timed = max(1, st.timed_layers)
+    sampled = max(1, min(st.timed_layers, SPAN_LAYERS))
     # dominant kernel: the grouped SwiGLU over cached experts (HBM-bound at decode)
     gemm_us = st.phase_us[2]
     achieved = st.hit_weight_bytes / (gemm_us * 1e-6) / 1e9 if gemm_us > 0 else 0.0
@@ -341,13 +363,14 @@ def run_ours(a, rank, world, local):
                 'traffic_note': (traffic.get('note') if traffic else 'no ncu capture committed')}
     if st.hit_gemm_kernel_launches:
         # the same launches on the device clock (earliest CTA start to latest CTA
-        # end): CUDA events on the compute stream also absorb the command-fetch
-        # delay the host link's saturating expert copies impose on every
-        # compute-stream command
+        # end), over exactly the launches whose spans were recorded: CUDA events
+        # on the compute stream also absorb the command-fetch delay the host
+        # link's saturating expert copies impose on every compute-stream command
         clk_us = st.hit_gemm_kernel_us / st.hit_gemm_kernel_launches
-        clk = st.hit_weight_bytes / st.hit_gemm_kernel_launches / (clk_us * 1e-6) / 1e9
+        clk = st.hit_gemm_kernel_bytes / (st.hit_gemm_kernel_us * 1e-6) / 1e9
         roofline['device_clock'] = {'achieved': round(clk, 1), 'frac': round(clk / hbm_gbs, 4),
                                     'launch_us': round(clk_us, 1),
+                                    'launches': int(st.hit_gemm_kernel_launches),
                                     'event_launch_us': round(gemm_us / layers_timed, 1)}
     # per-layer roofline: slowest of host-link fetch, NVLink exchange, tensor FLOPs
     expert_bytes = spec.expert_bytes
@@ -382,9 +405,10 @@ def run_ours(a, rank, world, local):
         'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': ms / a.steps,
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
         'data': 'synthetic: random-init N(0,0.02) weights, N(0,1) hidden states rho=0.5, Zipf(1.1) router bias',
-        'config': dict(bench_config(spec, world, T, caps, a.policy), **policy_opts(a), pool_layers=pool_layers,
-                   pool='one shared pinned pool per node' if shared else 'pinned pool per rank',
-                   l2='no flush: each layer step reads > 126 MB of expert weights (> L2)'),
+        'config': bench_config(a, spec, world, T, caps),
+        'pool': {'layers': pool_layers,
+                 'kind': 'one shared pinned pool per node' if shared else 'pinned pool per rank'},
+        'topology': topo_note,
         'roofline': roofline, 'layer_roofline': layer_roofline, 'layer_split_us': split,
         'gpu_launches': int(st.launches), 'h2d_expert_copies': int(fetch_copies),
         'host_wait_us_per_layer': round(st.host_wait_us / max(1, st.layers), 1),
@@ -394,15 +418,36 @@ def run_ours(a, rank, world, local):
         'copy_lane_us_per_layer': {name: round(st.copy_us[i] / layers_timed, 1) for i, name in enumerate(
             ['layout_end_to_first_copy', 'copies', 'last_copy_to_combine_end'])},
         # per-MoE-layer split on the device clock: each kernel's span (earliest
-        # CTA start to latest CTA end), averaged over the timed layers
-        'kernel_us_per_layer_device_clock': {name: round(st.kernel_us[i] / layers_timed, 1)
+        # CTA start to latest CTA end), summed over the layers whose spans were
+        # recorded (the first 4096 timed layers) and divided by their number
+        'kernel_us_per_layer_device_clock': {name: round(st.kernel_us[i] / sampled, 1)
                                              for i, name in enumerate(KERNELS) if st.kernel_launches[i]},
+        'kernel_us_per_launch_device_clock': {
+            name: {'us': round(st.kernel_us[i] / st.kernel_launches[i], 1),
+                   'launches': int(st.kernel_launches[i])}
+            for i, name in enumerate(KERNELS) if st.kernel_launches[i]},
         'setup_s': round(setup_s, 1), 'e2e': e2e, 'clocks': clocks,
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        result['cpu_baseline'] = cpu_baseline(spec, wl, caps, T, a.cpu_seconds, a)
+        result['cpu_baseline'] = cpu_baseline(spec, wl, caps, T, a.cpu_seconds, a, host)
+    result['self_check'] = self_check(result)
     rt.close()
     return result
+
+
+def self_check(result):
+    """Fractions of a measured peak above 1.2 mean the timed kernel did not do
+    the work counted for it (a bookkeeping error): flag them in the line."""
+    problems = []
+    roof = result.get('roofline') or {}
+    for name, frac in (('roofline', roof.get('frac')),
+                       ('roofline.device_clock', (roof.get('device_clock') or {}).get('frac')),
+                       ('layer_roofline', (result.get('layer_roofline') or {}).get('frac'))):
+        if frac is not None and frac > 1.2:
+            problems.append(f'{name}.frac = {frac} > 1.2')
+    for p in problems:
+        print(f'bench self-check: {p}', file=sys.stderr)
+    return {'ok': not problems, 'problems': problems}
 
 
 # ---------------------------------------------------------------------------
@@ -487,87 +532,97 @@ def run_full_model(a, rank, world, local):
             'fetches_per_rank': m['fetches_per_rank'], 'decode_fetches_per_rank': m['decode_fetches_per_rank']}
 
 
-def cpu_layers(spec, wl, caps, T, world, seconds, min_layers=2, max_layers=None, policy='ferry',
-               opts=None):
-    """Run the reference's CPU path (oracle port) over consecutive layers for
-    about `seconds`; returns (layers_done, elapsed)."""
+def reference_steps(spec, pool, gates, biases, caps, a, inputs, warmup, steps, budget_s=None):
+    """The reference's CPU path (oracle port: C planner/layout + torch-CPU
+    expert ops, every rank of the job emulated in this process) over full
+    decode steps: layer l of step i routes inputs[r][i][l] + out_(l-1) with the
+    hook's router, as the GPU arm does, through one persistent runtime.  Runs
+    `warmup` untimed steps, then `steps` timed ones (fewer if `budget_s` runs
+    out, at least two); returns the timed steps' seconds."""
     from oracle import expert_ops as ops
-    from oracle.layer import OracleRuntime
     from oracle import planner as op
+    from oracle.layer import OracleRuntime
+    world = len(caps)
     masks = np.asarray([1 << r for r in range(world)], np.int64)
     sec = np.ones(world)
     lut = op.build_lut(spec.experts, world, masks, sec)
-    o = dict(window=128, balance_tol_bps=200, salt=1, score='frequency')
-    o.update(opts or {})
-    orc = OracleRuntime(spec, wl.pool, caps, policy, masks, sec, lut, **o)
-    gates = [g.cpu() for g in wl.gate]
-    biases = [b.cpu() for b in wl.bias]
-    g = torch.Generator().manual_seed(11)
-    done, t0 = 0, time.perf_counter()
-    prev = [None] * world
-    while True:
-        layer = done % spec.layers
-        xs = []
-        for r in range(world):
-            x = torch.randn(T, spec.hidden, generator=g).to(torch.bfloat16)
-            xs.append(x if prev[r] is None else (x.float() + prev[r].float()).to(torch.bfloat16))
-        routed = [ops.route_qwen3(x, gates[layer], spec.topk, True, biases[layer]) for x in xs]
-        probs = [r[2] for r in routed] if o['score'] == 'probability' else None
-        prev, _, _ = orc.execute(layer, xs, [r[0] for r in routed], [r[1] for r in routed], probs)
-        done += 1
-        el = time.perf_counter() - t0
-        if (el >= seconds and done >= min_layers) or (max_layers and done >= max_layers):
-            return done, el
+    orc = OracleRuntime(spec, pool, caps, a.policy, masks, sec, lut, window=a.history_window,
+                        balance_tol_bps=a.balance_tol_bps, salt=a.salt, score=a.eviction_score)
+    prob = a.eviction_score == 'probability'
+    bf16 = torch.bfloat16
+
+    def step(i):
+        prev = [None] * world
+        for l in range(spec.layers):
+            xs = []
+            for r in range(world):
+                x = inputs[r][i][l]
+                xs.append(x if prev[r] is None else (x.float() + prev[r].float()).to(bf16))
+            routed = [ops.route_qwen3(x, gates[l], spec.topk, True, biases[l]) for x in xs]
+            prev, _, _ = orc.execute(l, xs, [q[0] for q in routed], [q[1] for q in routed],
+                                     [q[2] for q in routed] if prob else None)
+        return prev
+
+    for i in range(warmup):
+        step(i)
+    times, t_start = [], time.perf_counter()
+    for i in range(warmup, warmup + steps):
+        t0 = time.perf_counter()
+        step(i)
+        times.append(time.perf_counter() - t0)
+        if budget_s is not None and len(times) >= 2 and time.perf_counter() - t_start >= budget_s:
+            break
+    return times
 
 
-def cpu_baseline(spec, wl, caps, T, seconds, a):
+def cpu_baseline(spec, wl, caps, T, seconds, a, host):
+    """cpu_baseline of the GPU arm's line: the reference arm's measurement on a
+    bounded sample (one warm-up step, then as many full steps as fit in
+    `seconds`) of the same inputs."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    done, el = cpu_layers(spec, wl, caps, T, 1, seconds, policy=a.policy, opts=policy_opts(a))
-    per_layer = el / done
-    return {'value': T / (per_layer * spec.layers), 'unit': 'tokens/s', 'cores': threads,
-            'kind': 'port',
-            'sample': f'{done} consecutive MoE layers (64 tokens, 1 rank) of the same workload through '
-                      f'the oracle port (C planner/layout + torch-CPU expert ops), '
-                      f'{per_layer * 1e3:.1f} ms/layer, scaled to 48 layers'}
+    gates = [g.cpu() for g in wl.gate]
+    biases = [b.cpu() for b in wl.bias]
+    n = len(host) - 1
+    times = reference_steps(spec, wl.pool, gates, biases, caps, a, {0: host}, 1, n, budget_s=seconds)
+    step_s = sum(times) / len(times)
+    return {'value': T / step_s, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
+            'sample': f'{len(times)} full {spec.layers}-layer decode steps (after 1 warm-up step) of the '
+                      f'same inputs through the oracle port (C planner/layout + torch-CPU expert ops), '
+                      f'{step_s * 1e3:.0f} ms/step'}
 
 
 def run_reference(a, rank, world):
-    """The reference's CPU path on this host's cores (rank 0 only)."""
+    """The reference's CPU path on this host's cores (rank 0 only), on the GPU
+    arm's workload: the same config, inputs and weights, full steps."""
     from ferry_b200.workload import SyntheticMoE
     spec = qwen3_spec(a.layers)
     T = a.tokens
     caps = spec.cache_slots(a.cache_ratio, world)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    # the CPU path reads the expert weights straight from a host pool
-    wl = SyntheticMoE(spec, seed=0, device='cpu', pool_layers=1, build_pool=False)
-    g = torch.Generator().manual_seed(1)
-    wl.pool = (torch.randn(spec.experts, spec.expert_elements, generator=g) * 0.02).to(torch.bfloat16)
-    layers_per_step = 4
-    for _ in range(a.warmup):
-        cpu_layers(spec, wl, caps, T, world, 0.0, min_layers=1, max_layers=1, policy=a.policy,
-                   opts=policy_opts(a))
-    t0 = time.perf_counter()
-    total_layers = 0
-    for _ in range(a.steps):
-        done, _ = cpu_layers(spec, wl, caps, T, world, 0.0, min_layers=layers_per_step,
-                             max_layers=layers_per_step, policy=a.policy, opts=policy_opts(a))
-        total_layers += done
-    el = time.perf_counter() - t0
-    per_layer = el / total_layers
-    step_s = per_layer * spec.layers
+    dev = 'cuda' if torch.cuda.is_available() else 'cpu'
+    pool_layers = auto_pool_layers(spec, 1, a.pool_layers)
+    # the GPU only draws the expert pool (seeded, as the GPU arm draws it)
+    wl = SyntheticMoE(spec, seed=0, device=dev, pool_layers=pool_layers)
+    gates = [g.cpu() for g in wl.gate]
+    biases = [b.cpu() for b in wl.bias]
+    inputs = make_inputs(spec, T, world, range(world), a.warmup + a.steps)
+    times = reference_steps(spec, wl.pool, gates, biases, caps, a, inputs, a.warmup, a.steps)
+    step_s = sum(times) / len(times)
     value = world * T / step_s
-    return {'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': a.steps,
+    return {'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': len(times),
             'warmup': a.warmup, 'ms_per_step': step_s * 1e3, 'higher_is_better': True,
             'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'impl': 'reference',
-            'data': 'synthetic: random-init N(0,0.02) weights, N(0,1) hidden states, Zipf(1.1) router bias',
-            'config': dict(bench_config(spec, world, T, caps, a.policy), **policy_opts(a),
-                           execution=f'{world} rank(s) emulated in one host process'),
+            'data': 'synthetic: random-init N(0,0.02) weights, N(0,1) hidden states rho=0.5, Zipf(1.1) router bias',
+            'config': bench_config(a, spec, world, T, caps),
+            'pool': {'layers': pool_layers, 'kind': 'one pool in this process'},
+            'topology': 'uniform (the CPU emulation has no host links)',
+            'execution': f'{world} rank(s) emulated in one host process, {threads} threads',
             'cpu_baseline': {'value': value, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
-                             'sample': f'{layers_per_step} MoE layers per step x {a.steps} steps, '
-                                       f'{world} rank(s) emulated in one process, scaled to '
-                                       f'{spec.layers} layers ({per_layer * 1e3:.1f} ms/layer)'},
+                             'sample': f'{len(times)} timed full {spec.layers}-layer decode steps after '
+                                       f'{a.warmup} warm-up steps, {world} rank(s) emulated in one '
+                                       f'process ({step_s * 1e3:.0f} ms/step)'},
             'e2e': {'value': value, 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
 
 

@@ -64,7 +64,7 @@ class LayerStats(ctypes.Structure):
         ('host_wait_us', _dbl), ('phase_us', _dbl * 5), ('host_us', _dbl * 6),
         ('copy_us', _dbl * 3), ('hit_gemm_kernel_us', _dbl), ('hit_gemm_kernel_launches', _i64),
         ('dispatch_permute_us', _dbl), ('combine_store_us', _dbl),
-        ('kernel_us', _dbl * 9), ('kernel_launches', _i64 * 9)]
+        ('kernel_us', _dbl * 9), ('kernel_launches', _i64 * 9), ('hit_gemm_kernel_bytes', _i64)]
 
 
 # name -> (restype, argtypes); every symbol declared in include/ferryb.h.

@@ -79,9 +79,10 @@ struct ferryb_layer {
   // (start initially ~0, end initially 0), in the workspace; kernel order:
   // router, planner, layout, dispatch, permute, cached GEMM, fetched GEMM,
   // combine, final scatter (more than one rank)
-  static constexpr int kTs = 512, kSpans = 9;
+  static constexpr int kTs = 4096, kSpans = 9;
   unsigned long long* spans = nullptr;
   std::vector<char> ts_used;  // per timed layer: has a span slot
+  std::vector<int64_t> ts_hit_bytes;  // per timed layer: its cached experts' weight bytes
   size_t tev_used = 0;
   cudaEvent_t* tev = nullptr;
   GemmMaps maps{};
@@ -409,6 +410,7 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     L->tev_used += 10;
     L->tev_fetched.push_back(0);
     L->ts_used.push_back(L->ts_used.size() < (size_t)ferryb_layer::kTs ? 1 : 0);
+    L->ts_hit_bytes.push_back(0);
     FB_CUDA(cudaEventRecord(L->tev[0], stream));
   }
   // device-clock span slot k of this layer (timing mode), or null
@@ -600,6 +602,8 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
 
   L->last_event = event;
   L->last_layer = layer;
+  if (timing && !L->ts_hit_bytes.empty())
+    L->ts_hit_bytes.back() = (int64_t)sum.n_hit * 3 * (int64_t)c.hidden * c.intermediate * 2;
   // counters (the reference's fetches_per_rank, copies, dispatch/combine bytes)
   L->stats.layers += 1;
   L->stats.launches += launches;
@@ -667,6 +671,7 @@ extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
         if (k == 5) {
           L->stats.hit_gemm_kernel_us += (double)(t1 - t0) / 1000.0;
           L->stats.hit_gemm_kernel_launches += 1;
+          L->stats.hit_gemm_kernel_bytes += L->ts_hit_bytes[i];
         }
       }
     }
@@ -674,6 +679,7 @@ extern "C" int ferryb_layer_collect_timing(ferryb_layer* L) {
     FB_CUDA(cudaMemcpy(L->spans, ts.data(), ts.size() * sizeof(unsigned long long),
                        cudaMemcpyHostToDevice));
     L->ts_used.clear();
+    L->ts_hit_bytes.clear();
   }
   L->tev_used = 0;
   return FERRYB_OK;

@@ -50,7 +50,8 @@ class SyntheticMoE:
                                                     fill=lambda t: self._fill(t, seed + 1), group=group)
                 self.pool = self.shared_pool.tensor
             else:
-                self.pool = torch.empty((rows, spec.expert_elements), dtype=torch.bfloat16, pin_memory=True)
+                self.pool = torch.empty((rows, spec.expert_elements), dtype=torch.bfloat16,
+                                        pin_memory=torch.cuda.is_available())
                 self._fill(self.pool, seed + 1)
 
     def _fill(self, pool, seed):
@@ -64,7 +65,8 @@ class SyntheticMoE:
             block = torch.randn((n, spec.expert_elements), generator=gen, device=self.device,
                                 dtype=torch.float32).mul_(0.02).to(torch.bfloat16)
             pool[r0:r0 + n].copy_(block)
-        torch.cuda.synchronize(self.device)
+        if self.device.type == 'cuda':
+            torch.cuda.synchronize(self.device)
         return pool
 
     def hidden_stream(self, tokens, seed=0, world=1, rank=0):
@@ -73,19 +75,22 @@ class SyntheticMoE:
 
 
 class HiddenStream:
+    """Drawn on the CPU from a seeded generator (so every arm of the bench, GPU
+    or CPU, sees the same states) and handed out on `device`."""
+
     def __init__(self, spec, tokens, rho, seed, device):
-        self.gen = torch.Generator(device=device).manual_seed(seed)
+        self.gen = torch.Generator().manual_seed(seed)
+        self.device = torch.device(device)
         self.rho, self.c = rho, math.sqrt(1 - rho * rho)
-        self.state = [torch.randn((tokens, spec.hidden), generator=self.gen, device=device)
+        self.state = [torch.randn((tokens, spec.hidden), generator=self.gen)
                       for _ in range(spec.layers)]
 
     def next(self, layer):
         """The layer's hidden states for the next decode step (bf16)."""
         h = self.state[layer]
         out = h.to(torch.bfloat16)
-        self.state[layer] = h.mul(self.rho).add_(
-            torch.randn(h.shape, generator=self.gen, device=h.device), alpha=self.c)
-        return out
+        self.state[layer] = h.mul(self.rho).add_(torch.randn(h.shape, generator=self.gen), alpha=self.c)
+        return out.to(self.device)
 
 
 def cpu_pool(spec, layers, seed=0):

@@ -419,8 +419,13 @@ typedef struct ferryb_layer_stats {
   double kernel_us[9];        /* timing mode, device clock (earliest CTA start to latest CTA
                                  end), summed: router, planner, layout, dispatch, permute,
                                  cached-expert GEMM, fetched-expert GEMM, combine, final
-                                 scatter (more than one rank) */
+                                 scatter (more than one rank); spans are recorded for the
+                                 first 4096 layers after each collect, kernel_launches
+                                 counts the launches summed */
   int64_t kernel_launches[9];
+  int64_t hit_gemm_kernel_bytes; /* timing mode: cached-expert weight bytes of exactly the
+                                    launches in hit_gemm_kernel_us (the device-clock
+                                    roofline's numerator) */
 } ferryb_layer_stats;
 
 typedef struct ferryb_layer ferryb_layer;

@@ -40,7 +40,7 @@ def test_struct_sizes_match_c_layout():
     # 8 int32 + 2 x 256 int32 + 3 x 32 int32
     assert ctypes.sizeof(_lib.LayoutSummary) == 4 * (8 + 512 + 96)
     assert ctypes.sizeof(_lib.LayerConfig) == 14 * 4
-    assert ctypes.sizeof(_lib.LayerStats) == 10 * 8 + 8 + 5 * 8 + 6 * 8 + 3 * 8 + 8 + 8 + 8 + 8 + 9 * 8 + 9 * 8
+    assert ctypes.sizeof(_lib.LayerStats) == 10 * 8 + 8 + 5 * 8 + 6 * 8 + 3 * 8 + 8 + 8 + 8 + 8 + 9 * 8 + 9 * 8 + 8
     # 6 int32, 2 int64, 4 int32, 14 pointers
     assert ctypes.sizeof(_lib.Planner) == 24 + 16 + 16 + 16 * 8 + 8  # + order_cap, padded
 

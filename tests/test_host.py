@@ -127,11 +127,43 @@ def test_bench_helpers():
     from pathlib import Path
     sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
     import bench
+    import argparse
     spec = bench.qwen3_spec(48)
-    cfg = bench.bench_config(spec, 2, 64, [922, 921], 'ferry')
+    a = argparse.Namespace(policy='ferry', history_window=128, balance_tol_bps=200, salt=1,
+                           eviction_score='frequency')
+    cfg = bench.bench_config(a, spec, 2, 64, [922, 921])
     assert cfg['global_batch'] == 128 and cfg['parallelism'] == 'dp2-ep2' and 'model' not in cfg
+    assert cfg['window'] == 128 and cfg['score'] == 'frequency'
     assert bench.auto_pool_layers(spec, 8, 5) == 5
     assert 1 <= bench.auto_pool_layers(spec, 1, 0) <= 48
+    # both arms draw the same hidden states
+    small = bench.qwen3_spec(2)
+    x1 = bench.make_inputs(small, 4, 2, [1], 2)[1]
+    x2 = bench.make_inputs(small, 4, 2, [0, 1], 2)[1]
+    assert all(torch.equal(p, q) for p, q in zip(x1, x2)) and x1[0].shape == (2, 4, 2048)
+    # frac above 1.2 is flagged
+    assert bench.self_check({'roofline': {'frac': 0.8, 'device_clock': {'frac': 1.47}}})['ok'] is False
+    assert bench.self_check({'roofline': {'frac': 0.8}, 'layer_roofline': {'frac': 0.95}})['ok'] is True
+
+
+def test_reference_arm_small():
+    """--impl reference: full steps through the CPU path, the GPU arm's config."""
+    import argparse
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+    spec = bench.qwen3_spec(2)
+    a = argparse.Namespace(policy='ferry', history_window=128, balance_tol_bps=200, salt=1,
+                           eviction_score='frequency')
+    g = torch.Generator().manual_seed(0)
+    pool = (torch.randn(spec.experts, spec.expert_elements, generator=g) * 0.02).to(torch.bfloat16)
+    from ferry_b200.workload import zipf_bias
+    gates = [(torch.randn(spec.experts, spec.hidden, generator=g) * 0.02).to(torch.bfloat16) for _ in range(2)]
+    biases = [zipf_bias(spec.experts, 1.1, g) for _ in range(2)]
+    inputs = bench.make_inputs(spec, 8, 1, [0], 3)
+    times = bench.reference_steps(spec, pool, gates, biases, [60], a, inputs, 1, 2)
+    assert len(times) == 2 and all(t > 0 for t in times)
 
 
 def test_clock_sampler_parses_reasons():
