@@ -229,3 +229,43 @@ def test_forward_probability_score():
         held = slots[slots >= 0]
         assert len(set(held.tolist())) == held.size and (owner[held] == 0).all()
     rt.close()
+
+
+def test_bench_configuration_matches_oracle():
+    """The bench's own workload: the 48-layer Qwen3-30B-A3B MoE stack, 64 decode
+    tokens, 1,843 cache slots (30 % global), Zipf(1.1) router bias, rho = 0.5
+    hidden states, layer l routing x_l + out_(l-1), through forward() (router in
+    kernel 1) for three decode steps.  The oracle is fed this runtime's routing
+    and layer inputs, so that each of the 144 layers is compared on its own:
+    cache decisions bit-exact, outputs within the BF16 tolerance.  The pool
+    holds two layers' experts (key mod 256 rows, as bench.py --pool-layers 2)."""
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+    from ferry_b200.quota import Topology
+    from ferry_b200.runtime import OffloadRuntime
+    from ferry_b200.workload import SyntheticMoE
+    spec = bench.qwen3_spec(48)
+    T, caps = 64, spec.cache_slots(0.3, 1)
+    assert caps == [1843]
+    wl = SyntheticMoE(spec, seed=0, device=DEV, pool_layers=2)
+    topo = Topology.uniform(1, spec.experts)
+    rt = OffloadRuntime(spec, wl.pool, caps, 'ferry', topo)
+    orc = OracleRuntime(spec, wl.pool, caps, 'ferry', topo.masks, topo.seconds, topo.lut)
+    inputs = bench.make_inputs(spec, T, 1, [0], 3)[0]
+    sel = torch.empty((T, spec.topk), dtype=torch.int64, device=DEV)
+    w = torch.empty((T, spec.topk), dtype=torch.bfloat16, device=DEV)
+    for step in range(3):
+        prev = None
+        for l in range(spec.layers):
+            x = inputs[step][l].to(DEV)
+            h = x if prev is None else x + prev
+            prev = rt.forward(l, h, wl.gate[l], wl.bias[l], sel, w)
+            want, _, _ = orc.execute(l, [h.cpu()], [sel.cpu()], [w.cpu()])
+            assert_bf16_close(prev.cpu(), want[0], f'step {step} layer {l}')
+        np.testing.assert_array_equal(rt.controller.slots, orc.ctl.slots, err_msg=f'step {step}')
+        np.testing.assert_array_equal(rt.controller.owner, orc.ctl.owner)
+        np.testing.assert_array_equal(rt.controller.last, orc.ctl.last)
+    np.testing.assert_array_equal(rt.fetches_per_rank, orc.fetches_per_rank)
+    rt.close()
