@@ -85,6 +85,10 @@ def parse():
     p.add_argument('--per-rank-pool', action='store_true',
                    help='one pinned expert pool per rank (the reference\'s layout) instead of one '
                         'shared pool per node')
+    p.add_argument('--launch-log', default='',
+                   help='write, for every layer run (warm-up and timed, in order), its cached and '
+                        'fetched expert counts as JSON: the expert-GEMM launches an ncu capture '
+                        'of this command lists, with their algorithmic bytes')
     p.add_argument('--sync-fetch', action='store_true',
                    help='issue each layer\'s copies before its fetched-expert GEMM and wait on '
                         'them from the stream (for profilers that serialise GPU work)')
@@ -247,6 +251,7 @@ def make_inputs(spec, T, world, ranks, n_steps):
     return out
 
 
+PARITY_LAYERS = 3  # layers of the first warm-up step the parity gate replays
 SPAN_LAYERS = 4096  # device-clock spans recorded per collect (ferryb_layer_stats.kernel_us)
 KERNELS = ['router', 'planner', 'layout', 'dispatch', 'permute', 'gemm_cached', 'gemm_fetched',
            'combine', 'final_scatter']
@@ -295,15 +300,33 @@ def run_ours(a, rank, world, local):
     host = make_inputs(spec, T, world, [rank], n_steps)[rank]
     inputs = [x.to(dev) for x in host]
 
-    def step(inp):
+    def step(inp, capture=None):
         prev = None
         for l in range(L):
             h = inp[l] if prev is None else inp[l] + prev
-            prev = rt.forward(l, h, wl.gate[l], wl.bias[l])
+            if capture is not None and l < PARITY_LAYERS:
+                sel = torch.empty((T, spec.topk), dtype=torch.int64, device=dev)
+                w = torch.empty((T, spec.topk), dtype=torch.bfloat16, device=dev)
+                prev = rt.forward(l, h, wl.gate[l], wl.bias[l], sel, w)
+                capture['layers'].append((h.cpu(), sel.cpu(), w.cpu(), prev.cpu()))
+                if l == PARITY_LAYERS - 1:
+                    ctl = rt.controller
+                    capture['state'] = (ctl.slots.copy(), ctl.owner.copy(), ctl.last.copy())
+            else:
+                prev = rt.forward(l, h, wl.gate[l], wl.bias[l])
+            if launch_log is not None:
+                summ = rt.last_summary(T)
+                launch_log.append({'layer': l, 'cached_experts': int(summ.n_hit),
+                                   'fetched_experts': int(summ.n_fetch_mine), 'routes': int(summ.n_routes)})
         return prev
 
+    launch_log = [] if a.launch_log else None
+    # the first layers of the first warm-up step are recorded (inputs, this
+    # rank's routing and outputs, the replicated cache state) for the parity
+    # gate that runs after timing
+    capture = {'layers': [], 'state': None}
     for i in range(a.warmup):
-        step(inputs[i])
+        step(inputs[i], capture if i == 0 else None)
     torch.cuda.synchronize()
     ex = rt._executor(T)
     from ferry_b200._lib import call
@@ -428,11 +451,61 @@ def run_ours(a, rank, world, local):
             for i, name in enumerate(KERNELS) if st.kernel_launches[i]},
         'setup_s': round(setup_s, 1), 'e2e': e2e, 'clocks': clocks,
     }
+    if launch_log is not None:
+        Path(a.launch_log).write_text(json.dumps({
+            'expert_bytes': spec.expert_bytes,
+            'note': 'per layer in run order; the expert GEMM launches once for the cached experts '
+                    '(if any) and once for the fetched experts (if any)',
+            'layers': launch_log}))
+    result['parity'] = parity_gate(spec, wl.pool, caps, a, topo, capture, rank, world)
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         result['cpu_baseline'] = cpu_baseline(spec, wl, caps, T, a.cpu_seconds, a, host)
     result['self_check'] = self_check(result)
     rt.close()
     return result
+
+
+def parity_gate(spec, pool, caps, a, topo, capture, rank, world):
+    """Outside the timed region: the oracle (oracle/layer.py, every rank of the
+    job emulated in rank 0's process, on the run's own LUT) replays the first
+    PARITY_LAYERS layers of the first warm-up step with each rank's recorded
+    inputs and routing.  The replicated cache state (slots, owner, last use)
+    of every rank must equal the oracle's bit for bit, and every rank's layer
+    outputs must be within the BF16 tolerance (2e-2 abs, 1e-2 of max |ref|)."""
+    if a.warmup < 1:
+        return None
+    mine = {'layers': capture['layers'], 'state': capture['state']}
+    gathered = [None] * world
+    if world > 1:
+        dist.all_gather_object(gathered, mine)
+    else:
+        gathered = [mine]
+    if rank != 0:
+        return None
+    from oracle.layer import OracleRuntime
+    orc = OracleRuntime(spec, pool, caps, a.policy, topo.masks, topo.seconds, topo.lut,
+                        window=a.history_window, balance_tol_bps=a.balance_tol_bps, salt=a.salt,
+                        score=a.eviction_score)
+    if a.eviction_score == 'probability':
+        return {'skipped': 'the gate replays the frequency score only'}
+    max_abs, max_rel, ok_out = 0.0, 0.0, True
+    for l in range(len(mine['layers'])):
+        per = [g['layers'][l] for g in gathered]
+        want, _, _ = orc.execute(l, [p[0] for p in per], [p[1] for p in per], [p[2] for p in per])
+        for r in range(world):
+            err = (per[r][3].float() - want[r].float()).abs().max().item()
+            scale = want[r].float().abs().max().item()
+            max_abs = max(max_abs, err)
+            max_rel = max(max_rel, err / max(scale, 1e-30))
+            ok_out = ok_out and err <= 2e-2 and err <= 1e-2 * max(scale, 1e-30)
+    same = all(np.array_equal(g['state'][0], orc.ctl.slots) and np.array_equal(g['state'][1], orc.ctl.owner)
+               and np.array_equal(g['state'][2], orc.ctl.last) for g in gathered)
+    res = {'layers': len(mine['layers']), 'ranks': world,
+           'decisions': 'bit-exact' if same else 'DIFFER', 'max_abs': max_abs,
+           'max_rel': round(max_rel, 6), 'outputs_within_tolerance': ok_out, 'ok': bool(same and ok_out)}
+    if not res['ok']:
+        print(f'bench parity gate failed: {res}', file=sys.stderr)
+    return res
 
 
 def self_check(result):
@@ -445,6 +518,9 @@ def self_check(result):
                        ('layer_roofline', (result.get('layer_roofline') or {}).get('frac'))):
         if frac is not None and frac > 1.2:
             problems.append(f'{name}.frac = {frac} > 1.2')
+    par = result.get('parity')
+    if par and par.get('ok') is False:
+        problems.append('parity gate failed')
     for p in problems:
         print(f'bench self-check: {p}', file=sys.stderr)
     return {'ok': not problems, 'problems': problems}

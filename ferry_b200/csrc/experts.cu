@@ -298,6 +298,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // Persistent fused kernel: both phases of every group in one launch.
 //
+// Phase-1 items pack gate and up into one MMA: the A tile holds 64 gate rows
+// (features f0..f0+63) above the 64 up rows of the same features, so one
+// M = 128 tcgen05.mma per k-step yields both, in TMEM lanes 0-63 (gate) and
+// 64-127 (up).  An item then moves 512 KB of weights instead of 1 MB, which
+// halves the granularity of the work queue (the last wave's imbalance), and
+// the epilogue pairs each feature's gate and up through shared memory: the
+// warps that read TMEM lanes 64-127 hand the up values to the warps that read
+// lanes 0-63, which apply silu(gate) * up.  Phase-2 items are 128 down rows.
+//
 // Work items are claimed in order from an atomic counter:
 //   cached groups' phase-1 tiles, cached groups' phase-2 tiles, then for each
 //   fetched group (in fetch order) its phase-1 tiles and its phase-2 tiles.
@@ -309,10 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 // load of the items it claimed before, and every dependency belongs to an
 // earlier-claimed item or to an already-enqueued copy, so the grid (<= one
 // CTA per SM, all resident) always makes progress; each wait is bounded.
+constexpr int kPackM = 64;  // features per phase-1 item (gate rows = up rows)
+
 struct FusedParams {
   const GemmGroup* groups;
   int n_groups, n_hit;
-  int mt1, mt2, kb1, kb2;
+  int mt1, mt2, kb1, kb2;  // mt1 = I / 64 phase-1 items, mt2 = H / 128 phase-2 items
   int rows1, up_off, rows2, down_off;
   int inter, hidden;
   __nv_bfloat16* act;
@@ -388,13 +399,34 @@ __device__ bool spin_count(const int* cnt, int target, volatile int* abort_flag,
   return true;
 }
 
+// The four epilogue warps (threads 64..191) meet at named barrier 1 (barrier
+// 0 is __syncthreads).  epilogue_all is a barrier that also ANDs a predicate
+// over the 128 threads: every decision to leave the epilogue loop goes
+// through it, so the four warps always leave together and none can be left
+// waiting at a barrier.
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ bool epilogue_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+
 constexpr int kSched = 4;           // claimed-item ring depth
-constexpr int kFusedStages = 4;
-constexpr uint32_t kFusedStageBytes = 2 * kTileBytesA + kTileBytesB;  // 48 KB
-constexpr uint32_t kFusedSmem = kFusedStages * kFusedStageBytes + 1024 + 512;
+constexpr int kFusedStages = 6;
+constexpr uint32_t kFusedStageBytes = kTileBytesA + kTileBytesB;  // 32 KB
+constexpr int kXchgStride = 17;     // floats per feature row of the gate/up exchange (padded)
+constexpr uint32_t kFusedSmem =
+    kFusedStages * kFusedStageBytes + 1024 + 512 + kPackM * kXchgStride * 4;
 
 __global__ void __launch_bounds__(kThreads, 1)
-    swiglu_fused_kernel(const __grid_constant__ CUtensorMap w1, const __grid_constant__ CUtensorMap w2,
+    swiglu_fused_kernel(const __grid_constant__ CUtensorMap w1h, const __grid_constant__ CUtensorMap w2,
                         const __grid_constant__ BMaps bx, const __grid_constant__ BMaps ba,
                         const FusedParams p) {
   constexpr int S = kFusedStages;
@@ -411,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* sched = reinterpret_cast<int*>(sempty + kSched);  // [kSched]
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(sched + kSched);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
+  float* xchg = reinterpret_cast<float*>(smem + S * kFusedStageBytes + 512);  // [64][17]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_items = p.n_groups * (p.mt1 + p.mt2);
@@ -424,11 +457,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&w1);
+    tma_prefetch_desc(&w1h);
     tma_prefetch_desc(&w2);
     for (int i = 0; i < 4; ++i) { tma_prefetch_desc(&bx.m[i]); tma_prefetch_desc(&ba.m[i]); }
   }
-  if (warp == 1) { tmem_alloc(tmem_base_smem, 512); tmem_relinquish(); }
+  if (warp == 1) { tmem_alloc(tmem_base_smem, 256); tmem_relinquish(); }
   if (p.ts && threadIdx.x == 0) atomicMin(&p.ts[0], (unsigned long long)globaltimer_ns());
   tc_fence_before();
   __syncthreads();
@@ -462,11 +495,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         asm volatile("fence.proxy.async.global;" ::: "memory");
         const int kb_n = it.phase == 1 ? p.kb1 : p.kb2;
-        const CUtensorMap* wm = it.phase == 1 ? &w1 : &w2;
         const BMaps* bm = it.phase == 1 ? &bx : &ba;
-        const int row_a = it.phase == 1 ? g.slot * p.rows1 + it.tile * kBlockM
+        // phase 1: gate rows f0.. and up rows f0.. (64 each); phase 2: 128 down rows
+        const int row_a = it.phase == 1 ? g.slot * p.rows1 + it.tile * kPackM
                                         : g.slot * p.rows2 + p.down_off + it.tile * kBlockM;
-        const uint32_t a_bytes = (it.phase == 1 ? 2 : 1) * kTileBytesA;
         const int chunks = (g.count + kMaxN - 1) / kMaxN;
         for (int c = 0; c < chunks && ok; ++c) {
           const int n_valid = min(kMaxN, g.count - c * kMaxN);
@@ -476,10 +508,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kb = 0; kb < kb_n; ++kb) {
             if (!wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err)) { ok = false; break; }
             uint8_t* st = smem + stage * kFusedStageBytes;
-            mbar_expect_tx(&full[stage], a_bytes + b_bytes);
-            tma_load_2d(st, wm, &full[stage], kb * kBlockK, row_a);
-            if (it.phase == 1) tma_load_2d(st + kTileBytesA, wm, &full[stage], kb * kBlockK, row_a + p.up_off);
-            tma_load_2d(st + 2 * kTileBytesA, &bm->m[bi], &full[stage], kb * kBlockK, row_b);
+            mbar_expect_tx(&full[stage], kTileBytesA + b_bytes);
+            if (it.phase == 1) {
+              tma_load_2d(st, &w1h, &full[stage], kb * kBlockK, row_a);
+              tma_load_2d(st + kTileBytesA / 2, &w1h, &full[stage], kb * kBlockK, row_a + p.up_off);
+            } else {
+              tma_load_2d(st, &w2, &full[stage], kb * kBlockK, row_a);
+            }
+            tma_load_2d(st + kTileBytesA, &bm->m[bi], &full[stage], kb * kBlockK, row_b);
             pending |= 1u << stage;
             pend_parity = (pend_parity & ~(1u << stage)) | (phase << stage);
             if (++stage == S) { stage = 0; phase ^= 1; }
@@ -518,19 +554,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t idesc = idesc_bf16_f32(kBlockM, n_mma);
           if (!wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag, p.err)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t d0 = tmem_base + acc * 256;
-          const uint32_t d1 = d0 + 128;
+          const uint32_t d0 = tmem_base + acc * kMaxN;
           for (int kb = 0; kb < kb_n; ++kb) {
             if (!wait_bounded(&full[stage], phase, abort_flag, p.err)) { ok = false; break; }
             tc_fence_after();
             const uint32_t st = smem_u32(smem + stage * kFusedStageBytes);
-            const uint32_t sb = st + 2 * kTileBytesA;
+            const uint32_t sb = st + kTileBytesA;
 #pragma unroll
             for (int k = 0; k < kBlockK / 16; ++k) {
-              const uint64_t bdesc = smem_desc_sw128(sb + k * 32);
               const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-              umma_bf16(d0, smem_desc_sw128(st + k * 32), bdesc, idesc, accum);
-              if (it.phase == 1) umma_bf16(d1, smem_desc_sw128(st + kTileBytesA + k * 32), bdesc, idesc, accum);
+              umma_bf16(d0, smem_desc_sw128(st + k * 32), smem_desc_sw128(sb + k * 32), idesc, accum);
             }
             umma_commit(&empty[stage]);
             if (++stage == S) { stage = 0; phase ^= 1; }
@@ -547,51 +580,62 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    // warp w reads TMEM lanes 32*(w%4)..+31: qd 0,1 = gate rows of a phase-1
+    // tile (features f0 + 32*qd + lane), qd 2,3 = the up rows of the same
+    // features; in phase 2 all four hold down rows tile*128 + 32*qd + lane.
     const int qd = warp & 3;
+    const bool up_rows = qd >= 2;
+    const int f_local = (qd & 1) * 32 + lane;
     int acc = 0, q = 0;
     uint32_t acc_phase = 0, qphase = 0;
     bool ok = true;
     for (;;) {
-      if (!wait_bounded(&sfull[q], qphase, abort_flag, p.err)) break;
+      if (!epilogue_all(wait_bounded(&sfull[q], qphase, abort_flag, p.err))) break;
       const int item = sched[q];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sempty[q]);
       if (++q == kSched) { q = 0; qphase ^= 1; }
-      if (item < 0) break;
+      if (item < 0) break;  // the same entry for all four warps
       const FusedItem it = decode_item(p, item);
       const GemmGroup g = p.groups[it.group];
       const int chunks = (g.count + kMaxN - 1) / kMaxN;
-      const int feature = it.tile * kBlockM + qd * 32 + lane;
-      const int out_cols = it.phase == 1 ? p.inter : p.hidden;
       for (int c = 0; c < chunks; ++c) {
         const int n_valid = min(kMaxN, g.count - c * kMaxN);
-        if (!wait_bounded(&tfull[acc], acc_phase, abort_flag, p.err)) { ok = false; break; }
+        if (!epilogue_all(wait_bounded(&tfull[acc], acc_phase, abort_flag, p.err))) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d0 = tmem_base + (static_cast<uint32_t>(qd * 32) << 16) + acc * 256;
+        const uint32_t d0 = tmem_base + (static_cast<uint32_t>(qd * 32) << 16) + acc * kMaxN;
         for (int c0 = 0; c0 < n_valid; c0 += 16) {
           float v0[16];
           tmem_ld16(d0 + c0, v0);
           if (it.phase == 1) {
-            float v1[16];
-            tmem_ld16(d0 + 128 + c0, v1);
+            if (up_rows) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if (c0 + j < n_valid) {
-                const float gt = bf16_round(v0[j]);
-                const float up = bf16_round(v1[j]);
-                const float a = (gt / (1.0f + expf(-gt))) * up;
-                const size_t row = static_cast<size_t>(g.start + c * kMaxN + c0 + j);
-                p.act[row * out_cols + feature] = __float2bfloat16_rn(a);
+              for (int j = 0; j < 16; ++j) xchg[f_local * kXchgStride + j] = bf16_round(v0[j]);
+            }
+            epilogue_sync();
+            if (!up_rows) {
+              const int feature = it.tile * kPackM + f_local;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (c0 + j < n_valid) {
+                  const float gt = bf16_round(v0[j]);
+                  const float up = xchg[f_local * kXchgStride + j];
+                  const float a = (gt / (1.0f + expf(-gt))) * up;
+                  const size_t row = static_cast<size_t>(g.start + c * kMaxN + c0 + j);
+                  p.act[row * p.inter + feature] = __float2bfloat16_rn(a);
+                }
               }
             }
+            epilogue_sync();
           } else {
+            const int feature = it.tile * kBlockM + qd * 32 + lane;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               if (c0 + j < n_valid) {
                 const size_t row = static_cast<size_t>(g.start + c * kMaxN + c0 + j);
                 float y = bf16_round(v0[j]);
                 if (p.route_w) y = y * __bfloat162float(p.route_w[row]);
-                p.out[row * out_cols + feature] = __float2bfloat16_rn(y);
+                p.out[row * p.hidden + feature] = __float2bfloat16_rn(y);
               }
             }
           }
@@ -615,7 +659,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    tmem_dealloc(tmem_base, 256);
   }
   // the last CTA to finish leaves the counters zeroed for the next launch on
   // this stream (every CTA is past its last claim and dependency read)
@@ -645,7 +689,7 @@ int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups
   p.groups = groups;
   p.n_groups = n_groups;
   p.n_hit = n_hit;
-  p.mt1 = static_cast<int>(m.inter / kBlockM);
+  p.mt1 = static_cast<int>(m.inter / kPackM);
   p.mt2 = static_cast<int>(m.hidden / kBlockM);
   p.kb1 = static_cast<int>(m.hidden / kBlockK);
   p.kb2 = static_cast<int>(m.inter / kBlockK);
@@ -672,7 +716,7 @@ int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups
                                  (int)kFusedSmem));
     attr_set[device] = true;
   }
-  swiglu_fused_kernel<<<grid, kThreads, kFusedSmem, stream>>>(m.w1, m.w2, m.bx, m.ba, p);
+  swiglu_fused_kernel<<<grid, kThreads, kFusedSmem, stream>>>(m.w1h, m.w2, m.bx, m.ba, p);
   FB_LAUNCH_CHECK();
   return FERRYB_OK;
 }
@@ -740,6 +784,9 @@ int make_gemm_maps(GemmMaps* m, const void* cache, int64_t cache_slots, const vo
                (long long)hidden, (long long)inter);
   int s;
   if ((s = make_map_2d_bf16(&m->w1, cache, cache_slots * 3 * inter, hidden, hidden * 2, kBlockM,
+                            kBlockK)))
+    return s;
+  if ((s = make_map_2d_bf16(&m->w1h, cache, cache_slots * 3 * inter, hidden, hidden * 2, kPackM,
                             kBlockK)))
     return s;
   if ((s = make_map_2d_bf16(&m->w2, cache, cache_slots * 3 * hidden, inter, inter * 2, kBlockM,

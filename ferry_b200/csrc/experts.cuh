@@ -10,7 +10,8 @@ struct BMaps {
 };
 
 struct GemmMaps {
-  CUtensorMap w1, w2;  // cache as [slots*3I, H] and [slots*3H, I]
+  CUtensorMap w1, w2;  // cache as [slots*3I, H] and [slots*3H, I] (128-row boxes)
+  CUtensorMap w1h;     // [slots*3I, H] with 64-row boxes (the fused kernel's gate/up halves)
   BMaps bx, ba;        // X [rows_cap, H] and A [rows_cap, I]
   int64_t hidden, inter;
 };
