@@ -54,7 +54,10 @@ def parse():
     p.add_argument('--gpus', type=int, default=1)
     p.add_argument('--steps', type=int, default=10)
     p.add_argument('--warmup', type=int, default=3)
-    p.add_argument('--impl', default='ferry_b200', choices=['ferry_b200', 'reference'])
+    p.add_argument('--impl', default='ferry_b200', choices=['ferry_b200', 'reference', 'reference-gpu'],
+                   help='reference: the reference CPU path on the host cores (the driver\'s arm); '
+                        'reference-gpu: the reference runtime on the GPUs (oracle/ref_runtime.py), '
+                        'an extra comparator record')
     p.add_argument('--layers', type=int, default=48)
     p.add_argument('--tokens', type=int, default=64)
     p.add_argument('--cache-ratio', type=float, default=0.3)
@@ -702,6 +705,90 @@ def run_reference(a, rank, world):
             'e2e': {'value': value, 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
 
 
+def run_reference_gpu(a, rank, world, local):
+    """The reference's GPU runtime (oracle/ref_runtime.py: ferry/runtime.py's
+    execute over the reference's compiled ops and NCCL) on this arm's
+    workload: same config, inputs, weights, LUT and timing as run_ours.
+    Needs the whole pool resident (its H2DEngine indexes the pool by key)."""
+    from oracle.ref_runtime import RefGpuRuntime
+    from ferry_b200.workload import SyntheticMoE
+    dev = torch.device('cuda', local)
+    if not dist.is_initialized():  # the reference's collectives need a process group
+        os.environ.setdefault('MASTER_ADDR', '127.0.0.1')
+        os.environ.setdefault('MASTER_PORT', '29581')
+        dist.init_process_group('nccl', rank=0, world_size=1, device_id=dev,
+                                timeout=timedelta(seconds=180))
+    spec = qwen3_spec(a.layers)
+    T, L = a.tokens, spec.layers
+    caps = spec.cache_slots(a.cache_ratio, world)
+    base = {'metric': METRIC, 'impl': 'reference-gpu', 'n_gpus': world,
+            'config': bench_config(a, spec, world, T, caps)}
+    if a.eviction_score != 'frequency':
+        return dict(base, unavailable='the composed reference runtime replays the frequency score only')
+    shared = world > 1
+    pool_layers = auto_pool_layers(spec, 1 if shared else world, a.pool_layers)
+    if pool_layers < spec.layers:
+        return dict(base, unavailable=f'host memory holds {pool_layers} of {spec.layers} layers of '
+                                      'experts; the reference H2DEngine indexes the pool by key')
+    wl = SyntheticMoE(spec, seed=0, device=dev, pool_layers=pool_layers, shared=shared)
+    topo, topo_note = make_topology(a, spec, rank, world, wl.pool, dev)
+    rt = RefGpuRuntime(spec, wl.pool, caps, a.policy, topo.masks, topo.seconds, topo.lut,
+                       window=a.history_window, balance_tol_bps=a.balance_tol_bps, salt=a.salt)
+    n_steps = a.warmup + a.steps
+    host = make_inputs(spec, T, world, [rank], n_steps)[rank]
+    inputs = [x.to(dev) for x in host]
+
+    def step(inp):
+        prev = None
+        for l in range(L):
+            h = inp[l] if prev is None else inp[l] + prev
+            sel, w = rt.route(h, wl.gate[l], wl.bias[l])
+            prev = rt.execute(l, h, sel, w)
+        return prev
+
+    for i in range(a.warmup):
+        step(inputs[i])
+    barrier(world)
+    sampler = ClockSampler() if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(a.steps):
+        step(inputs[a.warmup + i])
+    ev1.record()
+    ev1.synchronize()
+    barrier(world)
+    clocks = sampler.stop([local]) if sampler else None
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    host_inputs = [x.pin_memory() for x in host[a.warmup:]]
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(a.steps):
+        step(host_inputs[i].to(dev, non_blocking=True)).cpu()
+    e1.record()
+    e1.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    fetches = int(rt.fetches_per_rank.sum())
+    rt.close()
+    return dict(base, value=world * T * a.steps / (ms / 1e3), unit='tokens/s', steps=a.steps,
+                warmup=a.warmup, ms_per_step=ms / a.steps, higher_is_better=True, scaling='weak',
+                vs_baseline=None, dtype='bf16',
+                data='synthetic: random-init N(0,0.02) weights, N(0,1) hidden states rho=0.5, Zipf(1.1) router bias',
+                pool={'layers': pool_layers, 'kind': 'one shared pinned pool per node' if shared else
+                      'pinned pool per rank'},
+                topology=topo_note, clocks=clocks,
+                execution='ferry/runtime.py execute: reference compiled ops (oracle/_ref: H2DEngine, '
+                          'pack/unpack, execute_experts, reduce/scatter), oracle planner/layout, NCCL '
+                          'all_gather_into_tensor + all_to_all_single, torch router',
+                fetches_per_layer=fetches / max(1, rt.event),
+                e2e={'value': world * T * a.steps / (e2e_ms / 1e3), 'unit': 'tokens/s',
+                     'h2d_bytes_per_step': int(host_inputs[0].numel() * 2),
+                     'd2h_bytes_per_step': int(T * spec.hidden * 2), 'ms_per_step': e2e_ms / a.steps})
+
+
 def main():
     a = parse()
     if a.impl == 'reference':
@@ -713,7 +800,9 @@ def main():
         return 0
     rank, world, local = init_dist(a.gpus)
     try:
-        if a.ep_sweep:
+        if a.impl == 'reference-gpu':
+            result = run_reference_gpu(a, rank, world, local)
+        elif a.ep_sweep:
             result = run_ep_sweep(a, rank, world, local)
         elif a.full_model:
             result = run_full_model(a, rank, world, local)
@@ -722,8 +811,9 @@ def main():
         if rank == 0:
             print(json.dumps(result), flush=True)
     finally:
-        if world > 1 and dist.is_initialized():
-            dist.barrier()
+        if dist.is_initialized():
+            if world > 1:
+                dist.barrier()
             dist.destroy_process_group()
     return 0
 

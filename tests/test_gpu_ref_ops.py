@@ -196,3 +196,66 @@ def test_transport_world1_matches_reference_composition(ref):
     partial = ref.reduce_partials(parts, [grp[1] for grp in layout['groups']], xr.shape[0], H, x)
     want = ref.scatter_returned(partial, layout['send_idx'], T)
     assert torch.equal(out, want)
+
+
+def _ref_runtime_worker(rank, world, port, out_dir):
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from ferry_b200.model import ModelSpec
+    from ferry_b200.quota import Topology
+    from ferry_b200.runtime import OffloadRuntime
+    from ferry_b200.workload import cpu_pool, zipf_bias
+    from oracle.ref_runtime import RefGpuRuntime
+    os.environ['NCCL_NVLS_ENABLE'] = '0'
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group('nccl', rank=rank, world_size=world, device_id=torch.device('cuda', rank),
+                            timeout=timedelta(seconds=60))
+    spec = ModelSpec('qwen3_moe', (0, 1), 64, 8, 2048, 768)
+    caps = [100]
+    pool = cpu_pool(spec, spec.layers, 0).pin_memory()
+    topo = Topology.uniform(1, spec.experts)
+    ref = RefGpuRuntime(spec, pool, caps, 'ferry', topo.masks, topo.seconds, topo.lut)
+    rt = OffloadRuntime(spec, pool, caps, 'ferry', topo)
+    g = torch.Generator().manual_seed(3)
+    gates = [(torch.randn(spec.experts, spec.hidden, generator=g) * 0.02).to(torch.bfloat16).cuda()
+             for _ in range(2)]
+    biases = [zipf_bias(spec.experts, 1.1, g).cuda() for _ in range(2)]
+    errs, same = [], True
+    for step in range(6):
+        layer = step % 2
+        x = torch.randn(32, spec.hidden, generator=g).to(torch.bfloat16).cuda()
+        sel, w = ref.route(x, gates[layer], biases[layer])
+        want = ref.execute(layer, x, sel, w)
+        got = rt.execute(layer, x, sel, w, None)
+        torch.cuda.synchronize()
+        errs.append(((got.float() - want.float()).abs().max().item(), want.float().abs().max().item()))
+        same = same and np.array_equal(rt.controller.slots, ref.ctl.slots)
+    rt.close()
+    ref.close()
+    torch.save({'errs': errs, 'same': same, 'copies': (ref.h2d.copies, rt.h2d.copies)},
+               os.path.join(out_dir, 'ref.pt'))
+    dist.destroy_process_group()
+
+
+def test_reference_runtime_composition_matches(ref):
+    """The composed reference runtime (oracle/ref_runtime.py, the comparator of
+    bench.py --impl reference-gpu) against this runtime on the same routed
+    layers (one rank, NCCL collectives of one rank): the same cache decisions
+    and copy counts, outputs within the BF16 tolerance."""
+    import os
+    import tempfile
+
+    import torch.multiprocessing as mp
+    from tests.tolerance import ABS_TOL, REL_TOL
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_ref_runtime_worker, args=(1, 29831, tmp), nprocs=1)
+        res = torch.load(os.path.join(tmp, 'ref.pt'), weights_only=False)
+    assert res['same'], 'cache decisions differ'
+    assert res['copies'][0] == res['copies'][1]
+    for err, scale in res['errs']:
+        assert err <= ABS_TOL and err <= REL_TOL * scale, (err, scale)
