@@ -584,20 +584,83 @@ def run_ep_sweep(a, rank, world, local):
             'nvlink_peer_gbs_reference': 770.0, 'ep_sweep': rows}
 
 
+def _reference_gpu_model_run(cfg, a, rank, world, dev, layers):
+    """The full model with the reference's MoE hooks (ferry/model.py:137-158)
+    over the composed reference GPU runtime (oracle/ref_runtime.py): the same
+    model, weights, prompts and metrics as ferry_b200.harness.run."""
+    from ferry_b200.build_quota_lut import topology_for_run
+    from ferry_b200.harness import build_model, decode_metrics, generate
+    from ferry_b200.workload import SyntheticMoE
+    from oracle.ref_runtime import RefGpuRuntime
+    if not dist.is_initialized():
+        os.environ.setdefault('MASTER_ADDR', '127.0.0.1')
+        os.environ.setdefault('MASTER_PORT', '29582')
+        dist.init_process_group('nccl', rank=0, world_size=1, device_id=dev, timeout=timedelta(seconds=180))
+    overrides = {'num_hidden_layers': layers} if layers else {}
+    model, spec = build_model(cfg, dev, 0, **overrides)
+    wl = SyntheticMoE(spec, seed=1, device=dev, shared=world > 1)
+    caps = spec.cache_slots(a.cache_ratio, world)
+    topo, topo_note = topology_for_run(a.topology, spec, rank, world, pool_row=wl.pool[0], device=dev)
+
+    def make_rt():
+        return RefGpuRuntime(spec, wl.pool, caps, a.policy, topo.masks, topo.seconds, topo.lut)
+    state = {'rt': make_rt()}
+    scaling = float(cfg.get('routed_scaling_factor', 1.0))
+    for layer, idx in enumerate(spec.moe_layers):
+        mlp = model.model.layers[idx].mlp
+        gate = mlp.gate.weight
+        shared = getattr(mlp, 'shared_experts', None)
+
+        def forward(hidden_states, _layer=layer, _gate=gate, _shared=shared):
+            rt = state['rt']
+            shape = hidden_states.shape
+            flat = hidden_states.reshape(-1, shape[-1])
+            if spec.model_type == 'qwen3_moe':
+                sel, w = rt.route(flat, _gate)
+            else:  # transformers' DeepseekV2 greedy routing, no renormalisation
+                probs = torch.softmax(torch.nn.functional.linear(flat.float(), _gate.float()), -1)
+                w, sel = torch.topk(probs, spec.topk, dim=-1)
+                w = (w * scaling).to(flat.dtype)
+            out = rt.execute(_layer, flat, sel, w)
+            if _shared is not None:
+                out = out + _shared(flat)
+            return out.view(shape)
+        mlp.forward = forward
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    prompts = torch.randint(0, cfg['vocab_size'], (a.batch, a.prompt_len), generator=g, device=dev)
+    generate(model, prompts, min(a.new_tokens, 4))
+    state['rt'].close()
+    state['rt'] = make_rt()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    tokens, times = generate(model, prompts, a.new_tokens)
+    m = decode_metrics(times, a.batch, world)
+    m.update(fetches_per_rank=state['rt'].fetches_per_rank.tolist(), decode_fetches_per_rank=None,
+             topology=topo_note)
+    state['rt'].close()
+    return m
+
+
 def run_full_model(a, rank, world, local):
     """BASELINE configs 2-4 through ferry_b200.harness: seeded random prompts
-    (uniform token ids), one warm-up generation, then one timed generation."""
+    (uniform token ids), one warm-up generation, then one timed generation.
+    With --impl reference-gpu the same model runs the reference's hooks over
+    the composed reference GPU runtime instead."""
     from ferry_b200.harness import run
     from ferry_b200.model import DEEPSEEK_V2_LITE, QWEN3_30B_A3B
     cfg = QWEN3_30B_A3B if a.full_model == 'qwen3' else DEEPSEEK_V2_LITE
     dev = torch.device('cuda', local)
     layers = a.layers if a.layers != 48 else None
-    model, rt, tokens, m = run(cfg, batch=a.batch, prompt_len=a.prompt_len, new_tokens=a.new_tokens,
-                               cache_ratio=a.cache_ratio, layers=layers, warmup=1, rank=rank, world=world,
-                               device=dev, policy=a.policy, topology=a.topology)
-    rt.close()
+    if a.impl == 'reference-gpu':
+        m = _reference_gpu_model_run(cfg, a, rank, world, dev, layers)
+    else:
+        model, rt, tokens, m = run(cfg, batch=a.batch, prompt_len=a.prompt_len, new_tokens=a.new_tokens,
+                                   cache_ratio=a.cache_ratio, layers=layers, warmup=1, rank=rank,
+                                   world=world, device=dev, policy=a.policy, topology=a.topology)
+        rt.close()
     name = 'Qwen3-30B-A3B' if a.full_model == 'qwen3' else 'DeepSeek-V2-Lite'
-    return {'metric': f'decode tokens/s, full {name} (box, max over ranks)',
+    return {'metric': f'decode tokens/s, full {name} (box, max over ranks)', 'impl': a.impl,
             'value': m['decode_tokens_per_s'], 'unit': 'tokens/s', 'n_gpus': world, 'steps': a.new_tokens,
             'warmup': 1, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
             'data': 'synthetic: random-init weights, seeded uniform token ids',
@@ -800,12 +863,12 @@ def main():
         return 0
     rank, world, local = init_dist(a.gpus)
     try:
-        if a.impl == 'reference-gpu':
+        if a.full_model:
+            result = run_full_model(a, rank, world, local)
+        elif a.impl == 'reference-gpu':
             result = run_reference_gpu(a, rank, world, local)
         elif a.ep_sweep:
             result = run_ep_sweep(a, rank, world, local)
-        elif a.full_model:
-            result = run_full_model(a, rank, world, local)
         else:
             result = run_ours(a, rank, world, local)
         if rank == 0:

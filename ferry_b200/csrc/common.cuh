@@ -72,6 +72,12 @@ int stream_mem_ops_supported(int device);
 // h2d.cu: record an event on the copy lane (0: before the next fetch, 1:
 // after the last fetch issued)
 int h2d_record_event(ferryb_h2d* h, cudaEvent_t ev, int which);
+// h2d.cu: whole-row copies raising flags_a[i] = value once bytes [0, split)
+// have landed and flags_b[i] once the whole row has (with split_last, the
+// last fetch of the call as two copies; every other fetch as one)
+int h2d_fetch_split_flagged(ferryb_h2d* h, const int64_t* slots, const int64_t* keys, int64_t n,
+                            uint32_t* flags_a, uint32_t* flags_b, uint32_t value, int64_t split,
+                            bool split_last);
 
 // 2D bf16 tensor map over a row-major [rows, cols] matrix (cols contiguous),
 // box = [box_cols, box_rows], 128-byte swizzle (box_cols * 2 must be 128).

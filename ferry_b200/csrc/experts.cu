@@ -329,8 +329,9 @@ struct FusedParams {
   __nv_bfloat16* act;
   __nv_bfloat16* out;
   const __nv_bfloat16* route_w;
-  const uint32_t* ready;  // [fetched] readiness flags, fetch order; null: the stream
-                          // already waited for the copies
+  const uint32_t* ready;  // [fetched] readiness of the gate/up rows, fetch order; null: the
+                          // stream already waited for the copies
+  const uint32_t* ready_down;  // [fetched] readiness of the down rows (phase-2 items)
   uint32_t ready_value;
   uint64_t ready_wait_ns;  // bound on one readiness wait
   int* queue;  // [1] claim counter, zero at launch
@@ -485,9 +486,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (item < 0) break;
         const FusedItem it = decode_item(p, item);
         const GemmGroup g = p.groups[it.group];
-        // dependencies: copy readiness, then (phase 2) the group's phase-1 tiles
+        // dependencies: copy readiness of the rows the item reads (gate/up for
+        // phase 1, down for phase 2), then (phase 2) the group's phase-1 tiles
         if (it.fetched >= 0 && p.ready &&
-            !spin_ready(p.ready + it.fetched, p.ready_value, p.ready_wait_ns, abort_flag, p.err)) {
+            !spin_ready((it.phase == 1 ? p.ready : p.ready_down) + it.fetched, p.ready_value,
+                        p.ready_wait_ns, abort_flag, p.err)) {
           ok = false; break;
         }
         if (it.phase == 2 && !spin_count(p.dep + it.group, 4 * p.mt1, abort_flag, p.err)) {
@@ -676,7 +679,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups, int n_hit,
-                        const uint32_t* ready, uint32_t ready_value, int* queue_dep,
+                        const uint32_t* ready, const uint32_t* ready_down, uint32_t ready_value,
+                        int* queue_dep,
                         const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
                         int* err, cudaStream_t stream, unsigned long long* ts,
                         uint64_t ready_wait_ns) {
@@ -703,6 +707,7 @@ int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups
   p.out = out;
   p.route_w = route_w;
   p.ready = ready;
+  p.ready_down = ready_down ? ready_down : ready;
   p.ready_value = ready_value;
   p.queue = queue_dep;
   p.done = queue_dep + 1;

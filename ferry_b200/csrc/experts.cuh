@@ -29,16 +29,19 @@ int swiglu_grouped_maps(const GemmMaps& m, const GemmGroup* groups, int n_groups
                         int* err, cudaStream_t stream);
 
 // Both phases of every group in one persistent launch; groups [n_hit,
-// n_groups) are fetched experts whose tiles wait for ready[j] >= ready_value
-// (raised when fetch j has landed; ready null: no readiness wait, the stream
-// already waited for the copies; each wait gives up after ready_wait_ns, 0 =
-// the default 2 s, and reports DEV_WAIT_TIMEOUT in *err).  queue_dep: device
+// n_groups) are fetched experts whose phase-1 tiles wait for ready[j] >=
+// ready_value (raised when fetch j's gate/up rows have landed) and phase-2
+// tiles for ready_down[j] (its down rows; null = ready); ready null: no
+// readiness wait, the stream already waited for the copies; each wait gives
+// up after ready_wait_ns, 0 = the default 2 s, and reports DEV_WAIT_TIMEOUT
+// in *err.  queue_dep: device
 // scratch of 2 + n_groups ints, zero before the first launch; every launch
 // leaves it zeroed again (its last CTA resets it).  ts: null, or device [2]
 // that the launch lowers to its earliest CTA start and raises to its latest CTA
 // end (globaltimer ns; start ~0 and end 0 beforehand).
 int swiglu_fused_launch(const GemmMaps& m, const GemmGroup* groups, int n_groups, int n_hit,
-                        const uint32_t* ready, uint32_t ready_value, int* queue_dep,
+                        const uint32_t* ready, const uint32_t* ready_down, uint32_t ready_value,
+                        int* queue_dep,
                         const __nv_bfloat16* route_w, __nv_bfloat16* act, __nv_bfloat16* out,
                         int* err, cudaStream_t stream, unsigned long long* ts = nullptr,
                         uint64_t ready_wait_ns = 0);

@@ -209,3 +209,48 @@ extern "C" int ferryb_h2d_fetch_flagged(ferryb_h2d* h, const int64_t* slots, con
   }
   return FERRYB_OK;
 }
+
+namespace ferryb {
+// Copies of whole expert rows with two readiness flags each: flags_a[i] for
+// bytes [0, split), flags_b[i] for the whole row.  The last fetch of the call
+// is copied in two parts, so with split = the gate + up rows its expert GEMM
+// starts the gate/up tiles while the down rows are still on the link; the
+// others raise both flags after one copy.  The slot's copy event follows the
+// whole row (wait_host / wait_device see it complete).
+int h2d_fetch_split_flagged(ferryb_h2d* h, const int64_t* slots, const int64_t* keys, int64_t n,
+                            uint32_t* flags_a, uint32_t* flags_b, uint32_t value, int64_t split,
+                            bool split_last) {
+  FB_CHECK_ARG(h && (n == 0 || (slots && keys && flags_a && flags_b)),
+               "h2d_fetch_split_flagged: bad arguments");
+  FB_CHECK_ARG(split > 0 && split < h->row_bytes && split % 16 == 0,
+               "h2d_fetch_split_flagged: split must be inside the row and 16-byte aligned");
+  PFN_writeValue32 wv = write_value32_fn();
+  if (!wv) return fail(FERRYB_ECUDA, "cuStreamWriteValue32 is unavailable");
+  DeviceGuard g(h->device);
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t slot = slots[i], key = keys[i];
+    FB_CHECK_ARG(slot >= 0 && slot < h->cache_slots, "h2d_fetch_split_flagged: slot out of range");
+    FB_CHECK_ARG(key >= 0, "h2d_fetch_split_flagged: negative key");
+    cudaStream_t s = h->streams[h->next_stream++ % h->streams.size()];
+    if (h->used_valid[slot]) FB_CUDA(cudaStreamWaitEvent(s, h->used[slot], 0));
+    uint8_t* dst = h->cache + slot * h->row_bytes;
+    const uint8_t* src = h->pool + (key % h->pool_rows) * h->row_bytes;
+    // only the last fetch is split: each extra copy command costs the link a
+    // little, and only the last one decides when the layer's GEMMs can end
+    const bool two = split_last && i == n - 1;
+    const int64_t parts[2][2] = {{0, two ? split : h->row_bytes}, {split, h->row_bytes - split}};
+    for (int q = 0; q < (two ? 2 : 1); ++q) {
+      FB_CUDA(cudaMemcpyAsync(dst + parts[q][0], src + parts[q][0], parts[q][1],
+                              cudaMemcpyHostToDevice, s));
+      FB_CUDA(cudaEventRecord(h->copy_done[slot], s));
+      FB_CUDA(cudaStreamWaitEvent(h->flag_stream, h->copy_done[slot], 0));
+      const bool whole = !two || q == 1;
+      if ((q == 0 && wv((CUstream)h->flag_stream, (CUdeviceptr)(flags_a + i), value, 0) != CUDA_SUCCESS) ||
+          (whole && wv((CUstream)h->flag_stream, (CUdeviceptr)(flags_b + i), value, 0) != CUDA_SUCCESS))
+        return fail(FERRYB_ECUDA, "cuStreamWriteValue32 failed");
+    }
+    ++h->copies;
+  }
+  return FERRYB_OK;
+}
+}  // namespace ferryb

@@ -20,6 +20,7 @@
 // behind it.  A layer's copies start only after its summary is on the host,
 // which follows every earlier compute on the stream, so a cache slot is never
 // overwritten while an earlier layer still reads it.
+#include <atomic>
 #include <chrono>
 #include <cstring>
 #include <vector>
@@ -37,6 +38,14 @@ int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
 }
 
 using namespace ferryb;
+
+// The plan summary as the host sees it: pinned, mapped host memory filled by
+// the layout kernel (SummaryMirror) and released by `seq` = event + 1.
+struct HostMirror {
+  ferryb_layout_summary sum;
+  int32_t errs[8];
+  uint64_t seq;
+};
 
 struct ferryb_layer {
   ferryb_layer_config cfg{};
@@ -67,9 +76,10 @@ struct ferryb_layer {
   __nv_bfloat16 *shared_act = nullptr, *shared_out = nullptr, *shared_ones = nullptr;
   GemmGroup* shared_group = nullptr;
   // host side
-  ferryb_layout_summary* summary_host = nullptr;
-  int32_t* errs_host = nullptr;  // pinned copy of the device error words
-  cudaEvent_t summary_ev = nullptr;
+  HostMirror* mirror_host = nullptr;  // pinned + mapped: the host's view of the plan summary
+  HostMirror* mirror_dev = nullptr;   // the same memory as the device addresses it
+  int32_t* errs_host = nullptr;  // pinned copy of the device error words (ferryb_layer_status)
+  cudaEvent_t summary_ev = nullptr;  // after the layout kernel: tells a late mirror from a lost one
   // timing mode: 10 events per layer (8 on the compute stream, 2 on the copy
   // lane), recorded without host syncs and collected by
   // ferryb_layer_collect_timing
@@ -309,7 +319,9 @@ static int init_layer(ferryb_layer* L, const ferryb_layer_config* cfg,
     const GemmGroup g{0, 0, cfg->tokens_per_rank, 0};
     FB_CUDA(cudaMemcpy(L->shared_group, &g, sizeof(g), cudaMemcpyHostToDevice));
   }
-  FB_CUDA(cudaHostAlloc(&L->summary_host, sizeof(ferryb_layout_summary), cudaHostAllocDefault));
+  FB_CUDA(cudaHostAlloc(&L->mirror_host, sizeof(HostMirror), cudaHostAllocMapped));
+  std::memset(L->mirror_host, 0, sizeof(HostMirror));
+  FB_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&L->mirror_dev), L->mirror_host, 0));
   FB_CUDA(cudaHostAlloc(&L->errs_host, 8 * sizeof(int32_t), cudaHostAllocDefault));
   FB_CUDA(cudaEventCreateWithFlags(&L->summary_ev, cudaEventDisableTiming));
   const int64_t routes = (int64_t)cfg->world * cfg->tokens_per_rank * cfg->topk;
@@ -391,6 +403,11 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
                "layer_forward: hidden must be 16-byte aligned with shared experts");
   uint8_t* half = L->symm + parity * L->sl.half;
   int64_t launches = 0;
+  // the mirror's release word restarts at 0: every layout kernel of an
+  // earlier call has completed (its mirror was observed, or the call failed
+  // before launching one), so nothing can still write it
+  reinterpret_cast<volatile uint64_t*>(&L->mirror_host->seq)[0] = 0;
+  std::atomic_thread_fence(std::memory_order_release);
   using clk = std::chrono::steady_clock;
   auto h_prev = clk::now();
   auto host_mark = [&](int stage) {
@@ -482,28 +499,41 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   la.n_send = L->n_send; la.n_recv = L->n_recv; la.recv_token = L->recv_token;
   la.csr_pos = L->csr_pos; la.peer_row = L->peer_row; la.groups = L->groups;
   la.summary = L->summary_dev; la.err = L->errs + 1;
-  if ((s = layout_launch(la, stream, span_of(2)))) return s;
+  const SummaryMirror mirror{&L->mirror_dev->sum, L->mirror_dev->errs, &L->mirror_dev->seq, L->errs,
+                             seq};
+  if ((s = layout_launch(la, stream, span_of(2), &mirror))) return s;
   launches += 1;  // layout
   if (timing) FB_CUDA(cudaEventRecord(L->tev[1], stream));
 
-  // 4 summary to the host
-  FB_CUDA(cudaMemcpyAsync(L->summary_host, L->summary_dev, sizeof(ferryb_layout_summary),
-                          cudaMemcpyDeviceToHost, stream));
-  FB_CUDA(cudaMemcpyAsync(L->errs_host, L->errs, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost,
-                          stream));
+  // 4 the summary reaches the host through the mapped mirror; the host polls
+  //   its release word (the layer's one host wait), checking the event behind
+  //   the layout kernel now and then so that a launch that failed is reported
+  //   instead of waited for
   FB_CUDA(cudaEventRecord(L->summary_ev, stream));
   host_mark(0);
-  FB_CUDA(cudaEventSynchronize(L->summary_ev));
   {
+    const volatile uint64_t* flag = &L->mirror_host->seq;
+    for (uint32_t spins = 1; *flag != seq; ++spins) {
+      if ((spins & 255) != 0) continue;
+      const cudaError_t q = cudaEventQuery(L->summary_ev);
+      if (q == cudaErrorNotReady) continue;
+      if (q != cudaSuccess) return fail(FERRYB_ECUDA, "layer %d: %s", layer, cudaGetErrorString(q));
+      if (*flag != seq)
+        return fail(FERRYB_EDEVICE, "layer %d (event %lld): the plan summary was not written", layer,
+                    (long long)event);
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
     const auto now = clk::now();
     L->stats.host_wait_us += std::chrono::duration<double, std::micro>(now - h_prev).count();
     h_prev = now;
   }
-  const ferryb_layout_summary sum = *L->summary_host;
+  const ferryb_layout_summary sum = L->mirror_host->sum;
   // error words: [0] planner, [1] layout (this layer), [2] GEMM, [3] transport
   // (the layers enqueued before this one)
-  if ((s = exec_errors(L, L->errs_host))) return s;
-  const int plan_err = L->errs_host[0];
+  int32_t errs_now[8];
+  std::memcpy(errs_now, L->mirror_host->errs, sizeof(errs_now));
+  if ((s = exec_errors(L, errs_now))) return s;
+  const int plan_err = errs_now[0];
   if (sum.err || plan_err) {
     if (plan_err == DEV_CAPACITY || sum.err == DEV_CAPACITY)
       return fail(FERRYB_ECAPACITY, "missing experts exceed the total admission capacity");
@@ -521,10 +551,16 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   const uint32_t ready_value = (uint32_t)seq;
   // failure injection: copies that never raise their readiness flags
   const bool no_flags = (L->hooks & FERRYB_HOOK_NO_READY_FLAGS) != 0;
+  // readiness per fetch: ready[j] once the gate + up rows (the phase-1 tiles'
+  // operand) have landed, ready[E + j] once the whole row has; the layer's
+  // last fetch is copied in two parts so that its phase-1 tiles overlap the
+  // copy of its down rows
+  const int64_t split = 2 * (int64_t)c.hidden * c.intermediate * 2;
   auto fetch = [&](int first, int n) {
     if (no_flags) return ferryb_h2d_fetch(L->h2d, fslots.data() + first, fkeys.data() + first, n);
-    return ferryb_h2d_fetch_flagged(L->h2d, fslots.data() + first, fkeys.data() + first, n,
-                                    L->ready + first, ready_value);
+    return h2d_fetch_split_flagged(L->h2d, fslots.data() + first, fkeys.data() + first, n,
+                                   L->ready + first, L->ready + c.experts + first, ready_value, split,
+                                   first + n == sum.n_fetch_mine);
   };
   if (sum.n_fetch_mine > 0) {
     if (timing && (s = h2d_record_event(L->h2d, L->tev[6], 0))) return s;
@@ -550,7 +586,8 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   // 8 grouped SwiGLU (kernel 5), both phases per launch: the experts cached
   //   before this layer (no waits), then the fetched experts, whose tiles
   //   start as their readiness flags arrive
-  if ((s = swiglu_fused_launch(L->maps, L->groups, sum.n_hit, sum.n_hit, nullptr, 0, L->queue_dep,
+  if ((s = swiglu_fused_launch(L->maps, L->groups, sum.n_hit, sum.n_hit, nullptr, nullptr, 0,
+                               L->queue_dep,
                                L->route_w, L->act, L->expert_out, L->errs + 2, stream,
                                span_of(5), L->hook_wait_ns)))
     return s;
@@ -575,7 +612,9 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   }
   // with sync_fetch the stream has already waited for every copy: no flag waits
   if ((s = swiglu_fused_launch(L->maps, L->groups + sum.n_hit, sum.n_fetch_mine, 0,
-                               c.sync_fetch ? nullptr : L->ready, ready_value, L->queue_dep,
+                               c.sync_fetch ? nullptr : L->ready,
+                               c.sync_fetch ? nullptr : L->ready + c.experts, ready_value,
+                               L->queue_dep,
                                L->route_w, L->act, L->expert_out, L->errs + 2, stream, span_of(6),
                                L->hook_wait_ns)))
     return s;
@@ -741,8 +780,8 @@ extern "C" int ferryb_layer_get_stats(const ferryb_layer* L, ferryb_layer_stats*
 }
 
 extern "C" int ferryb_layer_last_summary(const ferryb_layer* L, ferryb_layout_summary* out) {
-  FB_CHECK_ARG(L && out && L->summary_host, "layer_last_summary: null argument");
-  *out = *L->summary_host;
+  FB_CHECK_ARG(L && out && L->mirror_host, "layer_last_summary: null argument");
+  *out = L->mirror_host->sum;
   return FERRYB_OK;
 }
 
@@ -754,7 +793,7 @@ extern "C" int ferryb_layer_reset_stats(ferryb_layer* L) {
 
 extern "C" int ferryb_layer_destroy(ferryb_layer* L) {
   if (!L) return FERRYB_OK;
-  if (L->summary_host) cudaFreeHost(L->summary_host);
+  if (L->mirror_host) cudaFreeHost(L->mirror_host);
   if (L->errs_host) cudaFreeHost(L->errs_host);
   if (L->summary_ev) cudaEventDestroy(L->summary_ev);
   for (auto e : L->tev_pool) cudaEventDestroy(e);

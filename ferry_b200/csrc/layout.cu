@@ -104,7 +104,7 @@ __device__ __forceinline__ int packet_ids(const TokenRoutes& r, int K, int peer,
 }
 
 __global__ void __launch_bounds__(kLayThreads, 1)
-    layout_kernel(const LayoutArgs a, unsigned long long* ts) {
+    layout_kernel(const LayoutArgs a, unsigned long long* ts, const SummaryMirror mirror) {
   __shared__ LaySmem sm;
   __shared__ int total_sh;
   const int tid = threadIdx.x;
@@ -330,6 +330,21 @@ __global__ void __launch_bounds__(kLayThreads, 1)
     if (tid == 0) a.summary->err = atomicAdd(a.err, 0);
   }
   __syncthreads();
+  if (mirror.sum && a.summary) {
+    // the finished summary and the error words straight into the host's
+    // mapped mirror (no copy command, no event), then the release of `seq`
+    // after one system-scope fence behind a CTA barrier
+    static_assert(sizeof(ferryb_layout_summary) % 16 == 0, "summary copied in 16-byte pieces");
+    const uint4* src = reinterpret_cast<const uint4*>(a.summary);
+    uint4* dst = reinterpret_cast<uint4*>(mirror.sum);
+    for (int i = tid; i < (int)(sizeof(ferryb_layout_summary) / 16); i += blockDim.x) dst[i] = src[i];
+    if (tid < 8) mirror.errs[tid] = atomicAdd(const_cast<int32_t*>(mirror.errs_dev) + tid, 0);
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence_system();
+      st_release_sys(reinterpret_cast<uint64_t*>(mirror.seq), mirror.value);
+    }
+  }
   span_end(ts);
 }
 
@@ -344,10 +359,11 @@ __global__ void layer_slots_kernel(const int32_t* slots_row, int capacity, int l
   }
 }
 
-int layout_launch(const LayoutArgs& a, cudaStream_t stream, unsigned long long* ts) {
+int layout_launch(const LayoutArgs& a, cudaStream_t stream, unsigned long long* ts,
+                  const SummaryMirror* mirror) {
   FB_CHECK_ARG(a.experts <= kMaxExpertsL && a.topk <= 16 && a.world >= 1,
                "layout: experts <= %d and topk <= 16 required", kMaxExpertsL);
-  layout_kernel<<<1, kLayThreads, 0, stream>>>(a, ts);
+  layout_kernel<<<1, kLayThreads, 0, stream>>>(a, ts, mirror ? *mirror : SummaryMirror{});
   FB_LAUNCH_CHECK();
   return FERRYB_OK;
 }
