@@ -75,6 +75,10 @@ def parse():
     p.add_argument('--ep-sweep', default='',
                    help='comma-separated tokens per rank: time the EP dispatch + combine of one Qwen3 '
                         'MoE layer with every expert cached (no fetches) instead of the decode bench')
+    p.add_argument('--gemm-compare', type=int, default=0, metavar='EXPERTS',
+                   help='time the routed-expert GEMM of one decode layer (64 tokens, top-8 of 128, '
+                        'Zipf(1.1), this many cached experts) through this library\'s execute_experts '
+                        '(the fused tcgen05 kernel) and the reference\'s (oracle/_ref, cuBLAS per expert)')
     p.add_argument('--full-model', choices=['qwen3', 'deepseek'],
                    help='BASELINE configs 2-4: the whole model (transformers 5.5, random weights) with '
                         'its MoE blocks on this runtime; reports TTFT, TPOT and decode tokens/s')
@@ -384,8 +388,8 @@ def run_ours(a, rank, world, local):
                 'achieved': round(achieved, 1), 'peak': hbm_gbs, 'unit': 'GB/s',
                 'frac': round(achieved / hbm_gbs, 4), 'peak_source': peak_kind,
                 'algorithmic_bytes_per_layer': st.hit_weight_bytes / layers_timed,
-                'traffic': (round(traffic['dram_bytes_per_hit_expert'] * st.hit_experts / max(1, st.layers))
-                            if traffic and st.hit_experts else None),
+                'traffic': (round(traffic['traffic_per_algorithmic_byte'] * st.hit_weight_bytes /
+                                  max(1, st.layers)) if traffic and st.hit_experts else None),
                 'traffic_note': (traffic.get('note') if traffic else 'no ncu capture committed')}
     if st.hit_gemm_kernel_launches:
         # the same launches on the device clock (earliest CTA start to latest CTA
@@ -852,6 +856,65 @@ def run_reference_gpu(a, rank, world, local):
                      'd2h_bytes_per_step': int(T * spec.hidden * 2), 'ms_per_step': e2e_ms / a.steps})
 
 
+def run_gemm_compare(a, local):
+    """Routed-expert GEMM of one decode layer, the same groups through both
+    execute_experts implementations: this library's (gather + the fused
+    tcgen05 kernel, ferryb_execute_experts) and the reference's compiled one
+    (ferry/csrc/expert_ops.cpp:16-45, cuBLAS per expert).  Each call is timed
+    with CUDA events around it on the current stream after a synchronisation,
+    as a caller sees it; the weights (> L2) are read from HBM every call."""
+    from ferry_b200 import expert_ops as ours
+    from ferry_b200.workload import zipf_bias
+    from oracle.build_ref import load_ref
+    ref = load_ref()
+    dev = torch.device('cuda', local)
+    spec = qwen3_spec(1)
+    H, I, E, K, T = spec.hidden, spec.intermediate, spec.experts, spec.topk, a.tokens
+    g = torch.Generator(device=dev).manual_seed(5)
+    cg = torch.Generator().manual_seed(5)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    gate = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    logits = (x.float() @ gate.float().t() + zipf_bias(E, 1.1, cg).to(dev)).to(torch.bfloat16)
+    probs = torch.softmax(logits, -1, dtype=torch.float32)
+    w, sel = torch.topk(probs, K, -1)
+    w = (w / w.sum(-1, keepdim=True)).to(torch.bfloat16)
+    active = torch.unique(sel).tolist()[:a.gemm_compare]
+    cache = (torch.randn(len(active), spec.expert_elements, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    slots, rows, cols = [], [], []
+    for i, e in enumerate(active):
+        r, c = (sel == e).nonzero(as_tuple=True)
+        slots.append(i); rows.append(r.contiguous()); cols.append(c.contiguous())
+    routes = sum(int(r.numel()) for r in rows)
+
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(n):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(); fn(); e1.record(); e1.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts)
+
+    args = (cache, x, w, slots, rows, cols, H, I)
+    got = ours.execute_experts(*args)
+    res = {'metric': 'routed-expert GEMM of one decode layer (us per call, median)', 'experts': len(active),
+           'routes': routes, 'tokens': T, 'weight_bytes': len(active) * spec.expert_bytes,
+           'ours_us': round(timed(lambda: ours.execute_experts(*args), a.steps), 1)}
+    if ref is None:
+        res['reference'] = 'unavailable: oracle/_ref not built'
+        return res
+    want = ref.execute_experts(*args)
+    err = max((p.float() - q.float()).abs().max().item() for p, q in zip(got, want))
+    res['reference_us'] = round(timed(lambda: ref.execute_experts(*args), a.steps), 1)
+    res['speedup'] = round(res['reference_us'] / res['ours_us'], 2)
+    res['ours_gbs'] = round(res['weight_bytes'] / (res['ours_us'] * 1e-6) / 1e9, 1)
+    res['reference_gbs'] = round(res['weight_bytes'] / (res['reference_us'] * 1e-6) / 1e9, 1)
+    res['max_abs_diff'] = err
+    return res
+
+
 def main():
     a = parse()
     if a.impl == 'reference':
@@ -863,7 +926,9 @@ def main():
         return 0
     rank, world, local = init_dist(a.gpus)
     try:
-        if a.full_model:
+        if a.gemm_compare:
+            result = run_gemm_compare(a, local)
+        elif a.full_model:
             result = run_full_model(a, rank, world, local)
         elif a.impl == 'reference-gpu':
             result = run_reference_gpu(a, rank, world, local)

@@ -852,9 +852,10 @@ int swiglu_grouped(const void* cache, int64_t cache_slots, const GemmGroup* grou
 
 static int64_t align256(int64_t b) { return (b + 255) & ~int64_t(255); }
 
-// Workspace carve-up of ferryb_execute_experts.
+// Workspace carve-up of ferryb_execute_experts (and of the no-allocation
+// variant, which uses everything up to `err`).
 struct ExecWs {
-  int64_t x, act, w, groups, err, total;
+  int64_t x, act, w, groups, err, queue, total;
 };
 static ExecWs exec_ws(int64_t total, int64_t n_groups, int64_t hidden, int64_t inter) {
   ExecWs w{};
@@ -863,7 +864,8 @@ static ExecWs exec_ws(int64_t total, int64_t n_groups, int64_t hidden, int64_t i
   w.w = w.act + align256(total * inter * 2);
   w.groups = w.w + align256(total * 2);
   w.err = w.groups + align256(n_groups * (int64_t)sizeof(GemmGroup));
-  w.total = w.err + 256;
+  w.queue = w.err + 256;  // the fused kernel's claim/done/dependency counters
+  w.total = w.queue + align256((2 + n_groups) * 4);
   return w;
 }
 
@@ -917,8 +919,16 @@ extern "C" int ferryb_execute_experts(const void* cache, int64_t cache_slots, co
       static_cast<const __nv_bfloat16*>(routing_weights), topk, rows, cols, total, hidden, x, w,
       err);
   FB_LAUNCH_CHECK();
-  int s = swiglu_grouped(cache, cache_slots, groups, static_cast<int>(n_groups), total, x, w, act,
-                         static_cast<__nv_bfloat16*>(out), hidden, intermediate, err, stream);
+  // both phases of every group in one launch of the fused kernel (the layer
+  // executor's kernel; all groups cached, no readiness waits)
+  GemmMaps maps;
+  int s = make_gemm_maps(&maps, cache, cache_slots, x, act, total, hidden, intermediate);
+  if (s) return s;
+  int* queue = reinterpret_cast<int*>(base + ws.queue);
+  FB_CUDA(cudaMemsetAsync(queue, 0, (2 + n_groups) * sizeof(int), stream));
+  s = swiglu_fused_launch(maps, groups, static_cast<int>(n_groups), static_cast<int>(n_groups),
+                          nullptr, nullptr, 0, queue, w, act, static_cast<__nv_bfloat16*>(out), err,
+                          stream);
   if (s) return s;
   // Synchronous status check of the device error word (compat API semantics:
   // errors surface at the call, like the reference's TORCH_CHECKs).
@@ -992,12 +1002,14 @@ extern "C" int ferryb_execute_experts_noalloc(const void* cache, int64_t cache_s
   if (total == 0) return FERRYB_OK;
   FB_CHECK_ARG(cache && input && routing_weights && rows && cols && out, "null pointer");
   const ExecWs ws = exec_ws(total, n_groups, hidden, intermediate);
-  if (ws.total > kNoAllocScratchBytes)
+  // the two-launch GEMM needs the carve-up up to the error word's 256 bytes
+  const int64_t need = ws.queue;
+  if (need > kNoAllocScratchBytes)
     return fail(FERRYB_EINVAL,
                 "execute_experts_noalloc: %lld routes of hidden %lld / intermediate %lld need "
                 "%lld bytes of scratch, above the fixed %lld; use ferryb_execute_experts with a "
                 "workspace",
-                (long long)total, (long long)hidden, (long long)intermediate, (long long)ws.total,
+                (long long)total, (long long)hidden, (long long)intermediate, (long long)need,
                 (long long)kNoAllocScratchBytes);
   void* scratch = nullptr;
   int s = noalloc_scratch(&scratch);
