@@ -340,6 +340,7 @@ def run_ours(a, rank, world, local):
     call('ferryb_layer_collect_timing', ex.h)
     call('ferryb_layer_reset_stats', ex.h)
     copies0 = rt.h2d.copies
+    fetch0 = rt.fetches_per_rank.copy()  # every rank's fetches (the replicated plan's counts)
     barrier(world)
     sampler = ClockSampler() if rank == 0 else None
     if sampler:
@@ -412,12 +413,22 @@ def run_ours(a, rank, world, local):
     t_flops = flops / (bf16_tflops * 1e12)
     t_roof = max(t_host, t_nvl, t_flops)
     t_meas = ms_local / 1e3
-    # the job's layer is as slow as its slowest rank: both terms max over ranks
-    t_roof_job = max_over_ranks(t_roof, world)
+    # host-link term of the job: ranks that share a host path move their
+    # fetched bytes at that path's measured aggregate bandwidth
+    alone = [b_alone] * world
+    if world > 1:
+        dist.all_gather_object(alone, b_alone)
+    f_job = (rt.fetches_per_rank - fetch0).astype(np.float64)
+    t_host_job, limiting = host_link_time(topo, topo_note, f_job * expert_bytes, alone, b_host, world)
+    t_roof_job = max(t_host_job, max_over_ranks(t_nvl, world), max_over_ranks(t_flops, world))
+    # the job's layer is as slow as its slowest rank
     t_meas_job = max_over_ranks(t_meas, world)
-    layer_roofline = {'bound': ['host_link', 'nvlink', 'tensor'][int(np.argmax([t_host, t_nvl, t_flops]))],
+    terms = [t_host_job, max_over_ranks(t_nvl, world), max_over_ranks(t_flops, world)]
+    layer_roofline = {'bound': ['host_link', 'nvlink', 'tensor'][int(np.argmax(terms))],
                       'frac': round(t_roof_job / t_meas_job, 4) if t_meas_job > 0 else None,
-                      'frac_rank0': round(t_roof / t_meas, 4) if t_meas > 0 else None,
+                      'host_link_limiting': limiting,
+                      'fetches_per_layer_by_rank': [round(x / max(1, st.layers), 2) for x in f_job],
+                      'frac_rank0_own_link': round(t_roof / t_meas, 4) if t_meas > 0 else None,
                       'host_link_gbs_measured': round(b_host, 2),
                       'host_link_gbs_alone': round(b_alone, 2),
                       'host_link_note': 'measured with every rank copying at once (shared PCIe '
@@ -513,6 +524,32 @@ def parity_gate(spec, pool, caps, a, topo, capture, rank, world):
     if not res['ok']:
         print(f'bench parity gate failed: {res}', file=sys.stderr)
     return res
+
+
+def host_link_time(topo, topo_note, fetch_bytes, alone_gbs, all_gbs, world):
+    """Lower bound on the time the job's expert copies take: every group of
+    ranks that shares a host path moves the bytes its ranks fetch at that
+    group's aggregate bandwidth.  With a profiled topology the groups are its
+    domains (every subset of the ranks, each with the bandwidth measured while
+    that subset copies at once, as the quota LUT uses them); without one, each
+    rank alone at its own measured link and all ranks together at the
+    bandwidth measured while every rank copies.  fetch_bytes: per rank.
+    Returns (seconds, the limiting group)."""
+    groups = []
+    if topo_note != 'uniform':  # profiled on this box, or a topology file
+        for mask, sec in zip(topo.masks, topo.seconds):
+            groups.append((int(mask), (1 << 30) / float(sec)))
+    else:
+        groups = [(1 << r, alone_gbs[r] * 1e9) for r in range(world)]
+        if world > 1:
+            groups.append(((1 << world) - 1, all_gbs * 1e9 * world))
+    best, lim = 0.0, None
+    for mask, bw in groups:
+        b = sum(fetch_bytes[r] for r in range(world) if mask >> r & 1)
+        t = b / bw
+        if t > best:
+            best, lim = t, {'ranks': [r for r in range(world) if mask >> r & 1], 'gbs': round(bw / 1e9, 2)}
+    return best, lim
 
 
 def self_check(result):

@@ -2,6 +2,8 @@
 the expert row layout, and the synthetic workload's router bias."""
 import math
 
+import numpy as np
+
 import pytest
 import torch
 
@@ -204,3 +206,23 @@ def test_topology_for_run(tmp_path, monkeypatch):
         topology_for_run(str(path), spec, 0, 2)
     with pytest.raises(ValueError):
         topology_for_run('auto', spec, 0, 4)
+
+
+def test_bench_host_link_time_model():
+    """The job's host-link term: the slowest group of ranks that shares a host
+    path (profiled domains), or each rank alone plus all ranks together."""
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+
+    class _Topo:
+        masks = np.array([1, 2, 4, 8, 3, 12, 15])
+        seconds = np.array([1 / 50.0] * 4 + [1 / 50.0, 1 / 100.0, 1 / 110.0])
+    fb = np.array([4.0, 4.0, 1.0, 1.0]) * 2 ** 30
+    t, lim = bench.host_link_time(_Topo, 'auto: profiled', fb, [50.0] * 4, 27.5, 4)
+    assert lim['ranks'] == [0, 1] and abs(t - 8.0 / 50.0) < 1e-9  # ranks 0-1 share 50 GiB/s
+    t, lim = bench.host_link_time(_Topo, 'uniform', fb, [60.0] * 4, 27.5, 4)
+    assert lim['ranks'] == [0, 1, 2, 3] and abs(t - 10 * 2 ** 30 / 110e9) < 1e-9
+    t, lim = bench.host_link_time(_Topo, 'uniform', fb[:1], [50.0], 50.0, 1)
+    assert lim['ranks'] == [0] and abs(t - 4 * 2 ** 30 / 50e9) < 1e-9
