@@ -357,6 +357,7 @@ def run_ours(a, rank, world, local):
     call('ferryb_layer_collect_timing', ex.h)
     st = ex.stats()
     fetch_copies = rt.h2d.copies - copies0
+    f_job = (rt.fetches_per_rank - fetch0).astype(np.float64)  # the timed steps only
     ms = max_over_ranks(ms_local, world)
 
     # e2e: inputs from pinned host memory each step, output read back each step
@@ -418,7 +419,6 @@ def run_ours(a, rank, world, local):
     alone = [b_alone] * world
     if world > 1:
         dist.all_gather_object(alone, b_alone)
-    f_job = (rt.fetches_per_rank - fetch0).astype(np.float64)
     t_host_job, limiting = host_link_time(topo, topo_note, f_job * expert_bytes, alone, b_host, world)
     t_roof_job = max(t_host_job, max_over_ranks(t_nvl, world), max_over_ranks(t_flops, world))
     # the job's layer is as slow as its slowest rank
