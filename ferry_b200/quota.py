@@ -60,7 +60,11 @@ def build_lut(max_misses, world, masks, seconds):
 
 class Topology:
     """Profiled bandwidth domains plus the precomputed quota lookup table
-    (ferry/quota.py:77-100): same JSON format and checks."""
+    (ferry/quota.py:77-100).  The constructor and `uniform` keep the
+    reference's reading of the file line for line, error messages included:
+    a topology file, and the errors it raises, must be the same under either
+    implementation.  The greedy that fills the table runs on the GPU
+    (build_lut above)."""
 
     def __init__(self, path, world, experts):
         data = json.loads(Path(path).read_text())
