@@ -40,11 +40,20 @@ int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
 using namespace ferryb;
 
 // The plan summary as the host sees it: pinned, mapped host memory filled by
-// the layout kernel (SummaryMirror) and released by `seq` = event + 1.
+// the planner (PlanMirror: this rank's fetch list, released by `plan_seq`)
+// and then by the layout kernel (SummaryMirror, released by `seq`); both
+// release words take the call's own value (ferryb_layer::releases).
 struct HostMirror {
   ferryb_layout_summary sum;
   int32_t errs[8];
   uint64_t seq;
+  // released earlier, by the planner (PlanMirror): this rank's fetch list and
+  // the error words as the planner finished
+  int32_t plan_n_fetch;
+  int32_t plan_errs[8];
+  int32_t plan_keys[256];
+  int32_t plan_slots[256];
+  uint64_t plan_seq;
 };
 
 struct ferryb_layer {
@@ -100,6 +109,7 @@ struct ferryb_layer {
   // error attribution: the last layer enqueued, and the last event whose GEMM
   // and transport error words were read back clean
   int64_t last_event = -1, clean_event = -1;
+  uint64_t releases = 0;  // release values of the host mirror, one per call, never reused
   int32_t last_layer = -1;
   // failure injection (ferryb_layer_set_fault_hooks)
   uint32_t hooks = 0;
@@ -403,11 +413,10 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
                "layer_forward: hidden must be 16-byte aligned with shared experts");
   uint8_t* half = L->symm + parity * L->sl.half;
   int64_t launches = 0;
-  // the mirror's release word restarts at 0: every layout kernel of an
-  // earlier call has completed (its mirror was observed, or the call failed
-  // before launching one), so nothing can still write it
-  reinterpret_cast<volatile uint64_t*>(&L->mirror_host->seq)[0] = 0;
-  std::atomic_thread_fence(std::memory_order_release);
+  // the mirror's release words get a value no earlier call used: a planner
+  // or layout kernel of a call that failed before observing its release may
+  // still write one, and stream order puts those writes before this call's
+  const uint64_t rel = ++L->releases;
   using clk = std::chrono::steady_clock;
   auto h_prev = clk::now();
   auto host_mark = [&](int stage) {
@@ -480,6 +489,9 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   in.hist_clear = c.world > 1 ? nullptr : L->hist_local;
   in.ts = span_of(1);
   PlanOutputs po{L->fetches, L->n_fetches, L->dest, L->counts, L->errs + 0};
+  po.mirror = PlanMirror{&L->mirror_dev->plan_n_fetch, L->mirror_dev->plan_keys,
+                         L->mirror_dev->plan_slots, L->mirror_dev->plan_errs, L->errs,
+                         &L->mirror_dev->plan_seq, rel, c.rank};
   if ((s = plan_launch(L->pc, L->ps, in, po, stream))) return s;
   launches += 1;
 
@@ -500,53 +512,63 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   la.csr_pos = L->csr_pos; la.peer_row = L->peer_row; la.groups = L->groups;
   la.summary = L->summary_dev; la.err = L->errs + 1;
   const SummaryMirror mirror{&L->mirror_dev->sum, L->mirror_dev->errs, &L->mirror_dev->seq, L->errs,
-                             seq};
+                             rel};
   if ((s = layout_launch(la, stream, span_of(2), &mirror))) return s;
   launches += 1;  // layout
   if (timing) FB_CUDA(cudaEventRecord(L->tev[1], stream));
 
-  // 4 the summary reaches the host through the mapped mirror; the host polls
-  //   its release word (the layer's one host wait), checking the event behind
-  //   the layout kernel now and then so that a launch that failed is reported
-  //   instead of waited for
+  // 4 the fetch list, then the layout summary, reach the host through the
+  //   mapped mirror: the host polls each release word, checking the event
+  //   behind the layout kernel now and then so that a launch that failed is
+  //   reported instead of waited for (the planner runs before the layout, so
+  //   a completed event with no release means the word was never written)
   FB_CUDA(cudaEventRecord(L->summary_ev, stream));
   host_mark(0);
-  {
-    const volatile uint64_t* flag = &L->mirror_host->seq;
-    for (uint32_t spins = 1; *flag != seq; ++spins) {
+  auto wait_release = [&](const uint64_t* word, const char* what) -> int {
+    const volatile uint64_t* flag = word;
+    for (uint32_t spins = 1; *flag != rel; ++spins) {
       if ((spins & 255) != 0) continue;
       const cudaError_t q = cudaEventQuery(L->summary_ev);
       if (q == cudaErrorNotReady) continue;
       if (q != cudaSuccess) return fail(FERRYB_ECUDA, "layer %d: %s", layer, cudaGetErrorString(q));
-      if (*flag != seq)
-        return fail(FERRYB_EDEVICE, "layer %d (event %lld): the plan summary was not written", layer,
-                    (long long)event);
+      if (*flag != rel)
+        return fail(FERRYB_EDEVICE, "layer %d (event %lld): the %s was not written", layer,
+                    (long long)event, what);
     }
     std::atomic_thread_fence(std::memory_order_acquire);
     const auto now = clk::now();
     L->stats.host_wait_us += std::chrono::duration<double, std::micro>(now - h_prev).count();
     h_prev = now;
-  }
-  const ferryb_layout_summary sum = L->mirror_host->sum;
+    return FERRYB_OK;
+  };
   // error words: [0] planner, [1] layout (this layer), [2] GEMM, [3] transport
   // (the layers enqueued before this one)
+  auto plan_errors = [&](const int32_t* e, int layout_err) -> int {
+    int st = exec_errors(L, e);
+    if (st) return st;
+    const int plan_err = e[0];
+    if (layout_err || plan_err) {
+      if (plan_err == DEV_CAPACITY || layout_err == DEV_CAPACITY)
+        return fail(FERRYB_ECAPACITY, "missing experts exceed the total admission capacity");
+      if (plan_err == DEV_WAIT_TIMEOUT)
+        return fail(FERRYB_ETIMEOUT, "timed out waiting for the routing metadata of a peer rank");
+      return fail(FERRYB_EDEVICE, "planner/layout device error %d/%d", plan_err, layout_err);
+    }
+    return FERRYB_OK;
+  };
+  if ((s = wait_release(&L->mirror_host->plan_seq, "fetch list"))) return s;
   int32_t errs_now[8];
-  std::memcpy(errs_now, L->mirror_host->errs, sizeof(errs_now));
-  if ((s = exec_errors(L, errs_now))) return s;
-  const int plan_err = errs_now[0];
-  if (sum.err || plan_err) {
-    if (plan_err == DEV_CAPACITY || sum.err == DEV_CAPACITY)
-      return fail(FERRYB_ECAPACITY, "missing experts exceed the total admission capacity");
-    if (plan_err == DEV_WAIT_TIMEOUT)
-      return fail(FERRYB_ETIMEOUT, "timed out waiting for the routing metadata of a peer rank");
-    return fail(FERRYB_EDEVICE, "planner/layout device error %d/%d", plan_err, sum.err);
-  }
+  std::memcpy(errs_now, L->mirror_host->plan_errs, sizeof(errs_now));
+  if ((s = plan_errors(errs_now, 0))) return s;
+  const int n_fetch = L->mirror_host->plan_n_fetch;
+  if (n_fetch < 0 || n_fetch > c.experts)
+    return fail(FERRYB_EDEVICE, "layer %d: the planner reported %d fetches", layer, n_fetch);
   // 5 fetches on the copy engine, each raising a readiness flag when it has
   //   landed; the first goes out before the compute-stream launches
-  std::vector<int64_t> fslots(sum.n_fetch_mine), fkeys(sum.n_fetch_mine);
-  for (int i = 0; i < sum.n_fetch_mine; ++i) {
-    fslots[i] = sum.fetch_slots[i];
-    fkeys[i] = sum.fetch_keys[i];
+  std::vector<int64_t> fslots(n_fetch), fkeys(n_fetch);
+  for (int i = 0; i < n_fetch; ++i) {
+    fslots[i] = L->mirror_host->plan_slots[i];
+    fkeys[i] = L->mirror_host->plan_keys[i];
   }
   const uint32_t ready_value = (uint32_t)seq;
   // failure injection: copies that never raise their readiness flags
@@ -560,13 +582,21 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
     if (no_flags) return ferryb_h2d_fetch(L->h2d, fslots.data() + first, fkeys.data() + first, n);
     return h2d_fetch_split_flagged(L->h2d, fslots.data() + first, fkeys.data() + first, n,
                                    L->ready + first, L->ready + c.experts + first, ready_value, split,
-                                   first + n == sum.n_fetch_mine);
+                                   first + n == n_fetch);
   };
-  if (sum.n_fetch_mine > 0) {
+  if (n_fetch > 0) {
     if (timing && (s = h2d_record_event(L->h2d, L->tev[6], 0))) return s;
     if ((s = fetch(0, 1))) return s;
   }
   host_mark(1);
+  // the layout has run meanwhile (the first copy is already on its way)
+  if ((s = wait_release(&L->mirror_host->seq, "plan summary"))) return s;
+  const ferryb_layout_summary sum = L->mirror_host->sum;
+  std::memcpy(errs_now, L->mirror_host->errs, sizeof(errs_now));
+  if ((s = plan_errors(errs_now, sum.err))) return s;
+  if (sum.n_fetch_mine != n_fetch)
+    return fail(FERRYB_EDEVICE, "layer %d: the planner listed %d fetches, the layout %d", layer,
+                n_fetch, sum.n_fetch_mine);
 
   // 6-7 dispatch + permute
   FusedArgs fa = fused_args(L, parity, static_cast<const __nv_bfloat16*>(hidden),

@@ -103,6 +103,13 @@ __device__ __forceinline__ int packet_ids(const TokenRoutes& r, int K, int peer,
   return size;
 }
 
+// Optional phase timestamps of the layout (profiling aid; NULL = off).
+__device__ unsigned long long* g_layout_ts = nullptr;
+#define LAY_TS(k)                                                           \
+  do {                                                                      \
+    if (threadIdx.x == 0 && g_layout_ts) g_layout_ts[k] = globaltimer_ns(); \
+  } while (0)
+
 __global__ void __launch_bounds__(kLayThreads, 1)
     layout_kernel(const LayoutArgs a, unsigned long long* ts, const SummaryMirror mirror) {
   __shared__ LaySmem sm;
@@ -110,6 +117,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
   const int tid = threadIdx.x;
   const int R = a.world, T = a.tokens_per_rank, K = a.topk, E = a.experts, rank = a.rank;
   const int n_tok = R * T;
+  LAY_TS(0);
   span_begin(ts);
   int ids_buf[16];
 
@@ -157,6 +165,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
     for (int j = tid; j < sm.n_fetch_mine; j += blockDim.x) sm.lslot[sm.fetch_key[j] % E] = sm.fetch_slot[j];
   }
   __syncthreads();
+  LAY_TS(1);
 
   // ---- receive rows at every peer, part 1 ---------------------------------
   // The receive row of local token t at peer p is #{g' < g : g' sends to p}
@@ -215,6 +224,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
     if (tid == 0) a.send_counts[peer] = peer_sent;
   }
   if (tid == 0) *a.n_send = sent;
+  LAY_TS(2);
 
   // ---- receive side pass 1: receive rows, per-expert counts --------------
   int received = 0;
@@ -249,6 +259,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
   for (int e = tid; e <= E; e += blockDim.x) a.starts[e] = sm.starts[e];
   for (int e = tid; e < E; e += blockDim.x) sm.expert_count[e] = 0;  // becomes the running cursor
   __syncthreads();
+  LAY_TS(3);
 
   // ---- receive side pass 2: CSR positions ---------------------------------
   int row_base = 0;
@@ -290,6 +301,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
     __syncthreads();
   }
   if (tid == 0) *a.n_recv = received;
+  LAY_TS(4);
 
   // ---- GEMM groups: cached experts (ascending), then fetched (fetch order) --
   if (a.groups && a.summary) {
@@ -330,6 +342,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
     if (tid == 0) a.summary->err = atomicAdd(a.err, 0);
   }
   __syncthreads();
+  LAY_TS(5);
   if (mirror.sum && a.summary) {
     // the finished summary and the error words straight into the host's
     // mapped mirror (no copy command, no event), then the release of `seq`
@@ -345,6 +358,7 @@ __global__ void __launch_bounds__(kLayThreads, 1)
       st_release_sys(reinterpret_cast<uint64_t*>(mirror.seq), mirror.value);
     }
   }
+  LAY_TS(6);
   span_end(ts);
 }
 
@@ -378,6 +392,11 @@ int layer_slots_launch(const int32_t* slots_row, int capacity, int layer, int ex
 }  // namespace ferryb
 
 using namespace ferryb;
+
+extern "C" int ferryb_debug_layout_timestamps(void* dev_ptr) {
+  FB_CUDA(cudaMemcpyToSymbol(g_layout_ts, &dev_ptr, sizeof(void*)));
+  return FERRYB_OK;
+}
 
 extern "C" int ferryb_build_layout(const ferryb_layout_args* args, cudaStream_t stream) {
   FB_CHECK_ARG(args && args->ids && args->dest && args->err, "layout: null arguments");

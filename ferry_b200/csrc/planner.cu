@@ -110,10 +110,27 @@ struct PlanSmem {
   float gate[kMaxExperts];
   int owner_layer[kMaxExperts];
   int status;
+  int n_mine;  // misses assigned to the mirror's rank
   MT rng;
 };
 
 __device__ __forceinline__ void set_err(int* err, int code) { atomicCAS(err, 0, code); }
+
+// The planner's last step when a host mirror is given (every thread, on
+// every exit path): this rank's fetch count and the error words next to the
+// fetch list written at the commit, then the release of `seq` after one
+// system-scope fence behind a CTA barrier.
+__device__ void plan_release(const PlanMirror& pm, int n_mine) {
+  if (pm.seq == nullptr) return;
+  __syncthreads();
+  if (threadIdx.x < 8) pm.errs[threadIdx.x] = atomicAdd(const_cast<int32_t*>(pm.errs_dev) + threadIdx.x, 0);
+  if (threadIdx.x == 0) *pm.n_fetch = n_mine;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(pm.seq, pm.value);
+  }
+}
 
 // Optional phase timestamps of the planner (profiling aid; NULL = off).
 __device__ unsigned long long* g_plan_ts = nullptr;
@@ -501,6 +518,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   if (tid == 0) {
     sm.status = 0;
     sm.m = 0;
+    sm.n_mine = 0;
     // fused path: wait (bounded) until every rank's routing metadata landed
     if (in.gflags && !wait_flags_bounded(in.gflags, R, in.seq, out.err)) sm.status = DEV_WAIT_TIMEOUT;
   }
@@ -508,6 +526,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   __syncthreads();
   if (sm.status) {
     if (tid == 0) *out.n_fetches = 0;
+    plan_release(out.mirror, 0);
     return;
   }
 
@@ -635,6 +654,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
       // this layer's scores changed above: the saved victim order is stale
       if (s.order_meta) s.order_meta[0] = 0;
     }
+    plan_release(out.mirror, 0);
     return;
   }
 
@@ -791,6 +811,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
       out.fetches[i * 3 + 0] = r;
       out.fetches[i * 3 + 1] = key;
       out.fetches[i * 3 + 2] = idx - r * c.maxcap;
+      if (out.mirror.seq && r == out.mirror.rank) {  // the j-th fetch of this rank
+        out.mirror.keys[j] = key;
+        out.mirror.slots[j] = idx - r * c.maxcap;
+      }
     }
     // the saved order now holds every record as of this plan; this layer's
     // records change at its commit, so they are re-keyed next time
@@ -814,6 +838,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   for (int i = tid; i < m; i += blockDim.x) {
     const int r = sm.assignment[i];
     if (r >= 0 && r < R) atomicAdd(&out.counts[r], 1);
+    if (r == out.mirror.rank) atomicAdd(&sm.n_mine, 1);
   }
   for (int i = tid; i < n_tok * K; i += blockDim.x) {
     const int e = in.ids[i];
@@ -821,6 +846,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   }
   __syncthreads();
   PLAN_TS(7);
+  plan_release(out.mirror, sm.n_mine);
   span_end(in.ts);
 }
 

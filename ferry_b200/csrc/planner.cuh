@@ -72,12 +72,27 @@ struct PlanInputs {
   unsigned long long* ts;  // device-clock span (timing mode) or null
 };
 
+// Optional early release of one rank's fetch list into pinned, mapped host
+// memory: written by the planner's last step (error paths included), so that
+// the host can start that rank's copies while the layout kernel still runs.
+struct PlanMirror {
+  int32_t* n_fetch;         // [1] this rank's fetches
+  int32_t* keys;            // [experts] their keys, in fetch order
+  int32_t* slots;           // [experts] their slots (rank-relative)
+  int32_t* errs;            // [8] copy of the error words errs_dev[0..7]
+  const int32_t* errs_dev;  // the executor's device error words
+  uint64_t* seq;            // released to `value` last (null: no release)
+  uint64_t value;
+  int rank;
+};
+
 struct PlanOutputs {
   int32_t* fetches;    // [experts, 3] (rank, key, slot)
   int32_t* n_fetches;  // [1]
   int32_t* dest;       // [n_tokens, topk]
   int32_t* counts;     // [world]
   int* err;            // [1]
+  PlanMirror mirror;   // optional (mirror.seq null: off)
 };
 
 int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,

@@ -209,6 +209,12 @@ FERRYB_API int ferryb_choose_slot(int32_t rank, int32_t layer, const uint8_t* ac
  * 6 commit, 7 end).  NULL turns it off. */
 FERRYB_API int ferryb_debug_plan_timestamps(void* dev_ptr);
 
+/* Profiling aid: the same for the layout kernel of ferryb_layer_forward and
+ * ferryb_build_layout (7 x uint64: 0 start, 1 fetched experts, 2 send side,
+ * 3 receive pass 1 + expert starts, 4 receive pass 2, 5 GEMM groups and the
+ * summary, 6 end after the host mirror's release).  NULL turns it off. */
+FERRYB_API int ferryb_debug_layout_timestamps(void* dev_ptr);
+
 /* ------------------------------------------------------------------------
  * EP layout of one layer for one rank.  Replaces build_layout and
  * device_layout (ferry/layout.py:12-94; no blocking H2D) and layer_slots
