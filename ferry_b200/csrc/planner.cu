@@ -41,7 +41,6 @@ constexpr int kPlanThreads = 1024;
 constexpr int kMaxIncremental = 4096;
 constexpr int kIncPer = kMaxIncremental / kPlanThreads;
 constexpr int kRankSort = kPlanThreads;  // dirty records sorted by counting below this
-constexpr int kPlanWarps = kPlanThreads / 32;
 
 struct SlotRec {
   uint64_t k0;  // rank << 56 | class << 48 | score bits (eligible) / 0
@@ -156,46 +155,26 @@ __device__ void history_step(const PlanConfig& c, const PlanState& s, const Plan
   uint8_t* ring = s.ring + (size_t)L * W * K;
   float* ring_p = s.ring_p ? s.ring_p + (size_t)L * W * E : nullptr;
   // The ring positions written by this update: replace (n >= W) or append.
-  const int h0 = *head;
-  __syncthreads();
-  if (n_rows >= W) {
-    // rows[-W:] -> slots 0..W-1
-    for (int i = threadIdx.x; i < W * (ring_p ? E : K); i += blockDim.x) {
-      const int slot = ring_p ? i / E : i / K;
-      const int row = n_rows - W + slot;
-      if (ring_p) {
-        ring_p[i] = in.prob_rows[(size_t)row * E + i % E];
-      } else {
-        const int r = row / tail, t = T - tail + row % tail;
-        ring[i] = in.ids[((size_t)r * T + t) * K + i % K];
-      }
-    }
-  } else {
-    for (int i = threadIdx.x; i < n_rows * (ring_p ? E : K); i += blockDim.x) {
-      const int row = ring_p ? i / E : i / K;
-      const int slot = (h0 + row) % W;
-      if (ring_p) {
-        ring_p[(size_t)slot * E + i % E] = in.prob_rows[(size_t)row * E + i % E];
-      } else {
-        const int r = row / tail, t = T - tail + row % tail;
-        ring[(size_t)slot * K + i % K] = in.ids[((size_t)r * T + t) * K + i % K];
-      }
-    }
-  }
+  // Head and count are read once, before any thread writes them; after the
+  // update the slots [0, filled) hold rows (the ring never has holes).
+  const int h0 = *head, c0 = *count;
+  const int filled = n_rows >= W ? W : min(W, c0 + n_rows);
+  const int n = max(1, filled);
   __syncthreads();
   if (threadIdx.x == 0) {
-    if (n_rows >= W) {
-      *count = W;
-      *head = 0;
-    } else {
-      *head = (h0 + n_rows) % W;
-      *count = min(W, *count + n_rows);
-    }
+    *head = n_rows >= W ? 0 : (h0 + n_rows) % W;
+    *count = filled;
   }
-  __syncthreads();
-  const int filled = *count;  // slots [0, filled) hold rows (the ring never has holes)
-  const int n = max(1, filled);
   if (ring_p) {
+    if (n_rows >= W) {
+      // rows[-W:] -> slots 0..W-1
+      for (int i = threadIdx.x; i < W * E; i += blockDim.x)
+        ring_p[i] = in.prob_rows[(size_t)(n_rows - W + i / E) * E + i % E];
+    } else {
+      for (int i = threadIdx.x; i < n_rows * E; i += blockDim.x)
+        ring_p[(size_t)((h0 + i / E) % W) * E + i % E] = in.prob_rows[i];
+    }
+    __syncthreads();
     // float64 sum over slots in slot order; loads batched 8 ahead
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
       double acc = 0.0;
@@ -211,16 +190,53 @@ __device__ void history_step(const PlanConfig& c, const PlanState& s, const Plan
       gate_out[e] = __double2float_rn(__ddiv_rn(acc, (double)n));
     }
   } else {
-    // a row counts once for each distinct id it holds (rows are 0/1 indicators)
+    // frequency rows, one thread per ring slot: the slot's row is this
+    // update's (copied in here) or the one it held; a row counts once for
+    // each distinct id it holds (rows are 0/1 indicators)
+    constexpr int kRowMax = 16;  // rows up to this long are held in registers
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt_scratch[e] = 0;
     __syncthreads();
-    for (int slot = threadIdx.x; slot < filled; slot += blockDim.x) {
-      const uint8_t* row = ring + (size_t)slot * K;
-      for (int k = 0; k < K; ++k) {
-        const int e = row[k];
-        bool dup = e >= E;
-        for (int q = 0; q < k; ++q) dup |= row[q] == e;
-        if (!dup) atomicAdd(&cnt_scratch[e], 1);
+    for (int slot = threadIdx.x; slot < W; slot += blockDim.x) {
+      int row = -1;  // the row of this update that lands in `slot`
+      if (n_rows >= W) {
+        row = n_rows - W + slot;
+      } else if ((slot - h0 + W) % W < n_rows) {
+        row = (slot - h0 + W) % W;
+      }
+      uint8_t* dst = ring + (size_t)slot * K;
+      const uint8_t* src = dst;
+      if (row >= 0) src = in.ids + ((size_t)(row / tail) * T + (T - tail + row % tail)) * K;
+      if (K <= kRowMax) {
+        int v[kRowMax];
+#pragma unroll
+        for (int k = 0; k < kRowMax; ++k) v[k] = k < K ? src[k] : 0;
+        if (row >= 0) {
+#pragma unroll
+          for (int k = 0; k < kRowMax; ++k)
+            if (k < K) dst[k] = (uint8_t)v[k];
+        }
+        if (slot < filled) {
+#pragma unroll
+          for (int k = 0; k < kRowMax; ++k) {
+            if (k < K) {
+              bool dup = v[k] >= E;
+#pragma unroll
+              for (int q = 0; q < kRowMax; ++q) dup |= q < k && v[q] == v[k];
+              if (!dup) atomicAdd(&cnt_scratch[v[k]], 1);
+            }
+          }
+        }
+      } else {
+        if (row >= 0)
+          for (int k = 0; k < K; ++k) dst[k] = src[k];
+        if (slot < filled) {
+          for (int k = 0; k < K; ++k) {
+            const int e = dst[k];
+            bool dup = e >= E;
+            for (int q = 0; q < k; ++q) dup |= dst[q] == e;
+            if (!dup) atomicAdd(&cnt_scratch[e], 1);
+          }
+        }
       }
     }
     __syncthreads();
@@ -712,63 +728,78 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
       uint64_t* dk1 = dk0 + n;
       uint32_t* dsl = reinterpret_cast<uint32_t*>(dk1 + n);
       const int64_t* changed = s.order_meta + 1;  // layers planned since the order was saved
-      // each thread's saved entries i = tid + q * blockDim.x, in registers
+      // each thread's saved entries i = tid * nq + q (consecutive), in
+      // registers; a dirty entry is re-keyed at once (its key is in hand)
       const int nq = (n + (int)blockDim.x - 1) / (int)blockDim.x;  // <= kIncPer
       uint64_t e0[kIncPer], e1[kIncPer];
       uint32_t es[kIncPer];
-      bool dirty[kIncPer];
+      bool dirty[kIncPer], live[kIncPer];
+      int n_clean = 0;
 #pragma unroll
       for (int q = 0; q < kIncPer; ++q) {
-        const int i = tid + q * (int)blockDim.x;
+        const int i = tid * nq + q;
         dirty[q] = false;
-        if (q < nq && i < n) {
+        live[q] = q < nq && i < n;
+        if (live[q]) {
           e0[q] = s.ord_k0[i]; e1[q] = s.ord_k1[i]; es[q] = s.ord_sl[i];
           if (es[q] != 0xffffffffu) {
-            const int key = s.slots[es[q]];
+            const int idx = (int)es[q];
+            const int key = s.slots[idx];
             const int cls = (int)((e0[q] >> 48) & 0xff);
             const int saved_key = cls == 0 ? -1 : (int)(e1[q] & 0xffffff);
             const int kl = key >= 0 ? key / E : -1;
             dirty[q] = key != saved_key ||
                        (key >= 0 && (kl == L || ((changed[kl >> 6] >> (kl & 63)) & 1)));
+            if (dirty[q]) slot_record(c, s, sm.active, idx / c.maxcap, idx, key, L, e0[q], e1[q]);
           }
+          n_clean += !dirty[q];
         }
       }
-      // stable compaction of the clean entries (saved order kept) into k0/k1/sl;
-      // the dirty ones are re-keyed into dk0/dk1/dsl (entry i has i - cpos
-      // dirty entries before it)
-      int clean_base = 0;
+      PLAN_TS(8);
+      // stable compaction: the clean entries (saved order kept) into k0/k1/sl,
+      // the dirty records into dk0/dk1/dsl (one block scan of the per-thread
+      // clean counts; the entries before a thread's first are tid * nq)
+      int cpos = plan_block_scan(n_clean, sm.warp_sum, &sm.scan_total);
+      int dpos = tid * nq - cpos;
+      const int nc = sm.scan_total, nd = n - nc;
 #pragma unroll
       for (int q = 0; q < kIncPer; ++q) {
-        if (q >= nq) break;
-        const int i = tid + q * (int)blockDim.x;
-        const bool live = i < n;
-        const int cpos = clean_base + plan_block_scan(live && !dirty[q], sm.warp_sum, &sm.scan_total);
-        clean_base += sm.scan_total;
-        const int dpos = i - cpos;
-        if (live && !dirty[q]) { k0[cpos] = e0[q]; k1[cpos] = e1[q]; sl[cpos] = es[q]; }
-        if (live && dirty[q]) {
-          const int idx = (int)es[q];
-          const int r = idx / c.maxcap;
-          uint64_t a0, a1;
-          slot_record(c, s, sm.active, r, idx, s.slots[idx], L, a0, a1);
-          dk0[dpos] = a0; dk1[dpos] = a1; dsl[dpos] = es[q];
+        if (!live[q]) continue;
+        if (dirty[q]) {
+          dk0[dpos] = e0[q]; dk1[dpos] = e1[q]; dsl[dpos] = es[q];
+          ++dpos;
+        } else {
+          k0[cpos] = e0[q]; k1[cpos] = e1[q]; sl[cpos] = es[q];
+          ++cpos;
         }
       }
-      const int nc = clean_base, nd = n - clean_base;
       __syncthreads();
+      PLAN_TS(9);
+      if (threadIdx.x == 0 && g_plan_ts) g_plan_ts[12] = (unsigned long long)nd;
       if (nd <= kRankSort) {
-        // up to one dirty record per thread: each one's place is the number
-        // of dirty records below it (their keys are unique); all reads are
-        // done before the barrier, so the records move in place
+        // each dirty record's place is the number of dirty records below it
+        // (their keys are unique).  Lane l of warp w holds record w + 32 * l;
+        // the warp's lanes split the comparisons of each of its records.  All
+        // reads are done before the barrier, so the records move in place.
+        const int nw = (int)(blockDim.x >> 5);
+        const int own = warp + nw * lane;
         uint64_t a0 = 0, a1 = 0;
         uint32_t ax = 0;
         int place = 0;
-        if (tid < nd) {
-          a0 = dk0[tid]; a1 = dk1[tid]; ax = dsl[tid];
-          for (int k = 0; k < nd; ++k) place += dk0[k] < a0 || (dk0[k] == a0 && dk1[k] < a1);
+        if (own < nd) { a0 = dk0[own]; a1 = dk1[own]; ax = dsl[own]; }
+        for (int l = 0; warp + nw * l < nd; ++l) {
+          const uint64_t b0 = __shfl_sync(0xffffffffu, a0, l);
+          const uint64_t b1 = __shfl_sync(0xffffffffu, a1, l);
+          int below = 0;
+          for (int k = lane; k < nd; k += 32) {
+            const uint64_t x0 = dk0[k], x1 = dk1[k];
+            below += (int)((x0 < b0) | ((x0 == b0) & (x1 < b1)));
+          }
+          below = __reduce_add_sync(0xffffffffu, below);
+          if (lane == l) place = below;
         }
         __syncthreads();
-        if (tid < nd) { dk0[place] = a0; dk1[place] = a1; dsl[place] = ax; }
+        if (own < nd) { dk0[place] = a0; dk1[place] = a1; dsl[place] = ax; }
         __syncthreads();
       } else {
         int dn = 64;
@@ -777,6 +808,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
         __syncthreads();
         sort_records(dk0, dk1, dsl, dn);
       }
+      PLAN_TS(10);
       // merge: a clean record's position is its index plus the dirty records
       // below it, and the other way round (keys of real records are unique)
       for (int i = tid; i < nc; i += blockDim.x) {
@@ -788,6 +820,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
         s.ord_k0[pos] = dk0[j]; s.ord_k1[pos] = dk1[j]; s.ord_sl[pos] = dsl[j];
       }
       __syncthreads();
+      PLAN_TS(11);
       o0 = s.ord_k0; osl = s.ord_sl;
     }
     __syncthreads();

@@ -203,10 +203,12 @@ FERRYB_API int ferryb_choose_slot(int32_t rank, int32_t layer, const uint8_t* ac
                                   const int64_t* last, const float* scores, int32_t experts,
                                   int64_t* result, ferryb_stream_t stream);
 
-/* Profiling aid: when dev_ptr (device, 8 x uint64) is not NULL the planner
+/* Profiling aid: when dev_ptr (device, 16 x uint64) is not NULL the planner
  * writes %globaltimer stamps of its phases there (0 start, 1 gate scores,
  * 2 demand/misses/capacity, 3 quota + assignment, 4 victim records, 5 sort,
- * 6 commit, 7 end).  NULL turns it off. */
+ * 6 commit, 7 end; in the incremental victim order 8 saved entries read and
+ * classified, 9 clean/dirty split, 10 dirty records sorted, 11 merged) and
+ * at 12 the number of dirty records.  NULL turns it off. */
 FERRYB_API int ferryb_debug_plan_timestamps(void* dev_ptr);
 
 /* Profiling aid: the same for the layout kernel of ferryb_layer_forward and

@@ -183,7 +183,9 @@ def test_fused_layout_outputs(world, tokens, experts, topk):
 
 
 @pytest.mark.parametrize('world,caps_per_rank,layers,experts,topk,tokens', [
-    (1, 300, 6, 64, 6, 48), (2, 90, 5, 64, 4, 40), (4, 40, 4, 128, 8, 24)])
+    (1, 300, 6, 64, 6, 48), (2, 90, 5, 64, 4, 40), (4, 40, 4, 128, 8, 24),
+    # 2048 and 4096 slot records: two and four saved entries per thread
+    (1, 1500, 32, 64, 6, 48), (2, 1100, 24, 128, 8, 32)])
 def test_saved_victim_order_matches_full_sort(world, caps_per_rank, layers, experts, topk, tokens):
     """The incrementally maintained victim order against a controller that
     sorts every slot at every plan (its saved order cleared before each call):
