@@ -439,7 +439,7 @@ def run_ours(a, rank, world, local):
                       'nvlink_bytes_per_layer': nvl_bytes / max(1, st.layers),
                       'rank': rank}
     split = {name: round(st.phase_us[i] / layers_timed, 1) for i, name in enumerate(
-        ['route_plan_layout', 'summary_dispatch_permute', 'gemm_cached', 'gemm_fetched_incl_wait',
+        ['route_plan', 'layout_summary_dispatch_permute', 'gemm_cached', 'gemm_fetched_incl_wait',
          'combine'])}
     result = {
         'metric': METRIC, 'value': world * T * a.steps / (ms / 1e3), 'unit': 'tokens/s',
@@ -457,7 +457,7 @@ def run_ours(a, rank, world, local):
             ['route_plan_layout', 'first_fetch', 'dispatch_permute', 'gemm_cached', 'gemm_fetched_fetches',
              'combine'])},
         'copy_lane_us_per_layer': {name: round(st.copy_us[i] / layers_timed, 1) for i, name in enumerate(
-            ['layout_end_to_first_copy', 'copies', 'last_copy_to_combine_end'])},
+            ['plan_end_to_first_copy', 'copies', 'last_copy_to_combine_end'])},
         # per-MoE-layer split on the device clock: each kernel's span (earliest
         # CTA start to latest CTA end), summed over the layers whose spans were
         # recorded (the first 4096 timed layers) and divided by their number

@@ -288,6 +288,15 @@ __device__ __forceinline__ void span_end(unsigned long long* ts) {
   if (ts && threadIdx.x == 0) atomicMax(ts + 1, (unsigned long long)globaltimer_ns());
 }
 
+// Programmatic dependent launch: a primary kernel lets the next kernel of its
+// stream (launched with programmatic stream serialisation) start early; that
+// kernel waits for the primary's completion and memory before it reads the
+// primary's outputs.  Both are no-ops when the launches are not paired so.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -32,11 +32,6 @@
 #include "router.cuh"
 #include "transport.cuh"
 
-namespace ferryb {
-int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
-                const PlanOutputs& out, cudaStream_t stream);
-}
-
 using namespace ferryb;
 
 // The plan summary as the host sees it: pinned, mapped host memory filled by
@@ -492,8 +487,9 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
   po.mirror = PlanMirror{&L->mirror_dev->plan_n_fetch, L->mirror_dev->plan_keys,
                          L->mirror_dev->plan_slots, L->mirror_dev->plan_errs, L->errs,
                          &L->mirror_dev->plan_seq, rel, c.rank};
-  if ((s = plan_launch(L->pc, L->ps, in, po, stream))) return s;
+  if ((s = plan_launch(L->pc, L->ps, in, po, stream, /*after_router=*/true))) return s;
   launches += 1;
+  if (timing) FB_CUDA(cudaEventRecord(L->tev[1], stream));  // the critical path ends here
 
   // 3 layer slots + layout
   ferryb_layout_args la{};
@@ -515,7 +511,6 @@ static int layer_forward(ferryb_layer* L, int64_t event, int32_t layer, const vo
                              rel};
   if ((s = layout_launch(la, stream, span_of(2), &mirror))) return s;
   launches += 1;  // layout
-  if (timing) FB_CUDA(cudaEventRecord(L->tev[1], stream));
 
   // 4 the fetch list, then the layout summary, reach the host through the
   //   mapped mirror: the host polls each release word, checking the event

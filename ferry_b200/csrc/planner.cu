@@ -529,16 +529,20 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
   SlotRec* recs = reinterpret_cast<SlotRec*>(dsm + c.sort_offset);       // [sort_n]
   int64_t* greedy_load = reinterpret_cast<int64_t*>(dsm + c.greedy_offset);  // [G]
 
-  PLAN_TS(0);
-  span_begin(in.ts);
   if (tid == 0) {
     sm.status = 0;
     sm.m = 0;
     sm.n_mine = 0;
-    // fused path: wait (bounded) until every rank's routing metadata landed
-    if (in.gflags && !wait_flags_bounded(in.gflags, R, in.seq, out.err)) sm.status = DEV_WAIT_TIMEOUT;
   }
   for (int i = tid; i < E * R; i += blockDim.x) demand[i] = 0;
+  // launched early behind the router (programmatic dependent launch): its
+  // ids and histogram are read only after this
+  pdl_wait();
+  PLAN_TS(0);
+  span_begin(in.ts);
+  // fused path: wait (bounded) until every rank's routing metadata landed
+  if (tid == 0 && in.gflags && !wait_flags_bounded(in.gflags, R, in.seq, out.err))
+    sm.status = DEV_WAIT_TIMEOUT;
   __syncthreads();
   if (sm.status) {
     if (tid == 0) *out.n_fetches = 0;
@@ -1003,14 +1007,26 @@ __global__ void choose_slot_kernel(int rank, int layer, const uint8_t* active, c
 
 // ---------------------------------------------------------------------------
 int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
-                const PlanOutputs& out, cudaStream_t stream) {
+                const PlanOutputs& out, cudaStream_t stream, bool after_router) {
   const size_t dyn = c.dyn_smem;
   static int configured_bytes = -1;
   if ((int)dyn > configured_bytes) {
     FB_CUDA(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
     configured_bytes = (int)dyn;
   }
-  plan_kernel<<<1, kPlanThreads, dyn, stream>>>(c, s, in, out);
+  // behind the router kernel: a programmatic dependent launch, so that the
+  // planner's launch overlaps the router (the kernel waits for its outputs)
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kPlanThreads);
+  cfg.dynamicSmemBytes = dyn;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = after_router ? 1 : 0;
+  FB_CUDA(cudaLaunchKernelEx(&cfg, plan_kernel, c, s, in, out));
   FB_LAUNCH_CHECK();
   return FERRYB_OK;
 }

@@ -96,7 +96,7 @@ struct PlanOutputs {
 };
 
 int plan_launch(const PlanConfig& c, const PlanState& s, const PlanInputs& in,
-                const PlanOutputs& out, cudaStream_t stream);
+                const PlanOutputs& out, cudaStream_t stream, bool after_router = false);
 // Dynamic shared memory of the planner: demand, the slot records, greedy
 // loads and (room permitting) the dirty-record buffer of the incremental
 // victim order (*dirty_off = 0 when there is no room).

@@ -36,6 +36,7 @@ __global__ void __launch_bounds__(kRouterThreads)
   const int H = a.hdim, E = a.experts, K = a.topk;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const __nv_bfloat16* x = a.hidden + (size_t)t * H;
+  pdl_launch_dependents();  // the planner may take its SM and wait there
   span_begin(a.ts);
 
   if (a.mode == 2) {

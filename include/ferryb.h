@@ -403,19 +403,21 @@ typedef struct ferryb_layer_stats {
   int64_t timed_layers;      /* layers whose phase times are in phase_us */
   double host_wait_us;       /* host time blocked on the plan summary */
   double phase_us[5];        /* timing mode (CUDA events, collected by
-                                ferryb_layer_collect_timing): route+plan+layout,
-                                summary+dispatch+permute, cached-expert GEMM,
-                                fetched-expert GEMMs (incl. copy waits), combine */
+                                ferryb_layer_collect_timing): route+plan,
+                                layout+summary+dispatch+permute, cached-expert
+                                GEMM, fetched-expert GEMMs (incl. copy waits),
+                                combine */
   double host_us[6];         /* host time spent issuing each stage (steady
                                 clock, every call): router+planner+layout,
                                 first fetch after the summary arrives,
                                 dispatch+permute, cached-expert GEMM,
                                 fetched-expert GEMM + remaining fetches,
                                 combine + counters */
-  double copy_us[3];         /* timing mode, layers with fetches: layout end ->
-                                first copy start (the host round trip), first
-                                copy start -> last copy end, last copy end ->
-                                combine end (the compute tail) */
+  double copy_us[3];         /* timing mode, layers with fetches: planner end ->
+                                first copy start (the fetch list's release and
+                                the host round trip), first copy start -> last
+                                copy end, last copy end -> combine end (the
+                                compute tail) */
   double hit_gemm_kernel_us; /* timing mode: cached-expert GEMM launches timed on the device
                                 clock (earliest CTA start to latest CTA end), summed */
   int64_t hit_gemm_kernel_launches;
