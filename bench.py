@@ -96,6 +96,10 @@ def parse():
                    help='write, for every layer run (warm-up and timed, in order), its cached and '
                         'fetched expert counts as JSON: the expert-GEMM launches an ncu capture '
                         'of this command lists, with their algorithmic bytes')
+    p.add_argument('--phase-stamps', action='store_true',
+                   help='after timing, run one more step with the planner\'s and the layout\'s '
+                        'device-clock phase stamps on (a host sync after every layer) and report '
+                        'the median of each phase')
     p.add_argument('--sync-fetch', action='store_true',
                    help='issue each layer\'s copies before its fetched-expert GEMM and wait on '
                         'them from the stream (for profilers that serialise GPU work)')
@@ -475,12 +479,70 @@ def run_ours(a, rank, world, local):
             'note': 'per layer in run order; the expert GEMM launches once for the cached experts '
                     '(if any) and once for the fetched experts (if any)',
             'layers': launch_log}))
+    if a.phase_stamps:
+        result['phase_stamps_ns'] = phase_stamps(rt, wl, spec, inputs[a.warmup], dev)
     result['parity'] = parity_gate(spec, wl.pool, caps, a, topo, capture, rank, world)
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         result['cpu_baseline'] = cpu_baseline(spec, wl, caps, T, a.cpu_seconds, a, host)
     result['self_check'] = self_check(result)
     rt.close()
     return result
+
+
+PLAN_PHASES = ['gate_history', 'demand_capacity', 'quota_assignment', 'victim_positions',
+               'victim_order', 'commit', 'tail']
+ORDER_STEPS = ['read_classify', 'clean_dirty_split', 'dirty_sort', 'merge']
+LAYOUT_PHASES = ['fetched_experts', 'send_side', 'receive_pass1_starts', 'receive_pass2',
+                 'groups_summary', 'host_mirror']
+
+
+def phase_stamps(rt, wl, spec, inp, dev):
+    """One more decode step, after timing, with the planner's and the layout's
+    %globaltimer phase stamps on (ferryb_debug_plan_timestamps /
+    ferryb_debug_layout_timestamps) and a host sync after every layer: the
+    median over the step's layers of each phase, in ns."""
+    from ferry_b200._lib import call, ptr
+    pts = torch.zeros(16, dtype=torch.int64, device=dev)
+    lts = torch.zeros(8, dtype=torch.int64, device=dev)
+    rts = torch.zeros(4, dtype=torch.int64, device=dev)
+    plan, order, lay, rout = [], [], [], []
+    call('ferryb_debug_plan_timestamps', ptr(pts))
+    call('ferryb_debug_layout_timestamps', ptr(lts))
+    call('ferryb_debug_router_timestamps', ptr(rts))
+    try:
+        prev = None
+        for l in range(spec.layers):
+            pts.zero_()
+            lts.zero_()
+            rts.zero_()
+            rts[0] = torch.iinfo(torch.int64).max
+            h = inp[l] if prev is None else inp[l] + prev
+            prev = rt.forward(l, h, wl.gate[l], wl.bias[l])
+            torch.cuda.synchronize()
+            t, u, v = pts.cpu().numpy(), lts.cpu().numpy(), rts.cpu().numpy()
+            if np.all(v[1:] > 0) and np.all(np.diff(v) >= 0):
+                rout.append(np.append(np.diff(v), t[0] - v[3]))
+            if np.all(t[:8] > 0) and np.all(np.diff(t[:8]) >= 0):  # a layer with fetches
+                plan.append(np.diff(t[:8]))
+                if np.all(t[8:12] > 0):  # the saved victim order was used
+                    order.append(np.append(np.diff(np.concatenate([t[4:5], t[8:12]])), t[12]))
+            if np.all(u[:7] > 0) and np.all(np.diff(u[:7]) >= 0):
+                lay.append(np.diff(u[:7]))
+    finally:
+        call('ferryb_debug_plan_timestamps', None)
+        call('ferryb_debug_layout_timestamps', None)
+        call('ferryb_debug_router_timestamps', None)
+
+    def med(rows, names):
+        return {n: float(np.median([r[i] for r in rows])) for i, n in enumerate(names)} if rows else None
+    return {'layers': {'router': len(rout), 'planner': len(plan), 'victim_order_saved': len(order),
+                       'layout': len(lay)},
+            'router': med(rout, ['logits', 'softmax_topk', 'gather_writes', 'router_end_to_planner_start']),
+            'planner': med(plan, PLAN_PHASES), 'victim_order_steps': med(order, ORDER_STEPS + ['dirty_records']),
+            'layout': med(lay, LAYOUT_PHASES),
+            'note': 'device-clock stamps of one step run after timing with a host sync per layer: '
+                    'no copies in flight while the router and planner run; the layer\'s first '
+                    'copy is in flight while the layout runs (its host-mirror fence waits on the link)'}
 
 
 def parity_gate(spec, pool, caps, a, topo, capture, rank, world):

@@ -127,6 +127,7 @@ SIGNATURES = {
     'ferryb_layer_collect_timing': (_i32, [_vp]),
     'ferryb_debug_plan_timestamps': (_i32, [_vp]),
     'ferryb_debug_layout_timestamps': (_i32, [_vp]),
+    'ferryb_debug_router_timestamps': (_i32, [_vp]),
     'ferryb_layer_destroy': (_i32, [_vp]),
 }
 

@@ -24,6 +24,18 @@ namespace ferryb {
 
 constexpr int kRouterThreads = 1024;  // 32 warps: a few experts per warp
 
+// Optional phase stamps of the router (profiling aid; NULL = off), over all
+// CTAs: [0] earliest start, [1] latest end of the logits, [2] of the softmax
+// and top-k, [3] latest end.
+__device__ unsigned long long* g_router_ts = nullptr;
+#define ROUTER_TS(k)                                                              \
+  do {                                                                            \
+    if (threadIdx.x == 0 && g_router_ts) {                                        \
+      if ((k) == 0) atomicMin(g_router_ts, (unsigned long long)globaltimer_ns()); \
+      else atomicMax(g_router_ts + (k), (unsigned long long)globaltimer_ns());    \
+    }                                                                             \
+  } while (0)
+
 __global__ void __launch_bounds__(kRouterThreads)
     router_kernel(const RouterArgs a, uint64_t seq) {
   __shared__ float logit[kMaxRouterExperts];
@@ -37,6 +49,7 @@ __global__ void __launch_bounds__(kRouterThreads)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const __nv_bfloat16* x = a.hidden + (size_t)t * H;
   pdl_launch_dependents();  // the planner may take its SM and wait there
+  ROUTER_TS(0);
   span_begin(a.ts);
 
   if (a.mode == 2) {
@@ -102,6 +115,7 @@ __global__ void __launch_bounds__(kRouterThreads)
   }
   __syncthreads();
 
+  ROUTER_TS(1);
   // ---- softmax (float32), top-k and weights: warp 0 alone --------------
   // lane l holds logits l, l + 32, ... (E <= kMaxRouterExperts)
   if (warp == 0) {
@@ -183,6 +197,7 @@ __global__ void __launch_bounds__(kRouterThreads)
   __syncthreads();
   }  // mode 0 / 1
 
+  ROUTER_TS(2);
   // ---- all-gather of the ids: this token's k bytes into every rank ----
   if (threadIdx.x < a.world * K) {
     const int p = threadIdx.x / K, j = threadIdx.x % K;
@@ -191,6 +206,7 @@ __global__ void __launch_bounds__(kRouterThreads)
   }
   // With one rank the planner, next on the stream, reads the histogram and
   // the ids this kernel wrote (the kernel boundary orders them): no flags.
+  ROUTER_TS(3);
   span_end(a.ts);
   if (a.world == 1) return;
   // ---- last CTA: histogram + flags ----
@@ -235,3 +251,8 @@ int router_launch(const RouterArgs& a, uint64_t seq, cudaStream_t stream) {
 }
 
 }  // namespace ferryb
+
+extern "C" int ferryb_debug_router_timestamps(void* dev_ptr) {
+  FB_CUDA(cudaMemcpyToSymbol(ferryb::g_router_ts, &dev_ptr, sizeof(void*)));
+  return FERRYB_OK;
+}

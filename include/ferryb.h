@@ -217,6 +217,12 @@ FERRYB_API int ferryb_debug_plan_timestamps(void* dev_ptr);
  * summary, 6 end after the host mirror's release).  NULL turns it off. */
 FERRYB_API int ferryb_debug_layout_timestamps(void* dev_ptr);
 
+/* Profiling aid: the router kernel of ferryb_layer_forward over all its CTAs
+ * (4 x uint64, set to {UINT64_MAX, 0, 0, 0} before the launch): 0 earliest
+ * start, 1 latest end of the logits, 2 latest end of the softmax and top-k,
+ * 3 latest end.  NULL turns it off. */
+FERRYB_API int ferryb_debug_router_timestamps(void* dev_ptr);
+
 /* ------------------------------------------------------------------------
  * EP layout of one layer for one rank.  Replaces build_layout and
  * device_layout (ferry/layout.py:12-94; no blocking H2D) and layer_slots
