@@ -5,8 +5,9 @@ OffloadRuntime keeps the reference's constructor, reset/execute/close and
 counters (ferry/runtime.py:34-93).  execute() runs the whole layer through
 libferryb's fused executor (ferryb_layer_execute): P2P all-gather of the
 routing metadata, the device planner, the device layout, copy-engine
-fetches, P2P dispatch, the tcgen05 grouped SwiGLU and the P2P combine, with
-one host wait per layer.  forward() additionally moves the MoE hook's router
+fetches, P2P dispatch, the tcgen05 grouped SwiGLU and the P2P combine; the
+host only polls mapped memory (the planner's fetch list, then the layout's
+summary), with no copy or stream sync per layer.  forward() additionally moves the MoE hook's router
 into kernel 1 (ferryb_layer_forward).
 
 Ranks and world size come from torch.distributed when it is initialised

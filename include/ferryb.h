@@ -372,8 +372,10 @@ FERRYB_API int ferryb_symm_wait(const void* local_base, int64_t flag_offset, int
  * The fused per-layer executor.  Replaces OffloadRuntime.execute
  * (ferry/runtime.py:64-89) together with the MoE hook's router
  * (ferry/model.py:137-148).  One call runs, on this rank: router + all-gather
- * (kernel 1), planner (kernel 2), layout, one host wait for the ~2 KB plan
- * summary, this rank's fetches (kernel 3), P2P dispatch (kernel 4), the
+ * (kernel 1), planner (kernel 2, which publishes this rank's fetch list to the
+ * host), this rank's fetches (kernel 3, the first issued while the layout
+ * runs), layout (whose ~2 KB plan summary the host polls before the
+ * dispatch), P2P dispatch (kernel 4), the
  * grouped SwiGLU (kernel 5, cached experts first, then each fetched expert as
  * soon as its copy lands) and the combine (kernel 4).  The workspace and the
  * symmetric buffer are caller-allocated (sizes from the *_bytes queries); the
