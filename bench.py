@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Decode throughput of FERRY's per-MoE-layer hot path on B200.
 
-Workload (multi-GPU: config 4's scaling): Qwen3-30B-A3B
+Workload (the benchmark's config 1; config 4 scales it over GPUs): Qwen3-30B-A3B
 MoE layers (hidden 2048, 128 experts top-8 with renormalised softmax,
 moe_intermediate 768, SwiGLU, bf16, random init N(0, 0.02)) stacked as the
 model's 48 MoE layers, decode batch of 64 tokens per GPU, Zipf(1.1) router
@@ -80,7 +80,7 @@ def parse():
                         'Zipf(1.1), this many cached experts) through this library\'s execute_experts '
                         '(the fused tcgen05 kernel) and the reference\'s (oracle/_ref, cuBLAS per expert)')
     p.add_argument('--full-model', choices=['qwen3', 'deepseek'],
-                   help='BASELINE configs 2-4: the whole model (transformers 5.5, random weights) with '
+                   help='the benchmark\'s configs 2-4: the whole model (transformers 5.5, random weights) with '
                         'its MoE blocks on this runtime; reports TTFT, TPOT and decode tokens/s')
     p.add_argument('--batch', type=int, default=64, help='--full-model: sequences per GPU')
     p.add_argument('--prompt-len', type=int, default=1024, help='--full-model: input tokens')
@@ -634,7 +634,7 @@ def self_check(result):
 
 # ---------------------------------------------------------------------------
 def run_ep_sweep(a, rank, world, local):
-    """BASELINE config 4's EP sweep: one Qwen3 MoE layer (top-8 of 128, Zipf
+    """The benchmark's config-4 EP sweep: one Qwen3 MoE layer (top-8 of 128, Zipf
     1.1 router bias), T tokens per rank, the 128 experts spread over the ranks'
     caches (128 slots in all) so that, once warm, no step fetches: the step is
     router + planner + layout + P2P dispatch + grouped GEMM + P2P combine.
@@ -746,7 +746,7 @@ def _reference_gpu_model_run(cfg, a, rank, world, dev, layers):
 
 
 def run_full_model(a, rank, world, local):
-    """BASELINE configs 2-4 through ferry_b200.harness: seeded random prompts
+    """The benchmark's configs 2-4 through ferry_b200.harness: seeded random prompts
     (uniform token ids), one warm-up generation, then one timed generation.
     With --impl reference-gpu the same model runs the reference's hooks over
     the composed reference GPU runtime instead."""

@@ -2,7 +2,7 @@
 
 ModelSpec and read_spec keep the reference's fields and rules (MoE layer
 selection, expert row size, the global cache budget split).  QWEN3_30B_A3B
-and DEEPSEEK_V2_LITE are the configs of BASELINE.json (no checkpoint files
+and DEEPSEEK_V2_LITE are the benchmark's two models (no checkpoint files
 are available here; weights are random-initialised by ferry_b200.workload).
 """
 import json
@@ -74,7 +74,7 @@ def read_spec(model_path):
     return spec_from_config(json.loads((Path(model_path) / 'config.json').read_text()))
 
 
-# BASELINE.json configs 1/3/4 (Qwen3-30B-A3B) and 0/2 (DeepSeek-V2-Lite).
+# The benchmark's configs 1/3/4 (Qwen3-30B-A3B) and 0/2 (DeepSeek-V2-Lite).
 # (public model configs; the full-model harness builds them with random weights)
 QWEN3_30B_A3B = dict(model_type='qwen3_moe', num_hidden_layers=48, num_experts=128,
                      num_experts_per_tok=8, hidden_size=2048, moe_intermediate_size=768,

@@ -1,4 +1,4 @@
-"""Seeded synthetic workloads with the shapes of BASELINE.json's configs.
+"""Seeded synthetic workloads with the shapes of the benchmark's configs.
 
 No checkpoints or datasets are available, so (as the configs prescribe):
   * weights are random-init N(0, 0.02) in bf16: router gates [E, H] per MoE

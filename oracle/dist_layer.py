@@ -6,8 +6,8 @@ the uint8 ids (ferry/metadata.py:70-76), plans identically (oracle planner),
 builds its own layout, all-to-alls its packets (ferry/transport.py:17-29),
 runs its cached experts (weights read from the pool as the cache would hold
 them), reduces per packet, all-to-alls the partials back and scatters them
-(ferry/transport.py:31-38).  Config 0 of BASELINE.json runs this at
-world size 4.
+(ferry/transport.py:31-38).  The benchmark's config 0 (a DeepSeek-V2-Lite
+layer on CPU) runs this at world size 4.
 """
 import numpy as np
 import torch

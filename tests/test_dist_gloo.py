@@ -1,6 +1,6 @@
 """Multi-process CPU tests of the N > 1 path over gloo (no GPU).
 
-a DeepSeek-V2-Lite-shaped MoE layer (hidden 2048, 64
+The benchmark's config 0: a DeepSeek-V2-Lite-shaped MoE layer (hidden 2048, 64
 experts top-6, intermediate 1408) run by 4 gloo ranks with 16 tokens each for
 8 consecutive steps, through the reference's distributed flow restated in
 oracle/dist_layer.py; every rank's output must match what the single-process
@@ -90,7 +90,7 @@ def _run(world, shape, caps, steps, T, port):
 
 
 def test_config0_world4_gloo():
-    """DSV2-Lite layer, 4 gloo ranks x 16 tokens, 8 steps,
+    """The benchmark's config 0: DSV2-Lite layer, 4 gloo ranks x 16 tokens, 8 steps,
     global 30 % cache of a 2-layer slice (38 slots -> 10/10/9/9)."""
     _run(4, (2, 64, 6, 2048, 1408), [10, 10, 9, 9], 8, 16, 29651)
 
