@@ -226,3 +226,49 @@ def test_bench_host_link_time_model():
     assert lim['ranks'] == [0, 1, 2, 3] and abs(t - 10 * 2 ** 30 / 110e9) < 1e-9
     t, lim = bench.host_link_time(_Topo, 'uniform', fb[:1], [50.0], 50.0, 1)
     assert lim['ranks'] == [0] and abs(t - 4 * 2 ** 30 / 50e9) < 1e-9
+
+
+def test_bench_phase_stamps_medians(monkeypatch):
+    """bench.phase_stamps turns the kernels' stamp buffers into per-phase
+    medians: layers whose planner had no fetch (its victim stamps unset) or
+    that did not use the saved victim order are left out of those medians."""
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+    import ferry_b200._lib as fl
+    bufs = {}
+    monkeypatch.setattr(fl, 'ptr', lambda t: t)
+    monkeypatch.setattr(fl, 'call', lambda name, t: bufs.__setitem__(name, t))
+    monkeypatch.setattr(torch.cuda, 'synchronize', lambda *a: None)
+
+    class _Spec:
+        layers = 4
+
+    class _Wl:
+        gate = bias = [None] * 4
+
+    class _Rt:
+        def forward(self, l, h, g, b):
+            p = bufs['ferryb_debug_plan_timestamps']
+            lay = bufs['ferryb_debug_layout_timestamps']
+            r = bufs['ferryb_debug_router_timestamps']
+            r[:] = torch.tensor([100, 110, 120, 121])
+            p[:8] = 130 + torch.tensor([0, 4, 8, 10, 12, 22, 23, 24]) * (l + 1)
+            if l == 1:
+                p[4] = p[5] = 0  # no fetch: the victim stamps stay unset
+            if l != 2:
+                p[8:13] = torch.tensor([int(p[4]) + 3, int(p[4]) + 4, int(p[4]) + 6, int(p[4]) + 9, 80])
+            lay[:7] = 500 + torch.arange(7) * 2
+            return torch.zeros(1)
+
+    out = bench.phase_stamps(_Rt(), _Wl(), _Spec(), torch.zeros(4, 1), 'cpu')
+    assert out['layers'] == {'router': 4, 'planner': 3, 'victim_order_saved': 2, 'layout': 4}
+    assert out['router'] == {'logits': 10.0, 'softmax_topk': 10.0, 'gather_writes': 1.0,
+                             'router_end_to_planner_start': np.median([9 + 0, 9, 9, 9])}
+    # planner layers 0, 2, 3 (scales 1, 3, 4): gate history 4 * scale -> median 12
+    assert out['planner']['gate_history'] == 12.0 and out['planner']['victim_order'] == 30.0
+    assert out['victim_order_steps'] == {'read_classify': 3.0, 'clean_dirty_split': 1.0,
+                                         'dirty_sort': 2.0, 'merge': 3.0, 'dirty_records': 80.0}
+    assert out['layout']['receive_pass2'] == 2.0 and len(out['layout']) == 6
+    assert all(v is None for v in bufs.values())  # the hooks are switched off again
