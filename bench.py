@@ -82,6 +82,9 @@ def parse():
     p.add_argument('--full-model', choices=['qwen3', 'deepseek'],
                    help='the benchmark\'s configs 2-4: the whole model (transformers 5.5, random weights) with '
                         'its MoE blocks on this runtime; reports TTFT, TPOT and decode tokens/s')
+    p.add_argument('--checkpoint', default='',
+                   help='--full-model: a local checkpoint directory (config.json + safetensors) '
+                        'to load instead of random weights')
     p.add_argument('--batch', type=int, default=64, help='--full-model: sequences per GPU')
     p.add_argument('--prompt-len', type=int, default=1024, help='--full-model: input tokens')
     p.add_argument('--new-tokens', type=int, default=64, help='--full-model: greedy output tokens')
@@ -760,13 +763,15 @@ def run_full_model(a, rank, world, local):
     else:
         model, rt, tokens, m = run(cfg, batch=a.batch, prompt_len=a.prompt_len, new_tokens=a.new_tokens,
                                    cache_ratio=a.cache_ratio, layers=layers, warmup=1, rank=rank,
-                                   world=world, device=dev, policy=a.policy, topology=a.topology)
+                                   world=world, device=dev, policy=a.policy, topology=a.topology,
+                                   checkpoint=a.checkpoint or None)
         rt.close()
     name = 'Qwen3-30B-A3B' if a.full_model == 'qwen3' else 'DeepSeek-V2-Lite'
     return {'metric': f'decode tokens/s, full {name} (box, max over ranks)', 'impl': a.impl,
             'value': m['decode_tokens_per_s'], 'unit': 'tokens/s', 'n_gpus': world, 'steps': a.new_tokens,
             'warmup': 1, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
-            'data': 'synthetic: random-init weights, seeded uniform token ids',
+            'data': (f'checkpoint {a.checkpoint}, seeded uniform token ids' if a.checkpoint else
+                     'synthetic: random-init weights, seeded uniform token ids'),
             'config': {'workload': f'config {"3/4" if a.full_model == "qwen3" else "2"}: full {name}',
                        'batch_per_gpu': a.batch, 'prompt_len': a.prompt_len, 'new_tokens': a.new_tokens,
                        'cache_ratio': a.cache_ratio, 'layers': layers or cfg['num_hidden_layers'],

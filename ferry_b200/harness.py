@@ -15,12 +15,15 @@ Metrics (run_cell.py:150-154 semantics, CUDA events per rank, max over
 ranks): TTFT = prefill + first token; TPOT = mean time per later token;
 decode tokens/s = R * B * (new_tokens - 1) / (max_r last_r - max_r first_r).
 """
+import json
+import re
 import time
+from pathlib import Path
 
 import torch
 import torch.distributed as dist
 
-from .model import pack_expert, spec_from_config
+from .model import pack_expert, read_spec, spec_from_config
 
 
 def hf_config(cfg_dict, **overrides):
@@ -34,6 +37,17 @@ def hf_config(cfg_dict, **overrides):
 
 def _rope_modules(model):
     return [(name, mod) for name, mod in model.named_modules() if hasattr(mod, 'inv_freq')]
+
+
+def _fresh_rope(model, device):
+    """Rotary buffers computed on `device` (a model built on the meta device
+    never computed them)."""
+    for _, mod in _rope_modules(model):
+        fresh = type(mod)(mod.config, device=device)
+        for b in ('inv_freq', 'original_inv_freq'):
+            if hasattr(fresh, b):
+                setattr(mod, b, getattr(fresh, b))
+        mod.attention_scaling = fresh.attention_scaling
 
 
 def build_model(cfg_dict, device, seed=0, keep_experts=False, **overrides):
@@ -56,22 +70,107 @@ def build_model(cfg_dict, device, seed=0, keep_experts=False, **overrides):
                 p.fill_(1.0)
             else:
                 p.normal_(0.0, 0.02, generator=gen)
-        for name, mod in _rope_modules(model):  # buffers were never computed on the meta device
-            fresh = type(mod)(mod.config, device=device)
-            for b in ('inv_freq', 'original_inv_freq'):
-                if hasattr(fresh, b):
-                    setattr(mod, b, getattr(fresh, b))
-            mod.attention_scaling = fresh.attention_scaling
+        _fresh_rope(model, device)
     model.eval()
     return model, spec
 
 
+# Routed-expert tensors of a checkpoint: one 2-D weight per expert and
+# projection (the Hugging Face layout), or transformers 5's fused 3-D
+# parameters of a layer's experts.
+_EXPERT_2D = re.compile(r'model\.layers\.(\d+)\.mlp\.experts\.(\d+)\.(gate_proj|up_proj|down_proj)\.weight')
+_EXPERT_3D = re.compile(r'model\.layers\.(\d+)\.mlp\.experts\.(gate_up_proj|down_proj)')
+
+
+def load_checkpoint(model_path, device='cuda'):
+    """(model, spec, pool) from a local checkpoint directory (config.json and
+    model.safetensors, or shards listed by model.safetensors.index.json): the
+    reference's load (ferry/model.py:73-122).  Dense weights (attention,
+    norms, routers, shared experts, embeddings) land on `device` in bf16; the
+    routed experts go straight from the files into one host pool
+    [layers * experts, 3 * H * I] bf16 in the row layout [gate | up | down]
+    (pinned when CUDA is present), never into the model.  Raises ValueError
+    if an expert projection or a dense parameter is missing, or a tensor has
+    the wrong size."""
+    from safetensors import safe_open
+    from transformers import AutoConfig, AutoModelForCausalLM, GenerationConfig
+    path = Path(model_path)
+    spec = read_spec(path)
+    cfg = AutoConfig.from_pretrained(path, local_files_only=True)
+    with torch.device('meta'):
+        model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16)
+    for idx in spec.moe_layers:
+        model.model.layers[idx].mlp.experts = None  # routed experts live in the pool
+    index = path / 'model.safetensors.index.json'
+    if index.exists():
+        weight_map = json.loads(index.read_text())['weight_map']
+    else:
+        with safe_open(str(path / 'model.safetensors'), framework='pt') as f:
+            weight_map = {name: 'model.safetensors' for name in f.keys()}
+    layer_of = {idx: i for i, idx in enumerate(spec.moe_layers)}
+    E, H, I = spec.experts, spec.hidden, spec.intermediate
+    hi = H * I
+    part_at = {'gate_proj': 0, 'up_proj': hi, 'down_proj': 2 * hi}
+    pool = torch.empty((spec.layers * E, spec.expert_elements), dtype=torch.bfloat16,
+                       pin_memory=torch.cuda.is_available())
+    have = torch.zeros((spec.layers * E, 3), dtype=torch.bool)
+    dense = {}
+
+    def put(layer_idx, e, part, w):
+        if layer_idx not in layer_of or not 0 <= e < E:
+            raise ValueError(f'routed expert {e} of layer {layer_idx} is not in the model')
+        if w.numel() != hi:
+            raise ValueError(f'layer {layer_idx} expert {e} {part}: {w.numel()} elements, want {hi}')
+        key = layer_of[layer_idx] * E + e
+        pool[key, part_at[part]:part_at[part] + hi].copy_(w.reshape(-1))
+        have[key, ('gate_proj', 'up_proj', 'down_proj').index(part)] = True
+
+    for shard in sorted(set(weight_map.values())):
+        with safe_open(str(path / shard), framework='pt', device='cpu') as f:
+            for name in sorted(n for n, s in weight_map.items() if s == shard):
+                m2, m3 = _EXPERT_2D.fullmatch(name), _EXPERT_3D.fullmatch(name)
+                if m2:
+                    put(int(m2[1]), int(m2[2]), m2[3], f.get_tensor(name))
+                elif m3:
+                    w = f.get_tensor(name)  # gate_up [E, 2I, H] or down [E, H, I]
+                    for e in range(w.shape[0]):
+                        if m3[2] == 'gate_up_proj':
+                            put(int(m3[1]), e, 'gate_proj', w[e, :I])
+                            put(int(m3[1]), e, 'up_proj', w[e, I:])
+                        else:
+                            put(int(m3[1]), e, 'down_proj', w[e])
+                else:
+                    dense[name] = f.get_tensor(name).to(torch.bfloat16)
+    if not bool(have.all()):
+        key = int((~have.all(dim=1)).nonzero()[0])
+        raise ValueError(f'routed-expert weights are incomplete (first missing: MoE layer '
+                         f'{key // E}, expert {key % E})')
+    result = model.load_state_dict(dense, strict=False, assign=True)
+    model.tie_weights()
+    missing = [n for n, p in model.named_parameters() if p.is_meta]
+    if missing:
+        raise ValueError(f'{len(missing)} dense parameters are missing, e.g. {missing[0]}')
+    if result.unexpected_keys:
+        raise ValueError(f'unexpected tensors in the checkpoint, e.g. {result.unexpected_keys[0]}')
+    with torch.no_grad():
+        _fresh_rope(model, device)  # the only buffers a checkpoint does not carry
+    left = [n for n, b in model.named_buffers() if b.is_meta]
+    if left:
+        raise ValueError(f'buffer {left[0]} has no value')
+    model.to(device)
+    if (path / 'generation_config.json').exists():
+        model.generation_config = GenerationConfig.from_pretrained(path, local_files_only=True)
+    model.eval()
+    return model, spec, pool
+
+
 def expert_pool_from_model(model, spec):
-    """The routed experts of a keep_experts model as a pinned pool [L*E, 3HI]
-    in the row layout [gate | up | down] (ferry/model.py:86-105)."""
+    """The routed experts of a keep_experts model as a host pool [L*E, 3HI]
+    (pinned when CUDA is present) in the row layout [gate | up | down]
+    (ferry/model.py:86-105)."""
     I = spec.intermediate
     pool = torch.empty((spec.layers * spec.experts, spec.expert_elements), dtype=torch.bfloat16,
-                       pin_memory=True)
+                       pin_memory=torch.cuda.is_available())
     for layer, idx in enumerate(spec.moe_layers):
         ex = model.model.layers[idx].mlp.experts
         for e in range(spec.experts):
@@ -90,8 +189,10 @@ def shared_expert_rows(model, spec):
     return rows if any(r is not None for r in rows) else None
 
 
-def install_hooks(model, spec, runtime):
-    """Route every MoE block through runtime.forward (router in kernel 1)."""
+def install_hooks(model, spec, runtime, history_window=None):
+    """Route every MoE block through runtime.forward (router in kernel 1).
+    history_window is accepted for the reference's signature
+    (ferry/model.py:125); the runtime keeps its own window."""
     for layer, idx in enumerate(spec.moe_layers):
         mlp = model.model.layers[idx].mlp
         gate = mlp.gate.weight
@@ -139,20 +240,27 @@ def decode_metrics(times_ms, batch, world):
 
 
 def run(cfg_dict, *, batch, prompt_len, new_tokens, cache_ratio=0.3, seed=0, layers=None, warmup=1,
-        rank=0, world=1, device=None, timing=False, policy='ferry', topology=None):
+        rank=0, world=1, device=None, timing=False, policy='ferry', topology=None, checkpoint=None):
     """Build, hook and run one generation (after `warmup` untimed ones).
     topology: None/'uniform', 'auto' (profile the ranks' host links now) or a
-    topology JSON path (ferry_b200.build_quota_lut.topology_for_run)."""
+    topology JSON path (ferry_b200.build_quota_lut.topology_for_run).
+    checkpoint: a local checkpoint directory (load_checkpoint) whose weights
+    and config replace the random model of cfg_dict; each rank then holds its
+    own pinned pool, as the reference's does."""
     from .build_quota_lut import topology_for_run
     from .runtime import OffloadRuntime
     from .workload import SyntheticMoE
     device = device or torch.device('cuda', torch.cuda.current_device())
-    overrides = {'num_hidden_layers': layers} if layers else {}
-    model, spec = build_model(cfg_dict, device, seed, **overrides)
-    wl = SyntheticMoE(spec, seed=seed + 1, device=device, shared=world > 1)
+    if checkpoint is not None:
+        model, spec, pool = load_checkpoint(checkpoint, device)
+        cfg_dict = dict(model.config.to_dict(), model_type=spec.model_type)
+    else:
+        overrides = {'num_hidden_layers': layers} if layers else {}
+        model, spec = build_model(cfg_dict, device, seed, **overrides)
+        pool = SyntheticMoE(spec, seed=seed + 1, device=device, shared=world > 1).pool
     caps = spec.cache_slots(cache_ratio, world)
-    topo, topo_note = topology_for_run(topology, spec, rank, world, pool_row=wl.pool[0], device=device)
-    rt = OffloadRuntime(spec, wl.pool, caps, policy, topo,
+    topo, topo_note = topology_for_run(topology, spec, rank, world, pool_row=pool[0], device=device)
+    rt = OffloadRuntime(spec, pool, caps, policy, topo,
                         norm_topk_prob=bool(cfg_dict.get('norm_topk_prob', True)),
                         routed_scaling_factor=float(cfg_dict.get('routed_scaling_factor', 1.0)),
                         shared_experts=shared_expert_rows(model, spec), timing=timing)

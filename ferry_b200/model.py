@@ -49,7 +49,8 @@ def spec_from_config(c):
         step = c.get('decoder_sparse_step', 1)
         dense = set(c.get('mlp_only_layers') or [])
         layers = tuple(i for i in range(n) if i not in dense and (i + 1) % step == 0)
-        experts = c['num_experts']
+        # transformers 5 writes the expert count as num_local_experts
+        experts = c['num_experts'] if 'num_experts' in c else c['num_local_experts']
     elif kind == 'deepseek_v2':
         first = c['first_k_dense_replace']
         freq = c.get('moe_layer_freq', 1)

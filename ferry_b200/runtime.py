@@ -28,6 +28,15 @@ from .policy import Controller
 from .symm import SymmetricBuffer
 
 
+def expert_ops():
+    """The expert-op module that ferry/runtime.py:26-31 compiles and returns:
+    here ferry_b200.expert_ops (execute_experts, pack_dispatch,
+    unpack_dispatch, reduce_partials, scatter_returned, H2DEngine), whose
+    kernels are in libferryb.so."""
+    from . import expert_ops as ops
+    return ops
+
+
 def _rank_world(group=None):
     if dist.is_available() and dist.is_initialized():
         return dist.get_rank(group), dist.get_world_size(group)
