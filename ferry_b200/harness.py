@@ -251,13 +251,15 @@ def run(cfg_dict, *, batch, prompt_len, new_tokens, cache_ratio=0.3, seed=0, lay
     from .runtime import OffloadRuntime
     from .workload import SyntheticMoE
     device = device or torch.device('cuda', torch.cuda.current_device())
+    wl = None  # owns a shared pool's mapping: kept alive while the runtime runs
     if checkpoint is not None:
         model, spec, pool = load_checkpoint(checkpoint, device)
         cfg_dict = dict(model.config.to_dict(), model_type=spec.model_type)
     else:
         overrides = {'num_hidden_layers': layers} if layers else {}
         model, spec = build_model(cfg_dict, device, seed, **overrides)
-        pool = SyntheticMoE(spec, seed=seed + 1, device=device, shared=world > 1).pool
+        wl = SyntheticMoE(spec, seed=seed + 1, device=device, shared=world > 1)
+        pool = wl.pool
     caps = spec.cache_slots(cache_ratio, world)
     topo, topo_note = topology_for_run(topology, spec, rank, world, pool_row=pool[0], device=device)
     rt = OffloadRuntime(spec, pool, caps, policy, topo,
@@ -280,4 +282,5 @@ def run(cfg_dict, *, batch, prompt_len, new_tokens, cache_ratio=0.3, seed=0, lay
     m = decode_metrics(times, batch, world)
     m.update(fetches_per_rank=rt.fetches_per_rank.tolist(),
              decode_fetches_per_rank=rt.decode_fetches_per_rank.tolist(), wall_s=wall, topology=topo_note)
+    rt.pool_owner = wl  # the pool stays mapped as long as the runtime exists
     return model, rt, tokens, m
